@@ -1,0 +1,141 @@
+/*
+ * specq.h -- C ABI of the B200 (sm_100a) verification-shape kernels.
+ *
+ * Drop-in boundary for the three kernels of Vaibhav1067/specdec-quant-triton:
+ *   specq_w8a8            replaces kernels.py:71-86   (w8a8_matmul   -> _w8a8_kernel,  kernels.py:27-55)
+ *   specq_w4a16           replaces kernels.py:150-166 (w4a16_matmul  -> _w4a16_kernel, kernels.py:95-135)
+ *   specq_paged_attention replaces kernels.py:239-262 (paged_attention -> _paged_attn_kernel, kernels.py:179-236)
+ *   specq_kernel_info     replaces the compiled-kernel handle the wrappers return
+ *                         (`ck.n_regs`, `ck.n_spills`, `ck.metadata.shared`, read by regs.py:29-32)
+ *
+ * Conventions
+ *   - Plain pointers to device memory, sizes and strides in ELEMENTS of the pointed-to type.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Every call is asynchronous,
+ *     does no host synchronisation and no device allocation, so it may be captured in a CUDA
+ *     graph.
+ *   - `plan` (optional, device int32): when non-NULL the active extent is read on the device
+ *     (GEMMs: plan[0] = M; attention: plan[0] = n_seqs, plan[1] = q_len), CTAs outside it exit
+ *     early and outputs outside it are never written.  The grid is sized by the maximum
+ *     extent passed on the host (`grid_m_max`, `B`, `ql_max`).
+ *   - Return value: SPECQ_OK or an error code; specq_last_error() gives the message
+ *     (thread-local).  Invalid arguments are rejected on the host; nothing traps on the device.
+ *   - Device-side conditions (a bounded wait that ran out, a plan value that had to be
+ *     clamped) are recorded in a per-device status word read by specq_get_status().
+ */
+#ifndef SPECQ_H_
+#define SPECQ_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- return codes ---------------------------------------------------------------------- */
+#define SPECQ_OK 0
+#define SPECQ_ERR_INVALID_ARG 1  /* shape, stride, dtype or alignment the kernel cannot take   */
+#define SPECQ_ERR_UNSUPPORTED 2  /* valid for the reference, not (yet) for this build          */
+#define SPECQ_ERR_CUDA 3         /* a CUDA runtime / driver call failed                        */
+#define SPECQ_ERR_NO_DEVICE 4    /* no sm_100 device is current                                */
+
+/* ---- device status word bits (specq_get_status) ---------------------------------------- */
+#define SPECQ_STATUS_TIMEOUT_PIPELINE 0x01 /* a producer/consumer mbarrier wait ran out            */
+#define SPECQ_STATUS_TIMEOUT_MMA 0x02      /* waiting for tensor-core completion ran out           */
+#define SPECQ_STATUS_TIMEOUT_TEST 0x04     /* specq_selftest_wait_timeout's deliberate wait         */
+#define SPECQ_STATUS_PLAN_CLAMPED 0x100    /* a plan value was outside [0, max] and was clamped     */
+
+/* ---- dtypes for scale tensors ----------------------------------------------------------- */
+#define SPECQ_DTYPE_F16 0
+#define SPECQ_DTYPE_F32 1
+
+/*
+ * W8A8 GEMM.  out[m, n] = fp16( (fp32(sum_k a[m,k] * w[n,k]) * sa[m]) * sw[n] )
+ *   a   int8  [M, K]  row stride lda     (per-token quantised activations)
+ *   w   int8  [N, K]  row stride ldw     (per-channel quantised weights, "NT" layout)
+ *   sa  fp32  [M]     sw fp32 [N]
+ *   out fp16  [M, N]  strides (ldo, ldo_n)
+ *   M   rows of a/sa/out the kernel may touch (the grid extent: grid_m_max in plan mode)
+ * Reference: kernels.py:71-86 (wrapper), kernels.py:27-55 (kernel).
+ */
+int specq_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int64_t ldw, const float* sw,
+               void* out, int64_t ldo, int64_t ldo_n, const int32_t* plan, int M, int N, int K, void* stream);
+
+/*
+ * Same GEMM, but writes the raw INT32 accumulator acc[m, n] = sum_k a[m,k] * w[n,k] to
+ * `acc` (row stride ldacc) instead of the scaled fp16 output.  Used to check the tensor-core
+ * accumulator bit for bit against an exact integer reference (the `acc` of kernels.py:44-50).
+ */
+int specq_w8a8_acc(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw, int32_t* acc, int64_t ldacc,
+                   const int32_t* plan, int M, int N, int K, void* stream);
+
+/*
+ * W4A16 GEMM.  out[m, n] = fp16( sum_k a[m,k] * fp16(q[n,k] * sc[n, k / group]) )
+ *   a   fp16  [M, K]        row stride lda
+ *   wp  uint8 [N, K/2]      row stride ldwp; byte j holds q[n,j]+8 (low nibble) and
+ *                           q[n,j+K/2]+8 (high nibble)  (kernels.py:90-92, 143-145)
+ *   sc  fp16  [N, K/group]  row stride ldsc
+ *   out fp16  [M, N]        strides (ldo, ldo_n)
+ * Reference: kernels.py:150-166 (wrapper), kernels.py:95-135 (kernel).
+ */
+int specq_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const void* sc, int64_t ldsc,
+                int group, void* out, int64_t ldo, int64_t ldo_n, const int32_t* plan, int M, int N, int K,
+                void* stream);
+
+/*
+ * INT8 paged verification attention (kernels.py:239-262 wrapper, kernels.py:179-236 kernel).
+ *   q        fp16 [B, QL_MAX, H, D]         strides (q_sb, q_st, q_sh), unit stride along D
+ *   kc, vc   int8 [P, PAGE, H_KV, D]        strides (kv_sp, kv_so, kv_sh), unit stride along D;
+ *                                           n_pages = P
+ *   ks, vs   fp16 or fp32 [P, PAGE, H_KV]   strides (s_sp, s_so, s_sh); scale_dtype SPECQ_DTYPE_*
+ *   block_tbl int32 [B, max_pages]          row stride bt_sb, bt_cols = max_pages
+ *   ctx_len  int32 [B]                      context length including the q_len query tokens
+ *   out      fp16 like q                    strides (o_sb, o_st, o_sh)
+ * Rows (b, qi, head) with b < n_seqs and qi < q_len are written; nothing else is touched.
+ * Row qi attends to tokens t <= ctx_len[b] - q_len + qi (causal verification window).
+ * `qpp` (queries per program) only changes the schedule: 1 = one query token per CTA,
+ * q_len = all k+1 tokens of a GQA group in one CTA (the fused verification kernel).
+ * In plan mode, plan[0] = n_seqs and plan[1] = q_len; the grid is (B, ..., ceil(ql_max/qpp)).
+ */
+int specq_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, const int8_t* kc,
+                          const int8_t* vc, int64_t kv_sp, int64_t kv_so, int64_t kv_sh, int n_pages,
+                          const void* ks, const void* vs, int64_t s_sp, int64_t s_so, int64_t s_sh,
+                          int scale_dtype, const int32_t* block_tbl, int64_t bt_sb, int bt_cols,
+                          const int32_t* ctx_len, void* out, int64_t o_sb, int64_t o_st, int64_t o_sh,
+                          const int32_t* plan, int B, int n_seqs, int q_len, int ql_max, int H, int H_KV,
+                          int D, int page, int qpp, void* stream);
+
+/*
+ * Compiled-kernel metadata for the kernel variant a call with these arguments would launch
+ * (the reference returns Triton's compiled kernel `ck`; regs.py:29-32 reads n_regs,
+ * n_spills and metadata.shared from it).
+ *   which: 0 = W8A8, 1 = W4A16, 2 = paged attention;  variant: as reported by the launch.
+ */
+int specq_kernel_info(int which, int variant, int* num_regs, int* local_bytes, int* static_smem,
+                      int* dynamic_smem, int* max_threads);
+
+/* Variant id and launch geometry of the most recent successful launch on this host thread:
+ * kernel variant, grid (x, y, z), cluster size along x, threads per CTA, dynamic smem. */
+int specq_last_launch(int* variant, int* grid_x, int* grid_y, int* grid_z, int* cluster_x, int* threads,
+                      int* dynamic_smem);
+
+/* Read (and with clear != 0, reset) the status word of the current device. Synchronous. */
+int specq_get_status(int* status, int clear);
+
+/*
+ * Failure-detection self test: launches one CTA that waits on an mbarrier nothing will ever
+ * complete, with a wait limit of `limit_ns` nanoseconds; the wait gives up, records
+ * SPECQ_STATUS_TIMEOUT_TEST in the status word and the kernel returns normally.
+ */
+int specq_selftest_wait_timeout(uint64_t limit_ns, void* stream);
+
+/* Message of the last error on this host thread ("" if none). */
+const char* specq_last_error(void);
+
+/* ABI version (major * 100 + minor). */
+int specq_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPECQ_H_ */

@@ -1,0 +1,386 @@
+// specq_api.cu -- the extern "C" entry points of libspecq.so (declared in include/specq.h).
+//
+// Each entry point validates its arguments on the host, chooses the kernel variant and launch
+// geometry (split-K, token chunks, pipeline depth), encodes the TMA tensor maps and launches
+// on the caller's stream.  No allocation, no synchronisation: calls are graph-capturable.
+#include <algorithm>
+
+#include "specq_host.cuh"
+#include "w8a8.cuh"
+#include "w4a16.cuh"
+#include "paged_attn.cuh"
+
+namespace specq {
+
+// Per-device status word: kernels record timeouts and clamped plan values here.
+__device__ int g_specq_status = 0;
+
+int* device_status_symbol_address() {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_specq_status) != cudaSuccess) return nullptr;
+  return static_cast<int*>(p);
+}
+
+// ---------------------------------------------------------------------------------------------
+// W8A8
+// ---------------------------------------------------------------------------------------------
+namespace {
+
+constexpr int kSmemLimit = 232448;  // 227 KB opt-in per block on sm_100
+
+template <int VEC>
+int launch_w8a8_variant(const W8A8Params& p, const CUtensorMap& tw, const CUtensorMap& ta, dim3 grid, int smem,
+                        cudaStream_t stream) {
+  auto kern = w8a8_kernel<VEC>;
+  SPECQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kW8A8Threads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(p.splits);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = p.splits > 1 ? 1 : 0;
+  SPECQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p, tw, ta));
+  return SPECQ_OK;
+}
+
+int w8a8_variant_id(int vec) {
+  switch (vec) {
+    case 0: return 0;
+    case 16: return 1;
+    case 8: return 2;
+    case 4: return 3;
+    case 2: return 4;
+    default: return 5;
+  }
+}
+
+int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int64_t ldw, const float* sw,
+             void* out, int64_t ldo, int64_t ldo_n, int32_t* acc, int64_t ldacc, const int32_t* plan, int M, int N,
+             int K, void* stream) {
+  if (M < 0 || N <= 0 || K <= 0) return fail(SPECQ_ERR_INVALID_ARG, "w8a8: bad shape M=%d N=%d K=%d", M, N, K);
+  if (M == 0) return SPECQ_OK;   // nothing to compute (empty tensors may carry null pointers)
+  if (a == nullptr || w == nullptr) return fail(SPECQ_ERR_INVALID_ARG, "w8a8: null input pointer");
+  if (acc == nullptr && (out == nullptr || sa == nullptr || sw == nullptr))
+    return fail(SPECQ_ERR_INVALID_ARG, "w8a8: null output or scale pointer");
+  if (lda < K || ldw < K) return fail(SPECQ_ERR_INVALID_ARG, "w8a8: row strides (%lld, %lld) < K=%d",
+                                      (long long)lda, (long long)ldw, K);
+  if (K > (1 << 30) / 127) return fail(SPECQ_ERR_UNSUPPORTED, "w8a8: K=%d could overflow the INT32 accumulator", K);
+  if (M == 0) return SPECQ_OK;
+  DeviceState* dev = nullptr;
+  if (int rc = get_device_state(&dev)) return rc;
+
+  W8A8Params p = {};
+  p.a = a; p.w = w; p.sa = sa; p.sw = sw;
+  p.out = static_cast<__half*>(out);
+  p.acc_out = acc;
+  p.plan = plan;
+  p.status = dev->status;
+  p.lda = lda; p.ldw = ldw; p.ldo = ldo; p.ldo_n = ldo_n; p.ldacc = ldacc;
+  p.m_rows = M; p.N = N; p.K = K;
+
+  const int n_chunks = ceil_div(M, 256);
+  p.chunk = round_up(ceil_div(M, n_chunks), 16);
+  p.kb_total = ceil_div(K, 128);
+  const int n_tiles = ceil_div(N, 128);
+  const int base = n_tiles * n_chunks;
+  int S = 1;
+  for (int cand : {8, 4, 2}) {
+    const int kbps = ceil_div(p.kb_total, cand);
+    if ((cand - 1) * kbps < p.kb_total && base * cand <= dev->sm_count) { S = cand; break; }
+  }
+  p.splits = S;
+  p.kb_per_split = ceil_div(p.kb_total, S);
+
+  p.stage_bytes = kW8A8WTile + static_cast<uint32_t>(round_up(p.chunk, 32)) * 128u;
+  const uint32_t red_bytes = (S > 1) ? 128u * (static_cast<uint32_t>(p.chunk) * 4u + 16u) : 0u;
+  const int overhead = 1024 + 256;
+  int stages = std::min(8, (kSmemLimit - overhead) / static_cast<int>(p.stage_bytes));
+  if (stages < 2) return fail(SPECQ_ERR_UNSUPPORTED, "w8a8: token chunk %d does not fit shared memory", p.chunk);
+  while (static_cast<uint32_t>(stages) * p.stage_bytes < red_bytes && stages < 8) ++stages;
+  p.stages = stages;
+  const int smem = overhead + stages * static_cast<int>(p.stage_bytes);
+  if (smem > kSmemLimit) return fail(SPECQ_ERR_UNSUPPORTED, "w8a8: shared memory %d > limit", smem);
+  p.tmem_cols = static_cast<uint32_t>(std::max(32, next_pow2(p.chunk)));
+
+  // TMA needs 16-byte aligned bases and row strides; otherwise use the register-staged loader.
+  const bool tma_ok = aligned(a, 16) && aligned(w, 16) && (lda % 16 == 0) && (ldw % 16 == 0);
+  CUtensorMap tw, ta;
+  memset(&tw, 0, sizeof(tw));
+  memset(&ta, 0, sizeof(ta));
+  int vec = 0;
+  if (tma_ok) {
+    const uint64_t dw[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
+    const uint64_t sw_[1] = {static_cast<uint64_t>(ldw)};
+    const uint32_t bw[2] = {128, 128};
+    if (int rc = encode_tiled(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, dw, sw_, bw, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+    const uint64_t da[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+    const uint64_t sa_[1] = {static_cast<uint64_t>(lda)};
+    const uint32_t ba[2] = {128, 32};
+    if (int rc = encode_tiled(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a, da, sa_, ba, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+  } else {
+    vec = common_vec_width({reinterpret_cast<uintptr_t>(a), reinterpret_cast<uintptr_t>(w),
+                            static_cast<uint64_t>(lda), static_cast<uint64_t>(ldw), static_cast<uint64_t>(K)});
+  }
+
+  const dim3 grid(static_cast<unsigned>(S), static_cast<unsigned>(n_tiles), static_cast<unsigned>(n_chunks));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc;
+  switch (vec) {
+    case 0: rc = launch_w8a8_variant<0>(p, tw, ta, grid, smem, st); break;
+    case 16: rc = launch_w8a8_variant<16>(p, tw, ta, grid, smem, st); break;
+    case 8: rc = launch_w8a8_variant<8>(p, tw, ta, grid, smem, st); break;
+    case 4: rc = launch_w8a8_variant<4>(p, tw, ta, grid, smem, st); break;
+    case 2: rc = launch_w8a8_variant<2>(p, tw, ta, grid, smem, st); break;
+    default: rc = launch_w8a8_variant<1>(p, tw, ta, grid, smem, st); break;
+  }
+  if (rc == SPECQ_OK) {
+    LaunchRecord& r = last_launch_ref();
+    r.variant = w8a8_variant_id(vec);
+    r.grid[0] = static_cast<int>(grid.x); r.grid[1] = static_cast<int>(grid.y); r.grid[2] = static_cast<int>(grid.z);
+    r.cluster_x = S;
+    r.threads = kW8A8Threads;
+    r.dyn_smem = smem;
+  }
+  return rc;
+}
+
+const void* w8a8_kernel_by_variant(int variant) {
+  switch (variant) {
+    case 0: return reinterpret_cast<const void*>(w8a8_kernel<0>);
+    case 1: return reinterpret_cast<const void*>(w8a8_kernel<16>);
+    case 2: return reinterpret_cast<const void*>(w8a8_kernel<8>);
+    case 3: return reinterpret_cast<const void*>(w8a8_kernel<4>);
+    case 4: return reinterpret_cast<const void*>(w8a8_kernel<2>);
+    case 5: return reinterpret_cast<const void*>(w8a8_kernel<1>);
+    default: return nullptr;
+  }
+}
+
+
+// ---------------------------------------------------------------------------------------------
+// W4A16
+// ---------------------------------------------------------------------------------------------
+int run_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const void* sc, int64_t ldsc, int group,
+              void* out, int64_t ldo, int64_t ldo_n, const int32_t* plan, int M, int N, int K, void* stream) {
+  if (M < 0 || N <= 0 || K <= 0) return fail(SPECQ_ERR_INVALID_ARG, "w4a16: bad shape M=%d N=%d K=%d", M, N, K);
+  if (M == 0) return SPECQ_OK;   // nothing to compute (empty tensors may carry null pointers)
+  if (a == nullptr || wp == nullptr || sc == nullptr || out == nullptr)
+    return fail(SPECQ_ERR_INVALID_ARG, "w4a16: null pointer");
+  if (group <= 0) return fail(SPECQ_ERR_INVALID_ARG, "w4a16: group=%d", group);
+  if (K % 2 != 0) return fail(SPECQ_ERR_INVALID_ARG, "w4a16: K=%d must be even (split-half packing)", K);
+  if ((K / 2) % 64 != 0 || group % 64 != 0)
+    return fail(SPECQ_ERR_UNSUPPORTED, "w4a16: needs (K/2) %% 64 == 0 and group %% 64 == 0 (K=%d, group=%d)", K, group);
+  if (lda < K || ldwp < K / 2 || ldsc < (K + group - 1) / group)
+    return fail(SPECQ_ERR_INVALID_ARG, "w4a16: row strides too small");
+  if (!aligned(a, 16) || (lda * 2) % 16 != 0 || !aligned(wp, 16) || ldwp % 16 != 0)
+    return fail(SPECQ_ERR_UNSUPPORTED, "w4a16: activations/packed weights need 16-byte aligned rows");
+  if (M == 0) return SPECQ_OK;
+  DeviceState* dev = nullptr;
+  if (int rc = get_device_state(&dev)) return rc;
+
+  W4A16Params p = {};
+  p.a = static_cast<const __half*>(a);
+  p.wp = wp;
+  p.sc = static_cast<const __half*>(sc);
+  p.out = static_cast<__half*>(out);
+  p.plan = plan;
+  p.status = dev->status;
+  p.lda = lda; p.ldwp = ldwp; p.ldsc = ldsc; p.ldo = ldo; p.ldo_n = ldo_n;
+  p.m_rows = M; p.N = N; p.K = K; p.group = group;
+  p.kb_total = K / 128;
+  const int n_tiles = ceil_div(N, 128);
+  // The split depends on (N, K) only, never on M: plan and non-plan calls reduce the same
+  // partial sums in the same order.
+  int S = 1;
+  for (int cand : {8, 4, 2}) {
+    const int kbps = ceil_div(p.kb_total, cand);
+    if ((cand - 1) * kbps < p.kb_total && n_tiles * cand <= dev->sm_count) { S = cand; break; }
+  }
+  p.splits = S;
+  p.kb_per_split = ceil_div(p.kb_total, S);
+  p.dstages = 2;
+  const int cols_lo = (64 * p.kb_per_split + group - 1) / group + 1;
+  p.sc_cache_cols = static_cast<uint32_t>(2 * cols_lo);
+  const int sc_bytes = round_up(128 * static_cast<int>(p.sc_cache_cols) * 2, 16);
+
+  int n_chunks = ceil_div(M, 256);
+  int smem = 0;
+  while (true) {
+    p.chunk = round_up(ceil_div(M, n_chunks), 16);
+    p.stage_bytes = kW4A16PackTile + 2u * static_cast<uint32_t>(round_up(p.chunk, 32)) * 128u;
+    const int fixed = 1024 + p.dstages * static_cast<int>(kW4A16DSlot) + sc_bytes + 512;
+    const uint32_t red_bytes = (S > 1) ? 128u * (static_cast<uint32_t>(p.chunk) * 4u + 16u) : 0u;
+    int stages = std::min(6, (kSmemLimit - fixed) / static_cast<int>(p.stage_bytes));
+    while (stages >= 2 && static_cast<uint32_t>(stages) * p.stage_bytes < red_bytes && stages < 6) ++stages;
+    if (stages >= 2 && static_cast<uint32_t>(stages) * p.stage_bytes >= red_bytes &&
+        fixed + stages * static_cast<int>(p.stage_bytes) <= kSmemLimit) {
+      p.stages = stages;
+      smem = fixed + stages * static_cast<int>(p.stage_bytes);
+      break;
+    }
+    if (p.chunk <= 16) return fail(SPECQ_ERR_UNSUPPORTED, "w4a16: shapes do not fit shared memory");
+    ++n_chunks;
+  }
+  p.tmem_cols = static_cast<uint32_t>(std::max(32, next_pow2(p.chunk)));
+
+  CUtensorMap tw, ta;
+  memset(&tw, 0, sizeof(tw));
+  memset(&ta, 0, sizeof(ta));
+  {
+    const uint64_t d[2] = {static_cast<uint64_t>(K / 2), static_cast<uint64_t>(N)};
+    const uint64_t s_[1] = {static_cast<uint64_t>(ldwp)};
+    const uint32_t b[2] = {64, 128};
+    if (int rc = encode_tiled(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, wp, d, s_, b, CU_TENSOR_MAP_SWIZZLE_NONE)) return rc;
+  }
+  {
+    const uint64_t d[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+    const uint64_t s_[1] = {static_cast<uint64_t>(lda) * 2u};
+    const uint32_t b[2] = {64, 32};
+    if (int rc = encode_tiled(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, d, s_, b, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+  }
+  const dim3 grid(static_cast<unsigned>(S), static_cast<unsigned>(n_tiles), static_cast<unsigned>(n_chunks));
+  SPECQ_CUDA_TRY(cudaFuncSetAttribute(w4a16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kW4A16Threads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(S);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = S > 1 ? 1 : 0;
+  SPECQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, w4a16_kernel, p, tw, ta));
+  LaunchRecord& r = last_launch_ref();
+  r.variant = 0;
+  r.grid[0] = static_cast<int>(grid.x); r.grid[1] = static_cast<int>(grid.y); r.grid[2] = static_cast<int>(grid.z);
+  r.cluster_x = S;
+  r.threads = kW4A16Threads;
+  r.dyn_smem = smem;
+  return SPECQ_OK;
+}
+
+const void* w4a16_kernel_by_variant(int variant) {
+  return variant == 0 ? reinterpret_cast<const void*>(w4a16_kernel) : nullptr;
+}
+
+// ---------------------------------------------------------------------------------------------
+// failure-detection self test: a wait that nothing completes
+// ---------------------------------------------------------------------------------------------
+__global__ void selftest_wait_kernel(int* status, uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1u);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(&bar, 0u)) {
+      if (globaltimer_ns() - t0 > limit_ns) {
+        report_status(status, SPECQ_STATUS_TIMEOUT_TEST);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+}
+
+}  // namespace
+}  // namespace specq
+
+using namespace specq;
+
+extern "C" {
+
+int specq_version(void) { return 100; }
+
+const char* specq_last_error(void) { return last_error_ref().c_str(); }
+
+int specq_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int64_t ldw, const float* sw,
+               void* out, int64_t ldo, int64_t ldo_n, const int32_t* plan, int M, int N, int K, void* stream) {
+  return run_w8a8(a, lda, sa, w, ldw, sw, out, ldo, ldo_n, nullptr, 0, plan, M, N, K, stream);
+}
+
+int specq_w8a8_acc(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw, int32_t* acc, int64_t ldacc,
+                   const int32_t* plan, int M, int N, int K, void* stream) {
+  if (acc == nullptr) return fail(SPECQ_ERR_INVALID_ARG, "w8a8_acc: null accumulator pointer");
+  return run_w8a8(a, lda, nullptr, w, ldw, nullptr, nullptr, 0, 1, acc, ldacc, plan, M, N, K, stream);
+}
+
+int specq_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const void* sc, int64_t ldsc, int group,
+                void* out, int64_t ldo, int64_t ldo_n, const int32_t* plan, int M, int N, int K, void* stream) {
+  return run_w4a16(a, lda, wp, ldwp, sc, ldsc, group, out, ldo, ldo_n, plan, M, N, K, stream);
+}
+
+int specq_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, const int8_t* kc, const int8_t* vc,
+                          int64_t kv_sp, int64_t kv_so, int64_t kv_sh, int n_pages, const void* ks, const void* vs,
+                          int64_t s_sp, int64_t s_so, int64_t s_sh, int scale_dtype, const int32_t* block_tbl,
+                          int64_t bt_sb, int bt_cols, const int32_t* ctx_len, void* out, int64_t o_sb, int64_t o_st,
+                          int64_t o_sh, const int32_t* plan, int B, int n_seqs, int q_len, int ql_max, int H,
+                          int H_KV, int D, int page, int qpp, void* stream) {
+  return run_paged_attention(q, q_sb, q_st, q_sh, kc, vc, kv_sp, kv_so, kv_sh, n_pages, ks, vs, s_sp, s_so, s_sh,
+                             scale_dtype, block_tbl, bt_sb, bt_cols, ctx_len, out, o_sb, o_st, o_sh, plan, B, n_seqs,
+                             q_len, ql_max, H, H_KV, D, page, qpp, stream);
+}
+
+int specq_kernel_info(int which, int variant, int* num_regs, int* local_bytes, int* static_smem, int* dynamic_smem,
+                      int* max_threads) {
+  const void* fn = nullptr;
+  if (which == 0) fn = w8a8_kernel_by_variant(variant);
+  else if (which == 1) fn = w4a16_kernel_by_variant(variant);
+  else if (which == 2) fn = paged_attn_kernel_by_variant(variant);
+  if (fn == nullptr) return fail(SPECQ_ERR_INVALID_ARG, "kernel_info: unknown kernel %d variant %d", which, variant);
+  cudaFuncAttributes at;
+  SPECQ_CUDA_TRY(cudaFuncGetAttributes(&at, fn));
+  if (num_regs) *num_regs = at.numRegs;
+  if (local_bytes) *local_bytes = static_cast<int>(at.localSizeBytes);
+  if (static_smem) *static_smem = static_cast<int>(at.sharedSizeBytes);
+  if (dynamic_smem) *dynamic_smem = at.maxDynamicSharedSizeBytes;
+  if (max_threads) *max_threads = at.maxThreadsPerBlock;
+  return SPECQ_OK;
+}
+
+int specq_last_launch(int* variant, int* grid_x, int* grid_y, int* grid_z, int* cluster_x, int* threads,
+                      int* dynamic_smem) {
+  const LaunchRecord& r = last_launch_ref();
+  if (variant) *variant = r.variant;
+  if (grid_x) *grid_x = r.grid[0];
+  if (grid_y) *grid_y = r.grid[1];
+  if (grid_z) *grid_z = r.grid[2];
+  if (cluster_x) *cluster_x = r.cluster_x;
+  if (threads) *threads = r.threads;
+  if (dynamic_smem) *dynamic_smem = r.dyn_smem;
+  return SPECQ_OK;
+}
+
+int specq_get_status(int* status, int clear) {
+  DeviceState* dev = nullptr;
+  if (int rc = get_device_state(&dev)) return rc;
+  int v = 0;
+  SPECQ_CUDA_TRY(cudaMemcpy(&v, dev->status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (clear) {
+    const int zero = 0;
+    SPECQ_CUDA_TRY(cudaMemcpy(dev->status, &zero, sizeof(int), cudaMemcpyHostToDevice));
+  }
+  if (status) *status = v;
+  return SPECQ_OK;
+}
+
+int specq_selftest_wait_timeout(uint64_t limit_ns, void* stream) {
+  DeviceState* dev = nullptr;
+  if (int rc = get_device_state(&dev)) return rc;
+  selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(dev->status, limit_ns);
+  SPECQ_CUDA_TRY(cudaGetLastError());
+  return SPECQ_OK;
+}
+
+}  // extern "C"

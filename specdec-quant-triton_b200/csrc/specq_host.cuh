@@ -1,0 +1,154 @@
+// specq_host.cuh -- host-side plumbing shared by the C-ABI entry points: error reporting,
+// per-device state (status word, SM count, kernel attributes), tensor-map encoding through
+// the driver entry point (no link-time dependency on libcuda), launch records.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "specq.h"
+
+namespace specq {
+
+// ---- errors ---------------------------------------------------------------------------------
+inline std::string& last_error_ref() {
+  static thread_local std::string msg;
+  return msg;
+}
+
+inline int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  last_error_ref() = buf;
+  return code;
+}
+
+#define SPECQ_CUDA_TRY(expr)                                                                      \
+  do {                                                                                            \
+    cudaError_t e_ = (expr);                                                                      \
+    if (e_ != cudaSuccess) return ::specq::fail(SPECQ_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(e_)); \
+  } while (0)
+
+// ---- launch record ----------------------------------------------------------------------------
+struct LaunchRecord {
+  int variant = -1;
+  int grid[3] = {0, 0, 0};
+  int cluster_x = 0;
+  int threads = 0;
+  int dyn_smem = 0;
+};
+inline LaunchRecord& last_launch_ref() {
+  static thread_local LaunchRecord r;
+  return r;
+}
+
+// ---- per-device state ---------------------------------------------------------------------
+constexpr int kMaxDevices = 64;
+struct DeviceState {
+  bool init = false;
+  int sm_count = 0;
+  int max_smem_optin = 0;
+  int cc_major = 0, cc_minor = 0;
+  int* status = nullptr;  // device address of the status word
+};
+
+int* device_status_symbol_address();  // defined next to the __device__ status word
+
+inline int get_device_state(DeviceState** out) {
+  static std::mutex mu;
+  static DeviceState states[kMaxDevices];
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return fail(SPECQ_ERR_NO_DEVICE, "no current CUDA device");
+  std::lock_guard<std::mutex> lock(mu);
+  DeviceState& st = states[dev];
+  if (!st.init) {
+    cudaDeviceProp prop;
+    SPECQ_CUDA_TRY(cudaGetDeviceProperties(&prop, dev));
+    if (prop.major != 10)
+      return fail(SPECQ_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a only", dev,
+                  prop.major, prop.minor);
+    st.sm_count = prop.multiProcessorCount;
+    st.max_smem_optin = static_cast<int>(prop.sharedMemPerBlockOptin);
+    st.cc_major = prop.major;
+    st.cc_minor = prop.minor;
+    st.status = device_status_symbol_address();
+    if (st.status == nullptr) return fail(SPECQ_ERR_CUDA, "could not resolve the device status word");
+    st.init = true;
+  }
+  *out = &st;
+  return SPECQ_OK;
+}
+
+// ---- tensor maps ------------------------------------------------------------------------------
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline PFN_encodeTiled get_encode_tiled() {
+  static PFN_encodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(p);
+  });
+  return fn;
+}
+
+// Encode a tiled tensor map of rank 2 or 3.  dims/strides_bytes/box are innermost first;
+// strides_bytes[i] is the byte stride of dimension i+1.
+inline int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
+                        const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                        CUtensorMapSwizzle swizzle) {
+  PFN_encodeTiled enc = get_encode_tiled();
+  if (enc == nullptr) return fail(SPECQ_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t d[5];
+  cuuint64_t s[4];
+  cuuint32_t b[5];
+  cuuint32_t e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i + 1 < rank) s[i] = strides_bytes[i];
+  }
+  CUresult r = enc(map, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, s, b, e,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SPECQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+  return SPECQ_OK;
+}
+
+// ---- small integer helpers --------------------------------------------------------------------
+inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+inline int round_up(int a, int b) { return ceil_div(a, b) * b; }
+inline int next_pow2(int x) {
+  int p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+inline bool aligned(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
+
+// Widest access width (16, 8, 4, 2, 1 bytes) that every pointer and byte count in the list
+// is a multiple of.
+inline int common_vec_width(std::initializer_list<uint64_t> values) {
+  int w = 16;
+  for (uint64_t v : values) {
+    while (w > 1 && (v % static_cast<uint64_t>(w)) != 0) w >>= 1;
+  }
+  return w;
+}
+
+}  // namespace specq

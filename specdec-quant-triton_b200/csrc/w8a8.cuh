@@ -1,0 +1,291 @@
+// w8a8.cuh -- W8A8 INT8 GEMM for verification shapes on sm_100a.
+//
+// Computes out[m, n] = fp16((fp32(acc[m, n]) * sa[m]) * sw[n]), acc = sum_k a[m,k] * w[n,k]
+// (reference kernel: kernels.py:27-55; the epilogue order acc*sa*sw follows kernels.py:53).
+//
+// Design (B200-first, not the reference's tiling):
+//   * Swap-AB.  The tensor-core M=128 axis runs over 128 weight channels (A operand = the
+//     weight tile); the N axis runs over the CTA's tokens (B operand = activations).  One CTA
+//     holds the INT32 accumulators of up to 256 tokens for its 128 channels in TMEM, so the
+//     weights are streamed from HBM once whatever M = B*(k+1) is -- there is no M-tile
+//     staircase (the reference re-streams the weights for every BLOCK_M rows).
+//   * TMA loads 128-byte-swizzled [128 x 128 B] weight tiles and [32-row x 128 B] activation
+//     boxes into a multi-stage mbarrier ring; one elected thread issues tcgen05.mma
+//     kind::i8 (M=128, N=tokens rounded up to 16, K=32 per instruction).
+//   * Split-K across a thread-block cluster along grid.x fills the 148 SMs at small N; the
+//     INT32 partials are reduced through distributed shared memory, no HBM partials.
+//     Integer addition is exact, so any split gives the same bits.
+//   * Plan mode: M is read from plan[0] on the device; CTAs whose token chunk is empty exit,
+//     the MMA N extent is set from the active M, rows >= M are never written.
+//   * When a row stride / base address is not 16-byte aligned (e.g. K = 520), TMA cannot be
+//     used: the epilogue warps, idle during the main loop, load the tiles with vector loads
+//     of the widest aligned width and write the same swizzled layout.
+#pragma once
+
+#include "gemm_common.cuh"
+
+namespace specq {
+
+struct W8A8Params {
+  const int8_t* a;     // [m_rows, K], row stride lda bytes
+  const int8_t* w;     // [N, K], row stride ldw bytes
+  const float* sa;     // [m_rows]
+  const float* sw;     // [N]
+  __half* out;         // fp16 output, strides (ldo, ldo_n) elements   (null in acc mode)
+  int32_t* acc_out;    // raw INT32 accumulator, row stride ldacc    (null in fp16 mode)
+  const int32_t* plan; // optional: plan[0] = active M
+  int* status;
+  int64_t lda, ldw, ldo, ldo_n, ldacc;
+  int m_rows;          // rows the kernel may touch (grid extent)
+  int N, K;
+  int chunk;           // tokens per CTA along grid.z (multiple of 16, <= 256)
+  int kb_total;        // ceil(K / 128)
+  int kb_per_split;    // 128-byte K blocks per split-K CTA
+  int splits;          // cluster size along grid.x
+  int stages;          // pipeline depth
+  uint32_t stage_bytes;
+  uint32_t tmem_cols;
+};
+
+constexpr int kW8A8Threads = 192;  // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue (+ LDG producer)
+constexpr uint32_t kW8A8WTile = 128 * 128;  // bytes of one weight tile
+
+// VEC = 0: TMA producer; VEC in {16, 8, 4, 2, 1}: register-staged loads of that width.
+template <int VEC>
+__global__ void __launch_bounds__(kW8A8Threads, 1)
+    w8a8_kernel(const __grid_constant__ W8A8Params p, const __grid_constant__ CUtensorMap tmap_w,
+                const __grid_constant__ CUtensorMap tmap_a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.stages * p.stage_bytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + p.stages;
+  uint64_t* acc_full = bars + 2 * p.stages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * p.stages + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+  const int split = blockIdx.x;             // == cluster rank (cluster spans grid.x)
+  const int n0 = blockIdx.y * 128;
+  const int m0 = blockIdx.z * p.chunk;
+
+  // ---- active extent (plan mode reads M on the device) --------------------------------
+  int M = p.m_rows;
+  if (p.plan != nullptr) {
+    int pm = __ldg(p.plan);
+    if (pm < 0 || pm > p.m_rows) {
+      if (threadIdx.x == 0 && split == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+        report_status(p.status, SPECQ_STATUS_PLAN_CLAMPED);
+      pm = pm < 0 ? 0 : p.m_rows;
+    }
+    M = pm;
+  }
+  const int m_cnt = min(p.chunk, M - m0);
+  // Every CTA of a cluster shares (blockIdx.y, blockIdx.z), so the whole cluster leaves
+  // together and no cluster barrier is left waiting.
+  if (m_cnt <= 0) return;
+  const uint32_t n_pad = static_cast<uint32_t>((m_cnt + 15) & ~15);   // MMA N
+  const int a_rows = (m_cnt + 31) & ~31;                               // TMA boxes of 32 rows
+  const uint32_t a_bytes = static_cast<uint32_t>(a_rows) * 128u;
+
+  const int kb0 = split * p.kb_per_split;
+  const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
+  const int nkb = kb1 - kb0;                                          // >= 1 (host guarantees)
+
+  // ---- setup ---------------------------------------------------------------------------
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&full[s], VEC == 0 ? 1u : 128u);
+      mbar_init(&empty[s], 1u);
+    }
+    mbar_init(acc_full, 1u);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && VEC == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_w);
+    tma_prefetch_desc(&tmap_a);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, p.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_acc = *tmem_slot;
+
+  // ---- main loop -------------------------------------------------------------------------
+  if (warp == 0) {
+    if (VEC == 0 && elect_one()) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_a = policy_evict_last();
+      int issued = 0;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % p.stages;
+        const uint32_t ph = static_cast<uint32_t>(i / p.stages) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
+        uint8_t* wt = ring + s * p.stage_bytes;
+        uint8_t* at = wt + kW8A8WTile;
+        mbar_arrive_expect_tx(&full[s], kW8A8WTile + a_bytes);
+        const int kx = (kb0 + i) * 128;
+        tma_load_2d(wt, &tmap_w, &full[s], kx, n0, pol_w);
+        for (int r = 0; r < a_rows; r += 32) tma_load_2d(at + r * 128, &tmap_a, &full[s], kx, m0 + r, pol_a);
+        ++issued;
+      }
+      if (*abort_flag) {   // let copies in flight land before the CTA can exit
+        for (int i = max(0, issued - p.stages); i < issued; ++i)
+          mbar_wait(&full[i % p.stages], static_cast<uint32_t>(i / p.stages) & 1u, p.status,
+                    SPECQ_STATUS_TIMEOUT_PIPELINE);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      const uint32_t idesc = idesc_i8(128, n_pad);
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % p.stages;
+        const uint32_t ph = static_cast<uint32_t>(i / p.stages) & 1u;
+        if (!mbar_wait(&full[s], ph, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
+        tc_fence_after();
+        const uint32_t wt = smem_u32(ring + s * p.stage_bytes);
+        const uint32_t at = wt + kW8A8WTile;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t ad = sdesc_sw128(wt + 32u * k, 16u, 1024u);
+          const uint64_t bd = sdesc_sw128(at + 32u * k, 16u, 1024u);
+          umma_i8_ss(tmem_acc, ad, bd, idesc, (i > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);   // stage is free once these MMAs have read it
+      }
+      umma_commit(acc_full);      // accumulator complete
+    }
+  } else {
+    // epilogue warps; in the LDG variant they first produce every stage
+    const int te = static_cast<int>(threadIdx.x) - 64;   // 0..127
+    if constexpr (VEC != 0) {
+      const uint8_t* wbase = reinterpret_cast<const uint8_t*>(p.w);
+      const uint8_t* abase = reinterpret_cast<const uint8_t*>(p.a);
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % p.stages;
+        const uint32_t ph = static_cast<uint32_t>(i / p.stages) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
+        uint8_t* wt = ring + s * p.stage_bytes;
+        uint8_t* at = wt + kW8A8WTile;
+        const int kx = (kb0 + i) * 128;
+        ldg_tile_sw128<VEC>(wt, wbase, p.ldw, n0, 128, p.N, kx, p.K, te, 128);
+        ldg_tile_sw128<VEC>(at, abase, p.lda, m0, a_rows, M, kx, p.K, te, 128);
+        fence_proxy_async_smem();
+        mbar_arrive(&full[s]);
+      }
+    }
+  }
+  __syncwarp();
+
+  // ---- epilogue --------------------------------------------------------------------------
+  const bool epi = warp >= 2;
+  const uint32_t quad = warp & 3u;                      // TMEM lane quadrant of this warp
+  const int row = static_cast<int>(quad * 32 + lane);   // channel within the tile
+  bool ok = true;
+  if (epi) {
+    ok = mbar_wait(acc_full, 0u, p.status, SPECQ_STATUS_TIMEOUT_MMA) && (*abort_flag == 0);
+    tc_fence_after();
+  }
+
+  if (p.splits == 1) {
+    if (epi && ok) {
+      const int n = n0 + row;
+      const float swn = (n < p.N && p.acc_out == nullptr) ? __ldg(p.sw + n) : 0.f;
+      for (uint32_t c0 = 0; c0 < n_pad; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(tmem_acc + ((quad * 32u) << 16) + c0, r);
+        tmem_wait_ld();
+        if (n < p.N) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + static_cast<int>(c0) + j;
+            if (m < M) {
+              const int32_t acc = static_cast<int32_t>(r[j]);
+              if (p.acc_out != nullptr) {
+                p.acc_out[static_cast<int64_t>(m) * p.ldacc + n] = acc;
+              } else {
+                const float v = __fmul_rn(__fmul_rn(static_cast<float>(acc), __ldg(p.sa + m)), swn);
+                p.out[static_cast<int64_t>(m) * p.ldo + static_cast<int64_t>(n) * p.ldo_n] = __float2half_rn(v);
+              }
+            }
+          }
+        }
+      }
+    }
+  } else {
+    // Split-K: every CTA parks its INT32 partial tile in its own (now idle) ring buffer,
+    // the cluster synchronises, then CTA r sums rows [r*R, (r+1)*R) over all ranks through
+    // DSMEM and writes them.  All warps take part in both cluster barriers.
+    const uint32_t pitch = n_pad * 4u + 16u;   // padded row pitch: conflict-free v4 access
+    if (epi && ok) {
+      uint8_t* red = ring;
+      for (uint32_t c0 = 0; c0 < n_pad; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(tmem_acc + ((quad * 32u) << 16) + c0, r);
+        tmem_wait_ld();
+        uint4* dst = reinterpret_cast<uint4*>(red + row * pitch + c0 * 4u);
+        dst[0] = make_uint4(r[0], r[1], r[2], r[3]);
+        dst[1] = make_uint4(r[4], r[5], r[6], r[7]);
+        dst[2] = make_uint4(r[8], r[9], r[10], r[11]);
+        dst[3] = make_uint4(r[12], r[13], r[14], r[15]);
+      }
+    }
+    cluster_sync();
+    if (epi) {
+      const int S = p.splits;
+      const int R = 128 / S;                     // rows owned by this CTA
+      const int nq = static_cast<int>(n_pad >> 2);
+      const int te = static_cast<int>(threadIdx.x) - 64;
+      const uint32_t red_local = smem_u32(ring);
+      // every rank's status is folded in: if any peer aborted its partial is garbage
+      for (int item = te; item < R * nq; item += 128) {
+        const int rl = item % R;
+        const int cq = item / R;
+        const int trow = split * R + rl;
+        const int n = n0 + trow;
+        const uint32_t off = static_cast<uint32_t>(trow) * pitch + static_cast<uint32_t>(cq) * 16u;
+        int32_t s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+        for (int pr = 0; pr < S; ++pr) {
+          const uint4 v = dsmem_ld_v4(dsmem_map(red_local + off, static_cast<uint32_t>(pr)));
+          s0 += static_cast<int32_t>(v.x);
+          s1 += static_cast<int32_t>(v.y);
+          s2 += static_cast<int32_t>(v.z);
+          s3 += static_cast<int32_t>(v.w);
+        }
+        if (ok && n < p.N) {
+          const int32_t sv[4] = {s0, s1, s2, s3};
+          const float swn = (p.acc_out == nullptr) ? __ldg(p.sw + n) : 0.f;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int m = m0 + cq * 4 + j;
+            if (m < M) {
+              if (p.acc_out != nullptr) {
+                p.acc_out[static_cast<int64_t>(m) * p.ldacc + n] = sv[j];
+              } else {
+                const float v = __fmul_rn(__fmul_rn(static_cast<float>(sv[j]), __ldg(p.sa + m)), swn);
+                p.out[static_cast<int64_t>(m) * p.ldo + static_cast<int64_t>(n) * p.ldo_n] = __float2half_rn(v);
+              }
+            }
+          }
+        }
+      }
+    }
+    cluster_sync();   // peers may still be reading this CTA's partial tile
+  }
+
+  // ---- teardown ----------------------------------------------------------------------------
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_acc, p.tmem_cols);
+  }
+}
+
+}  // namespace specq
