@@ -128,6 +128,14 @@ int specq_get_status(int* status, int clear);
  */
 int specq_selftest_wait_timeout(uint64_t limit_ns, void* stream);
 
+/*
+ * Pipeline tracing (builds compiled with -DSPECQ_TRACE only; other builds return
+ * SPECQ_ERR_UNSUPPORTED): the CTA with linear index `cta` records SM-clock timestamps of its
+ * pipeline events into `buffer` (device, 64 x 64 uint64: [event slot][iteration]).
+ * buffer = NULL switches tracing off.
+ */
+int specq_trace_configure(void* buffer, int cta);
+
 /* Message of the last error on this host thread ("" if none). */
 const char* specq_last_error(void);
 

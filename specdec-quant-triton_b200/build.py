@@ -49,13 +49,17 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(s) <= t for s in sources())
 
 
-def build(force: bool = False, verbose_ptxas: bool = False, quiet: bool = False) -> str:
-    if not force and up_to_date():
+def build(force: bool = False, verbose_ptxas: bool = False, quiet: bool = False, trace: bool = False) -> str:
+    """Build libspecq.so; trace=True builds libspecq_trace.so with the pipeline trace points."""
+    out = OUT.replace("libspecq.so", "libspecq_trace.so") if trace else OUT
+    if not force and not trace and up_to_date():
         return OUT
     cmd = [nvcc_path(), *NVCC_FLAGS, "-I", INCLUDE, "-I", CSRC]
+    if trace:
+        cmd += ["-DSPECQ_TRACE"]
     if verbose_ptxas:
         cmd += ["-Xptxas", "-v"]
-    cmd += [os.path.join(CSRC, "specq_api.cu"), "-o", OUT + ".tmp"]
+    cmd += [os.path.join(CSRC, "specq_api.cu"), "-o", out + ".tmp"]
     if not quiet:
         print(" ".join(cmd), flush=True)
     res = subprocess.run(cmd, capture_output=True, text=True)
@@ -64,16 +68,19 @@ def build(force: bool = False, verbose_ptxas: bool = False, quiet: bool = False)
         raise RuntimeError("nvcc failed building libspecq.so")
     if verbose_ptxas or not quiet:
         sys.stderr.write(res.stderr)
-    os.replace(OUT + ".tmp", OUT)
-    return OUT
+    os.replace(out + ".tmp", out)
+    return out
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose-ptxas", action="store_true")
+    ap.add_argument("--trace", action="store_true", help="also build libspecq_trace.so (-DSPECQ_TRACE)")
     args = ap.parse_args()
     print(build(force=args.force, verbose_ptxas=args.verbose_ptxas))
+    if args.trace:
+        print(build(force=True, trace=True))
 
 
 if __name__ == "__main__":

@@ -57,8 +57,9 @@ struct AttnParams {
   uint32_t tmem_cols, col_stride;
 };
 
-constexpr int kAttnThreads = 448;        // warps 0-3 softmax, 4 TMA, 5 MMA, 6-13 convert
-constexpr int kAttnConvThreads = 256;
+constexpr int kAttnConvWarps = 6;
+constexpr int kAttnConvThreads = 32 * kAttnConvWarps;
+constexpr int kAttnThreads = 320 + kAttnConvThreads;   // warps 0-7 softmax, 8 TMA, 9 MMA, 10-15 convert
 constexpr uint32_t kAttnKV8 = 128 * 128;       // int8 K (or V) block: 128 tokens x 128 B
 constexpr uint32_t kAttnStage = 2 * kAttnKV8;  // K + V
 constexpr uint32_t kAttnOp = 128 * 256;        // fp16 operand tile: 128 tokens x 128 d
@@ -118,6 +119,25 @@ __device__ __forceinline__ void i8x16_to_f16(uint4 v, uint32_t (&h)[8]) {
   }
 }
 
+// Write the 16 fp16 values converted from int8 chunk `ch` (d = 16ch .. 16ch+15) of token `row`
+// into a [2 atom columns][128 rows][128 B] 128B-swizzled operand tile.  Threads with ch < 4 and
+// ch >= 4 of the same row land in the two atom columns (16 KB apart, same banks); the upper
+// half stores its two chunks in the opposite order so each 8-thread phase hits 8 distinct
+// bank groups.
+__device__ __forceinline__ void store_f16_chunk_pair(uint8_t* tile, int row, int ch, const uint32_t (&h)[8]) {
+  uint8_t* dst = tile + (ch >> 2) * 16384;
+  const uint4 a = make_uint4(h[0], h[1], h[2], h[3]);
+  const uint4 c = make_uint4(h[4], h[5], h[6], h[7]);
+  const uint32_t k0 = 2u * static_cast<uint32_t>(ch & 3);
+  if (ch < 4) {
+    *reinterpret_cast<uint4*>(dst + sw128_offset(row, k0)) = a;
+    *reinterpret_cast<uint4*>(dst + sw128_offset(row, k0 + 1)) = c;
+  } else {
+    *reinterpret_cast<uint4*>(dst + sw128_offset(row, k0 + 1)) = c;
+    *reinterpret_cast<uint4*>(dst + sw128_offset(row, k0)) = a;
+  }
+}
+
 __device__ __forceinline__ float load_scale(const void* base, int scale_f32, int64_t idx) {
   return scale_f32 ? __ldg(static_cast<const float*>(base) + idx)
                    : __half2float(__ldg(static_cast<const __half*>(base) + idx));
@@ -127,16 +147,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     paged_attn_kernel(const __grid_constant__ AttnParams p, const __grid_constant__ CUtensorMap tmap_k,
                       const __grid_constant__ CUtensorMap tmap_v) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
+  SPECQ_TRACE_INIT();
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int NQ = p.nq;
   uint8_t* ring = smem;                                           // stages x (K int8 | V int8)
-  uint8_t* kop = ring + p.stages * kAttnStage;                    // fp16 K tile  [2][128][128 B]
-  uint8_t* vop = kop + kAttnOp;                                   // fp16 V tile  [2][128][128 B]
-  uint8_t* qop = vop + kAttnOp;                                   // fp16 Q       [2][NQ][128 B]
-  uint8_t* pop = qop + NQ * 256;                                  // fp16 P^T     [2][NQ][128 B]
-  float* scl_c = reinterpret_cast<float*>(pop + NQ * 256);        // [2][128] ks * log2e / sqrt(D)
-  float* scl_v = scl_c + 256;                                     // [2][128] vs
-  float* m_s = scl_v + 256;                                       // [64] running max (log2 units)
+  uint8_t* kop = ring + p.stages * kAttnStage;                    // fp16 K tile      [2][128][128 B]
+  uint8_t* vop = kop + kAttnOp;                                   // fp16 V tiles  x2 [2][128][128 B]
+  uint8_t* qop = vop + 2 * kAttnOp;                               // fp16 Q           [2][NQ][128 B]
+  uint8_t* pop = qop + NQ * 256;                                  // fp16 P^T      x2 [2][NQ][128 B]
+  float* scl_c = reinterpret_cast<float*>(pop + 2 * NQ * 256);    // [2][128] ks * log2e / sqrt(D)
+  __half* scl_vh = reinterpret_cast<__half*>(scl_c + 256);       // [2][128] vs (fp16)
+  float* m_s = scl_c + 512;                                       // [64] running max (log2 units)
   float* alpha_s = m_s + 64;                                      // [64]
   float* l_s = alpha_s + 64;                                      // [64]
   float* wmax = l_s + 64;                                         // [4][64]
@@ -145,14 +166,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* stage_full = bars;
   uint64_t* stage_empty = stage_full + p.stages;
   uint64_t* k_full = stage_empty + p.stages;
-  uint64_t* v_full = k_full + 1;
-  uint64_t* scl_full = v_full + 1;       // [2]
+  uint64_t* v_full = k_full + 1;         // [2]
+  uint64_t* scl_full = v_full + 2;       // [2]
   uint64_t* scl_empty = scl_full + 2;    // [2]
   uint64_t* s_full = scl_empty + 2;      // [2]
   uint64_t* s_empty = s_full + 2;        // [2]
-  uint64_t* p_full = s_empty + 2;
-  uint64_t* pv_done = p_full + 1;
-  uint64_t* q_full = pv_done + 1;
+  uint64_t* p_full = s_empty + 2;        // [2]
+  uint64_t* pv_done = p_full + 2;        // [2]  PV(j) done: frees P and V buffer j % 2
+  uint64_t* q_full = pv_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_full + 1);
 
   const uint32_t warp = warp_id();
@@ -184,7 +205,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int q_lo = qc * p.qpp;
   const int q_hi = min(q_lo + p.qpp, q_len);
   const int rows_valid = (q_hi - q_lo) * p.g;
-  const int qpos0 = L - q_len + q_lo;                 // last visible token of query row group 0
+  const int qpos0 = L - q_len + q_lo;                 // last visible token of query-row group 0
   const int kv_end = max(0, L - q_len + q_hi);
   const int tchunk = ((kv_end + p.splits - 1) / p.splits + 127) & ~127;
   const int t_begin = split * tchunk;
@@ -192,32 +213,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int nblk = (t_end > t_begin) ? (t_end - t_begin + 127) / 128 : 0;
 
   const uint32_t cs = p.col_stride;
-  const uint32_t S_col0 = 0, O_col = 2 * cs, L_col = 3 * cs, ONES_col = 4 * cs;
+  const uint32_t O_col = 2 * cs, L_col = 3 * cs, ONES_col = 4 * cs;
 
   // ---- setup ---------------------------------------------------------------------------------
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&stage_full[s], 1u);
-      mbar_init(&stage_empty[s], 8u);
+      mbar_init(&stage_empty[s], kAttnConvWarps);
     }
-    mbar_init(k_full, 8u);
-    mbar_init(v_full, 8u);
+    mbar_init(k_full, kAttnConvWarps);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&scl_full[i], 8u);
-      mbar_init(&scl_empty[i], 4u);
+      mbar_init(&v_full[i], kAttnConvWarps);
+      mbar_init(&scl_full[i], kAttnConvWarps);
+      mbar_init(&scl_empty[i], 8u);
       mbar_init(&s_full[i], 1u);
-      mbar_init(&s_empty[i], 4u);
+      mbar_init(&s_empty[i], 8u);
+      mbar_init(&p_full[i], 8u);
+      mbar_init(&pv_done[i], 1u);
     }
-    mbar_init(p_full, 4u);
-    mbar_init(pv_done, 1u);
-    mbar_init(q_full, 4u);
+    mbar_init(q_full, 8u);
     fence_barrier_init();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == 8 && lane == 0) {
     tma_prefetch_desc(&tmap_k);
     tma_prefetch_desc(&tmap_v);
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, p.tmem_cols);
     tmem_relinquish();
   }
@@ -227,13 +248,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t tmem = *tmem_slot;
   int* status = p.status;
   bool ok = true;
+  if (threadIdx.x == 0) SPECQ_TRACE_POINT(1, 0);
 
-  if (warp < 4) {
+  if (warp < 8) {
     // =================================== softmax warps ===================================
-    const int t = static_cast<int>(threadIdx.x);             // token lane of S^T, d lane of O^T
-    const uint32_t lane_base = tmem + ((warp * 32u) << 16);
+    // Warps w and w+4 share TMEM lane quadrant w: the same 32 tokens of S^T (the same 32 head
+    // dims of O^T).  Warps 0-3 take the first half of the query columns, warps 4-7 the second.
+    const int t = static_cast<int>(threadIdx.x);             // 0..255
+    const int tl = t & 127;                                  // token lane of S^T, d lane of O^T
+    const int grp = t >> 7;
+    const int nqh = NQ >> 1;                                 // columns per group (multiple of 8)
+    const int col0 = grp * nqh;
+    const uint32_t quad = warp & 3u;
+    const uint32_t lane_base = tmem + ((quad * 32u) << 16);
     // Q rows -> fp16 operand [2 atom columns][NQ rows][128 B], 128B-swizzled; padding rows = 0
-    for (int c = t; c < NQ * 16; c += 128) {
+    for (int c = t; c < NQ * 16; c += 256) {
       const int row = c >> 4;
       const int piece = c & 15;
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
@@ -251,66 +280,92 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
       for (int i = 0; i < 16; ++i) ones[i] = 0x3C003C00u;
 #pragma unroll
-      for (int c = 0; c < 128; c += 16) tmem_st16(lane_base + ONES_col + c, ones);
+      for (int c = 0; c < 64; c += 16) tmem_st16(lane_base + ONES_col + grp * 64 + c, ones);
       tmem_wait_st();
     }
     fence_proxy_async_smem();
     tc_fence_before();
-    named_barrier_sync(3, 128);
+    named_barrier_sync(3, 256);
     __syncwarp();
     if (lane == 0) mbar_arrive(q_full);
 
     // Multi-thread roles never leave a loop early: after a wait runs out (ok = false) they skip
     // the remaining waits but still reach every named barrier, so no warp is stranded.
     for (int j = 0; j < nblk; ++j) {
-      const int tok0 = t_begin + j * 128;
-      const int t_abs = tok0 + t;
-      const bool tok_ok = t_abs < t_end;
+      const int t_abs = t_begin + j * 128 + tl;
       const uint32_t sb = static_cast<uint32_t>(j & 1);
       const uint32_t par2 = static_cast<uint32_t>(j >> 1) & 1u;
-      // per-token K scale (already times log2e / sqrt(D))
+      // query rows q >= q_first may see this token (causal window), rows >= q_stop never do
+      const int q_first = max(0, (t_abs - qpos0) * p.g);
+      const int q_stop = (t_abs < t_end) ? rows_valid : 0;
       ok = ok && mbar_wait(&scl_full[sb], par2, status, SPECQ_STATUS_TIMEOUT_PIPELINE);
-      const float c_t = scl_c[sb * 128 + t];
+      if (t == 0) SPECQ_TRACE_POINT(20, j);
+      const float c_t = scl_c[sb * 128 + tl];
       __syncwarp();
       if (lane == 0) mbar_arrive(&scl_empty[sb]);
       ok = ok && mbar_wait(&s_full[sb], par2, status, SPECQ_STATUS_TIMEOUT_MMA);
+      // P buffer sb is free once PV(j-2) has read it
+      if (j >= 2) ok = ok && mbar_wait(&pv_done[sb], par2 ^ 1u, status, SPECQ_STATUS_TIMEOUT_MMA);
       tc_fence_after();
-      const uint32_t s_addr = lane_base + S_col0 + sb * cs;
+      if (t == 0) SPECQ_TRACE_POINT(21, j);
+      const uint32_t s_addr = lane_base + sb * cs + col0;
+      uint8_t* prow = pop + sb * (NQ * 256) + (tl >> 6) * (NQ * 128) + (tl & 7) * 2;
+      const uint32_t tch = static_cast<uint32_t>((tl & 63) >> 3);
 
-      // pass 1: does any score exceed the running max by more than 2^8?
-      float xmax = -INFINITY;
-      for (int c0 = 0; c0 < NQ; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(s_addr + c0, r);
+      // one optimistic pass: P against the current max, noting whether any score exceeds it
+      // by more than 2^8 (then the block is redone below with a raised max)
+      auto write_p = [&](float& xmax) {
+        // every TMEM load of the pass is issued before a single wait (one round trip)
+        uint32_t r[32];
+#pragma unroll
+        for (int c0 = 0; c0 < 32; c0 += 8)
+          if (c0 < nqh) tmem_ld8(s_addr + c0, *reinterpret_cast<uint32_t(*)[8]>(r + c0));
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int q = c0 + i;
-          const bool valid = tok_ok && q < rows_valid && t_abs <= qpos0 + q / p.g;
-          const float x = __uint_as_float(r[i]) * c_t - m_s[q];
-          xmax = valid ? fmaxf(xmax, x) : xmax;
-        }
-      }
-      const bool need = named_barrier_or(2, 128, xmax > kLazyMaxLog2);
-      if (j > 0) ok = ok && mbar_wait(pv_done, static_cast<uint32_t>(j - 1) & 1u, status, SPECQ_STATUS_TIMEOUT_MMA);
-      tc_fence_after();
-      if (need) {
-        // block max per query row: warp shuffles, then across the four warps
-        for (int c0 = 0; c0 < NQ; c0 += 16) {
-          uint32_t r[16];
-          tmem_ld16(s_addr + c0, r);
-          tmem_wait_ld();
+        for (int c0 = 0; c0 < 32; c0 += 8) {
+          if (c0 < nqh) {
+            const float4* mv = reinterpret_cast<const float4*>(m_s + col0 + c0);
+            const float4 m0 = mv[0], m1 = mv[1];
+            const float mq[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int q = c0 + i;
-            const bool valid = tok_ok && q < rows_valid && t_abs <= qpos0 + q / p.g;
-            float y = valid ? __uint_as_float(r[i]) * c_t : -INFINITY;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) y = fmaxf(y, __shfl_xor_sync(0xffffffffu, y, o));
-            if (lane == 0) wmax[warp * 64 + q] = y;
+            for (int i = 0; i < 8; ++i) {
+              const int q = col0 + c0 + i;
+              const bool valid = q >= q_first && q < q_stop;
+              const float x = __uint_as_float(r[c0 + i]) * c_t - mq[i];
+              xmax = valid ? fmaxf(xmax, x) : xmax;
+              const float pr = valid ? fast_exp2(x) : 0.f;
+              *reinterpret_cast<__half*>(prow + q * 128 + ((tch ^ (static_cast<uint32_t>(q) & 7u)) << 4)) =
+                  __float2half_rn(pr);
+            }
           }
         }
-        named_barrier_sync(3, 128);
+      };
+      float xmax = -INFINITY;
+      write_p(xmax);
+      const bool need = named_barrier_or(2, 256, xmax > kLazyMaxLog2);
+      if (t == 0) SPECQ_TRACE_POINT(22, j);
+      if (need) {
+        if (t == 0) SPECQ_TRACE_POINT(26, j);
+        // the running O^T / normaliser must be final before they are rescaled
+        if (j >= 1)
+          ok = ok && mbar_wait(&pv_done[sb ^ 1u], static_cast<uint32_t>((j - 1) >> 1) & 1u, status,
+                               SPECQ_STATUS_TIMEOUT_MMA);
+        tc_fence_after();
+        // block max per query column: warp shuffles, then across the four lane quadrants
+        for (int c0 = 0; c0 < nqh; c0 += 8) {
+          uint32_t r[8];
+          tmem_ld8(s_addr + c0, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int q = col0 + c0 + i;
+            float y = (q >= q_first && q < q_stop) ? __uint_as_float(r[i]) * c_t : -INFINITY;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) y = fmaxf(y, __shfl_xor_sync(0xffffffffu, y, o));
+            if (lane == 0) wmax[quad * 64 + q] = y;
+          }
+        }
+        named_barrier_sync(3, 256);
         if (t < NQ) {
           const float mb = fmaxf(fmaxf(wmax[t], wmax[64 + t]), fmaxf(wmax[128 + t], wmax[192 + t]));
           const float mo = m_s[t];
@@ -318,74 +373,73 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           alpha_s[t] = (mn == -INFINITY) ? 1.f : fast_exp2(mo - mn);   // exp2(-inf) = 0
           m_s[t] = mn;
         }
-        named_barrier_sync(3, 128);
-        if (j > 0) {   // rescale the running O^T (all lanes) and the normaliser row
-          for (int c0 = 0; c0 < NQ; c0 += 16) {
-            uint32_t r[16];
-            tmem_ld16(lane_base + O_col + c0, r);
+        named_barrier_sync(3, 256);
+        if (j > 0) {   // rescale this group's columns of O^T (all lanes) and of the normaliser row
+          for (int c0 = 0; c0 < nqh; c0 += 8) {
+            uint32_t r[8];
+            tmem_ld8(lane_base + O_col + col0 + c0, r);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha_s[c0 + i]);
-            tmem_st16(lane_base + O_col + c0, r);
-            if (warp == 0) {
-              tmem_ld16(lane_base + L_col + c0, r);
+            for (int i = 0; i < 8; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha_s[col0 + c0 + i]);
+            tmem_st8(lane_base + O_col + col0 + c0, r);
+            if (quad == 0) {
+              tmem_ld8(lane_base + L_col + col0 + c0, r);
               tmem_wait_ld();
 #pragma unroll
-              for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha_s[c0 + i]);
-              tmem_st16(lane_base + L_col + c0, r);
+              for (int i = 0; i < 8; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha_s[col0 + c0 + i]);
+              tmem_st8(lane_base + L_col + col0 + c0, r);
             }
           }
           tmem_wait_st();
         }
-      }
-      // pass 2: P^T[q][t] = fp16(exp2(s * c_t - m_q)) into the K-major operand (t contiguous)
-      uint8_t* prow = pop + (t >> 6) * (NQ * 128) + (t & 7) * 2;
-      const uint32_t tch = static_cast<uint32_t>((t & 63) >> 3);
-      for (int c0 = 0; c0 < NQ; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(s_addr + c0, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int q = c0 + i;
-          const bool valid = tok_ok && q < rows_valid && t_abs <= qpos0 + q / p.g;
-          const float pr = valid ? fast_exp2(__uint_as_float(r[i]) * c_t - m_s[q]) : 0.f;
-          *reinterpret_cast<__half*>(prow + q * 128 + ((tch ^ (static_cast<uint32_t>(q) & 7u)) << 4)) =
-              __float2half_rn(pr);
-        }
+        float unused = -INFINITY;
+        write_p(unused);
       }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&s_empty[sb]);
-        mbar_arrive(p_full);
+        mbar_arrive(&p_full[sb]);
       }
+      if (t == 0) SPECQ_TRACE_POINT(24, j);
     }
     // ---- final normaliser and accumulator ----
     if (nblk > 0) {
       // bounded even after a failure: the tensor core must be idle before TMEM is freed
-      ok = mbar_wait(pv_done, static_cast<uint32_t>(nblk - 1) & 1u, status, SPECQ_STATUS_TIMEOUT_MMA) && ok;
+      const int jl = nblk - 1;
+      ok = mbar_wait(&pv_done[jl & 1], static_cast<uint32_t>(jl >> 1) & 1u, status, SPECQ_STATUS_TIMEOUT_MMA) && ok;
       tc_fence_after();
-      if (warp == 0) {
-        for (int c0 = 0; c0 < NQ; c0 += 16) {
-          uint32_t r[16];
-          tmem_ld16(lane_base + L_col + c0, r);
+      if (quad == 0) {
+        for (int c0 = 0; c0 < nqh; c0 += 8) {
+          uint32_t r[8];
+          tmem_ld8(lane_base + L_col + col0 + c0, r);
           tmem_wait_ld();
           if (lane == 0) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) l_s[c0 + i] = __uint_as_float(r[i]);
+            for (int i = 0; i < 8; ++i) l_s[col0 + c0 + i] = __uint_as_float(r[i]);
           }
         }
       }
     }
-    named_barrier_sync(3, 128);
-  } else if (warp == 4) {
+    named_barrier_sync(3, 256);
+  } else if (warp == 8) {
     // =================================== TMA producer ===================================
     if (elect_one()) {
       const uint64_t pol = policy_evict_first();
       const int nbox = 128 / p.box_rows;
+      // page ids of the next block are loaded into registers one block ahead (independent
+      // loads, all in flight together), so the block-table latency overlaps the ring wait
+      int pgv[16];
+      auto load_pages = [&](int j) {
+        const int tok0 = t_begin + j * 128;
+        const int nb = (min(tok0 + 128, t_end) - tok0 + p.box_rows - 1) / p.box_rows;
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          pgv[i] = (i < nb) ? __ldg(p.bt + b * p.bt_sb + (tok0 + i * p.box_rows) / p.page) : -1;
+      };
       int issued = 0;
+      if (nblk > 0) load_pages(0);
       for (int j = 0; j < nblk; ++j) {
         const int s = j % p.stages;
         if (!mbar_wait(&stage_empty[s], (static_cast<uint32_t>(j / p.stages) & 1u) ^ 1u, status,
@@ -396,11 +450,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int tok0 = t_begin + j * 128;
         const int nb = (min(tok0 + 128, t_end) - tok0 + p.box_rows - 1) / p.box_rows;
         int* pg = pgs + s * 128;
-        for (int i = 0; i < nbox; ++i) {
-          int page = -1;
-          if (i < nb) page = __ldg(p.bt + b * p.bt_sb + (tok0 + i * p.box_rows) / p.page);
-          pg[i] = page;
-        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (i < nbox) pg[i] = pgv[i];
+        for (int i = 16; i < nbox; ++i)      // page sizes below 8 tokens: more than 16 boxes
+          pg[i] = (i < nb) ? __ldg(p.bt + b * p.bt_sb + (tok0 + i * p.box_rows) / p.page) : -1;
+        SPECQ_TRACE_POINT(50, j);
         mbar_arrive_expect_tx(&stage_full[s], static_cast<uint32_t>(nb * p.box_rows * 128 * 2));
         uint8_t* kdst = ring + s * kAttnStage;
         uint8_t* vdst = kdst + kAttnKV8;
@@ -410,7 +465,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tma_load_4d(kdst + i * p.box_rows * 128, &tmap_k, &stage_full[s], 0, kvh, off, pg[i], pol);
           tma_load_4d(vdst + i * p.box_rows * 128, &tmap_v, &stage_full[s], 0, kvh, off, pg[i], pol);
         }
+        SPECQ_TRACE_POINT(51, j);
         ++issued;
+        if (j + 1 < nblk) load_pages(j + 1);
       }
       if (!ok) {
         for (int j = max(0, issued - p.stages); j < issued; ++j)
@@ -418,54 +475,76 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     SPECQ_STATUS_TIMEOUT_PIPELINE);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // =================================== MMA issuer ===================================
     if (elect_one()) {
       const uint32_t id_qk = idesc_f16(128, static_cast<uint32_t>(NQ));
       const uint32_t id_pv = idesc_f16(128, static_cast<uint32_t>(NQ), 1u, 0u);   // A (V^T) MN-major
       const uint32_t kop_a = smem_u32(kop), vop_a = smem_u32(vop), qop_a = smem_u32(qop), pop_a = smem_u32(pop);
       const uint32_t half_q = static_cast<uint32_t>(NQ) * 128u;
-      auto issue_pv = [&](int i) -> bool {
-        if (!mbar_wait(p_full, static_cast<uint32_t>(i) & 1u, status, SPECQ_STATUS_TIMEOUT_PIPELINE) ||
-            !mbar_wait(v_full, static_cast<uint32_t>(i) & 1u, status, SPECQ_STATUS_TIMEOUT_PIPELINE))
-          return false;
+      auto issue_pv = [&](int i) {
+        const uint32_t bi = static_cast<uint32_t>(i & 1);
         tc_fence_after();
+        SPECQ_TRACE_POINT(32, i);
+        const uint32_t vb = vop_a + bi * kAttnOp;
+        const uint32_t pb = pop_a + bi * (2u * half_q);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {   // 16 tokens per step
-          const uint64_t av = sdesc_sw128(vop_a + k * 2048u, 16384u, 1024u);
-          const uint64_t bp = sdesc_sw128(pop_a + (k >> 2) * half_q + (k & 3) * 32u, 16u, 1024u);
+          const uint64_t av = sdesc_sw128(vb + k * 2048u, 16384u, 1024u);
+          const uint64_t bp = sdesc_sw128(pb + (k >> 2) * half_q + (k & 3) * 32u, 16u, 1024u);
           const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
           umma_f16_ss(tmem + O_col, av, bp, id_pv, acc);
           umma_f16_ts(tmem + L_col, tmem + ONES_col + 8u * k, bp, id_qk, acc);
         }
-        umma_commit(pv_done);
-        return true;
+        umma_commit(&pv_done[bi]);
+        SPECQ_TRACE_POINT(33, i);
       };
-      if (nblk > 0) ok = mbar_wait(q_full, 0u, status, SPECQ_STATUS_TIMEOUT_PIPELINE);
-      for (int j = 0; j < nblk && ok; ++j) {
+      auto issue_qk = [&](int j) {
         const uint32_t sb = static_cast<uint32_t>(j & 1);
-        if (!mbar_wait(k_full, static_cast<uint32_t>(j) & 1u, status, SPECQ_STATUS_TIMEOUT_PIPELINE) ||
-            !mbar_wait(&s_empty[sb], (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u, status,
-                       SPECQ_STATUS_TIMEOUT_PIPELINE)) {
-          ok = false;
-          break;
-        }
         tc_fence_after();
+        SPECQ_TRACE_POINT(30, j);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {   // 16 of the 128 head dims per step
           const uint64_t ak = sdesc_sw128(kop_a + (k >> 2) * 16384u + (k & 3) * 32u, 16u, 1024u);
           const uint64_t bq = sdesc_sw128(qop_a + (k >> 2) * half_q + (k & 3) * 32u, 16u, 1024u);
-          umma_f16_ss(tmem + S_col0 + sb * cs, ak, bq, id_qk, k > 0 ? 1u : 0u);
+          umma_f16_ss(tmem + sb * cs, ak, bq, id_qk, k > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[sb]);
-        if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+        SPECQ_TRACE_POINT(31, j);
+      };
+      if (nblk > 0) ok = mbar_wait(q_full, 0u, status, SPECQ_STATUS_TIMEOUT_PIPELINE);
+      // Event loop: QK(j) and PV(j) use disjoint TMEM, so each is issued as soon as its own
+      // inputs are ready (PV(j) never waits behind the conversion of the next K tile).
+      int nqk = 0, npv = 0;
+      uint64_t idle_since = 0;
+      while (ok && npv < nblk) {
+        bool progressed = false;
+        if (nqk < nblk && mbar_test_wait(k_full, static_cast<uint32_t>(nqk) & 1u) &&
+            mbar_test_wait(&s_empty[nqk & 1], (static_cast<uint32_t>(nqk >> 1) & 1u) ^ 1u)) {
+          issue_qk(nqk++);
+          progressed = true;
+        }
+        if (npv < nqk) {
+          const uint32_t bi = static_cast<uint32_t>(npv & 1);
+          const uint32_t par = static_cast<uint32_t>(npv >> 1) & 1u;
+          if (mbar_test_wait(&p_full[bi], par) && mbar_test_wait(&v_full[bi], par)) {
+            issue_pv(npv++);
+            progressed = true;
+          }
+        }
+        if (progressed) {
+          idle_since = 0;
+        } else if (idle_since == 0) {
+          idle_since = globaltimer_ns();
+        } else if (globaltimer_ns() - idle_since > kWaitLimitNs) {
+          report_status(status, SPECQ_STATUS_TIMEOUT_PIPELINE);
+          ok = false;
+        }
       }
-      if (ok && nblk > 0) ok = issue_pv(nblk - 1);
     }
   } else {
     // =================================== converters ===================================
-    const int c = static_cast<int>(threadIdx.x) - 192;   // 0..255
-    const int ch = c & 7;                                // 16-byte chunk of a 128-byte row
+    const int c = static_cast<int>(threadIdx.x) - 320;   // 0..kAttnConvThreads-1
     float ks_cur = 0.f, vs_cur = 0.f;
     auto fetch_scales = [&](int j, float& ksv, float& vsv) -> bool {
       ksv = 0.f;
@@ -488,98 +567,96 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (nblk > 0) ok = fetch_scales(0, ks_cur, vs_cur);
     for (int j = 0; j < nblk; ++j) {
       const int s = j % p.stages;
+      const uint32_t sb = static_cast<uint32_t>(j & 1);
+      const uint32_t par2 = static_cast<uint32_t>(j >> 1) & 1u;
+      if (c == 0) SPECQ_TRACE_POINT(40, j);
       const uint8_t* k8 = ring + s * kAttnStage;
       const uint8_t* v8 = k8 + kAttnKV8;
-      // ---- K: wait until QK(j-1) has read the previous tile
+      // ---- K: the single fp16 K tile is free once QK(j-1) has completed
       if (j > 0)
-        ok = ok && mbar_wait(&s_full[(j - 1) & 1], static_cast<uint32_t>((j - 1) >> 1) & 1u, status,
+        ok = ok && mbar_wait(&s_full[sb ^ 1u], static_cast<uint32_t>((j - 1) >> 1) & 1u, status,
                              SPECQ_STATUS_TIMEOUT_MMA);
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int row = (c >> 3) + 32 * r;
+      // 1024 16-byte chunks per tile: (token row = idx / 8, chunk = idx % 8)
+      for (int idx = c; idx < 1024; idx += kAttnConvThreads) {
+        const int row = idx >> 3;
+        const int ch = idx & 7;
         const uint4 v = *reinterpret_cast<const uint4*>(k8 + row * 128 + ch * 16);
         uint32_t h[8];
         i8x16_to_f16(v, h);
-        uint8_t* dst = kop + (ch >> 2) * 16384;
-        *reinterpret_cast<uint4*>(dst + sw128_offset(row, 2 * (ch & 3))) = make_uint4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<uint4*>(dst + sw128_offset(row, 2 * (ch & 3) + 1)) = make_uint4(h[4], h[5], h[6], h[7]);
+        store_f16_chunk_pair(kop, row, ch, h);
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(k_full);
+      if (c == 0) SPECQ_TRACE_POINT(42, j);
       // ---- per-token scales of this block
-      const uint32_t sb = static_cast<uint32_t>(j & 1);
-      ok = ok && mbar_wait(&scl_empty[sb], (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u, status,
-                           SPECQ_STATUS_TIMEOUT_PIPELINE);
+      ok = ok && mbar_wait(&scl_empty[sb], par2 ^ 1u, status, SPECQ_STATUS_TIMEOUT_PIPELINE);
       if (c < 128) {
         scl_c[sb * 128 + c] = ks_cur * p.sm_scale_log2;
-        scl_v[sb * 128 + c] = vs_cur;
+        scl_vh[sb * 128 + c] = __float2half_rn(vs_cur);
       }
       named_barrier_sync(1, kAttnConvThreads);
       __syncwarp();
       if (lane == 0) mbar_arrive(&scl_full[sb]);
-      // ---- V (scale folded in): wait until PV(j-1) has read the previous tile
-      if (j > 0) ok = ok && mbar_wait(pv_done, static_cast<uint32_t>(j - 1) & 1u, status, SPECQ_STATUS_TIMEOUT_MMA);
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int row = (c >> 3) + 32 * r;
+      if (c == 0) SPECQ_TRACE_POINT(43, j);
+      // ---- V (scale folded in) into buffer sb, free once PV(j-2) has completed
+      if (j >= 2) ok = ok && mbar_wait(&pv_done[sb], par2 ^ 1u, status, SPECQ_STATUS_TIMEOUT_MMA);
+      uint8_t* vdst = vop + sb * kAttnOp;
+      for (int idx = c; idx < 1024; idx += kAttnConvThreads) {
+        const int row = idx >> 3;
+        const int ch = idx & 7;
         const uint4 v = *reinterpret_cast<const uint4*>(v8 + row * 128 + ch * 16);
         uint32_t h[8];
         i8x16_to_f16(v, h);
-        const float vsr = scl_v[sb * 128 + row];
-        if (p.scale_f32) {
+        // the token's V scale in fp16 (exact for fp16 scales; one rounding for fp32 scales), so
+        // the per-element multiply stays on the fp16 pipe
+        const __half2 s2 = __half2half2(scl_vh[sb * 128 + row]);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float2 f = __half22float2(*reinterpret_cast<__half2*>(&h[i]));
-            __half2 o = __floats2half2_rn(f.x * vsr, f.y * vsr);
-            h[i] = *reinterpret_cast<uint32_t*>(&o);
-          }
-        } else {
-          const __half2 s2 = __half2half2(__float2half_rn(vsr));   // exact: vsr came from fp16
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            __half2 o = __hmul2(*reinterpret_cast<__half2*>(&h[i]), s2);
-            h[i] = *reinterpret_cast<uint32_t*>(&o);
-          }
+        for (int i = 0; i < 8; ++i) {
+          __half2 o = __hmul2(*reinterpret_cast<__half2*>(&h[i]), s2);
+          h[i] = *reinterpret_cast<uint32_t*>(&o);
         }
-        uint8_t* dst = vop + (ch >> 2) * 16384;
-        *reinterpret_cast<uint4*>(dst + sw128_offset(row, 2 * (ch & 3))) = make_uint4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<uint4*>(dst + sw128_offset(row, 2 * (ch & 3) + 1)) = make_uint4(h[4], h[5], h[6], h[7]);
+        store_f16_chunk_pair(vdst, row, ch, h);
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(v_full);
+        mbar_arrive(&v_full[sb]);
         mbar_arrive(&stage_empty[s]);
       }
+      if (c == 0) SPECQ_TRACE_POINT(45, j);
       if (j + 1 < nblk) ok = (ok && fetch_scales(j + 1, ks_cur, vs_cur)) && ok;
     }
   }
   __syncwarp();
 
   // ======================= epilogue: normalise, combine splits, store =======================
-  const bool soft = warp < 4;
+  // softmax warps: thread tl owns head dim d = tl (TMEM lane) for its group's query columns
+  const bool soft = warp < 8;
   const int t = static_cast<int>(threadIdx.x);
+  const int tl = t & 127;
+  const int col0 = (t >> 7) * (NQ >> 1);
+  const uint32_t o_lane = tmem + (((warp & 3u) * 32u) << 16) + O_col + static_cast<uint32_t>(col0);
   if (p.splits == 1) {
     if (soft && ok) {
-      uint32_t r[16];
-      for (int c0 = 0; c0 < NQ; c0 += 16) {
+      for (int c0 = 0; c0 < (NQ >> 1); c0 += 8) {
+        uint32_t r[8];
         if (nblk > 0) {
-          tmem_ld16(tmem + ((warp * 32u) << 16) + O_col + c0, r);
+          tmem_ld8(o_lane + c0, r);
           tmem_wait_ld();
         } else {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) r[i] = 0u;
+          for (int i = 0; i < 8; ++i) r[i] = 0u;
         }
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int q = c0 + i;
+        for (int i = 0; i < 8; ++i) {
+          const int q = col0 + c0 + i;
           if (q < rows_valid) {
             const int qi = q_lo + q / p.g;
             const int head = kvh * p.g + q % p.g;
             const float l = l_s[q];
             const float o = __uint_as_float(r[i]) / (l == 0.f ? 1.f : l);
-            p.out[b * p.o_sb + static_cast<int64_t>(qi) * p.o_st + static_cast<int64_t>(head) * p.o_sh + t] =
+            p.out[b * p.o_sb + static_cast<int64_t>(qi) * p.o_st + static_cast<int64_t>(head) * p.o_sh + tl] =
                 __float2half_rn(o);
           }
         }
@@ -588,37 +665,50 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else {
     float* comb = reinterpret_cast<float*>(ring);   // [NQ][128] partial O (ring is idle now)
     if (soft) {
-      uint32_t r[16];
-      for (int c0 = 0; c0 < NQ; c0 += 16) {
+      for (int c0 = 0; c0 < (NQ >> 1); c0 += 8) {
+        uint32_t r[8];
         if (nblk > 0 && ok) {
-          tmem_ld16(tmem + ((warp * 32u) << 16) + O_col + c0, r);
+          tmem_ld8(o_lane + c0, r);
           tmem_wait_ld();
         } else {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) r[i] = 0u;
+          for (int i = 0; i < 8; ++i) r[i] = 0u;
         }
 #pragma unroll
-        for (int i = 0; i < 16; ++i) comb[(c0 + i) * 128 + t] = __uint_as_float(r[i]);
+        for (int i = 0; i < 8; ++i) comb[(col0 + c0 + i) * 128 + tl] = __uint_as_float(r[i]);
       }
       if (nblk == 0 && t < 64) { m_s[t] = -INFINITY; l_s[t] = 0.f; }
     }
     cluster_sync();
     if (soft) {
       const int S = p.splits;
-      const int dr = 128 / S;
+      const int lgdr = 7 - (31 - __clz(S));   // d columns per rank: 128 / S
+      const int dr = 1 << lgdr;
       const int d0 = split * dr;
-      const uint32_t comb_a = smem_u32(comb), m_a = smem_u32(m_s), l_a = smem_u32(l_s);
-      for (int item = t; item < rows_valid * dr; item += 128) {
-        const int q = item / dr;
-        const int d = d0 + item % dr;
+      for (int item = t; item < rows_valid * dr; item += 256) {
+        const int q = item >> lgdr;
+        const int d = d0 + (item & (dr - 1));
+        float mp[8], lp[8], op[8];
+#pragma unroll
+        for (int pr = 0; pr < 8; ++pr) {     // every peer's loads in flight together
+          if (pr < S) {
+            mp[pr] = *dsmem_ptr(m_s + q, static_cast<uint32_t>(pr));
+            lp[pr] = *dsmem_ptr(l_s + q, static_cast<uint32_t>(pr));
+            op[pr] = *dsmem_ptr(comb + q * 128 + d, static_cast<uint32_t>(pr));
+          }
+        }
         float mmax = -INFINITY;
-        for (int pr = 0; pr < S; ++pr) mmax = fmaxf(mmax, dsmem_ld_f32(dsmem_map(m_a + q * 4u, pr)));
+#pragma unroll
+        for (int pr = 0; pr < 8; ++pr)
+          if (pr < S) mmax = fmaxf(mmax, mp[pr]);
         float lsum = 0.f, osum = 0.f;
-        for (int pr = 0; pr < S; ++pr) {   // fixed order: identical bits for any schedule
-          const float mp = dsmem_ld_f32(dsmem_map(m_a + q * 4u, pr));
-          const float w = (mp == -INFINITY) ? 0.f : fast_exp2(mp - mmax);
-          lsum += w * dsmem_ld_f32(dsmem_map(l_a + q * 4u, pr));
-          osum += w * dsmem_ld_f32(dsmem_map(comb_a + (q * 128u + d) * 4u, pr));
+#pragma unroll
+        for (int pr = 0; pr < 8; ++pr) {     // fixed order: identical bits for any schedule
+          if (pr < S) {
+            const float w = (mp[pr] == -INFINITY) ? 0.f : fast_exp2(mp[pr] - mmax);
+            lsum += w * lp[pr];
+            osum += w * op[pr];
+          }
         }
         if (ok) {
           const int qi = q_lo + q / p.g;
@@ -633,7 +723,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (threadIdx.x == 0) SPECQ_TRACE_POINT(9, 0);
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, p.tmem_cols);
   }
@@ -699,7 +790,7 @@ inline int run_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_
   // plan-mode launches reduce identical partials.
   const int max_ctx = bt_cols * page;
   p.splits = std::min(8, std::max(1, ceil_div(max_ctx, 2048)));
-  p.stages = 3;
+  p.stages = 2;
   p.sm_scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
   p.col_stride = static_cast<uint32_t>(round_up(p.nq, 32));
   p.tmem_cols = static_cast<uint32_t>(next_pow2(static_cast<int>(4 * p.col_stride + 128)));
@@ -707,8 +798,9 @@ inline int run_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_
   if (static_cast<int64_t>(b_grid) * p.n_qc > 65535)
     return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: grid too large");
 
-  const int smem = 1024 + p.stages * static_cast<int>(kAttnStage) + 2 * static_cast<int>(kAttnOp) + 2 * p.nq * 256 +
-                   512 * 4 + 448 * 4 + p.stages * 128 * 4 + 32 * 8 + 64;
+  // ring + fp16 K tile + two fp16 V tiles + Q + two P^T tiles + scales + softmax state + pages
+  const int smem = 1024 + p.stages * static_cast<int>(kAttnStage) + 3 * static_cast<int>(kAttnOp) + 3 * p.nq * 256 +
+                   512 * 4 + 448 * 4 + p.stages * 128 * 4 + (2 * p.stages + 16) * 8 + 64;
   if (smem > 232448) return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: shared memory %d too large", smem);
   if (p.nq * 128 * 4 > p.stages * static_cast<int>(kAttnStage))
     return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: combine buffer does not fit");

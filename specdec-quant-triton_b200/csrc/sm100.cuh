@@ -39,6 +39,33 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
+// ---- optional pipeline tracing (compiled in only with -DSPECQ_TRACE) -------------------------
+// One selected CTA records SM-clock timestamps of its pipeline events into a device buffer
+// [slot][iteration] (64 x 64 uint64) configured through specq_trace_configure().
+#ifdef SPECQ_TRACE
+__device__ unsigned long long* g_specq_trace_buf = nullptr;
+__device__ int g_specq_trace_cta = 0;
+// Resolve once per kernel (at entry) whether this CTA records, so that each trace point is
+// only a clock read and a store.
+#define SPECQ_TRACE_INIT()                                                                    \
+  unsigned long long* specq_trace_ =                                                         \
+      (static_cast<int>(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)) ==   \
+       ::specq::g_specq_trace_cta)                                                           \
+          ? ::specq::g_specq_trace_buf                                                       \
+          : nullptr
+#define SPECQ_TRACE_POINT(slot, iter)                                                         \
+  do {                                                                                        \
+    if (specq_trace_ != nullptr) specq_trace_[(slot) * 64 + min(static_cast<int>(iter), 63)] = clock64(); \
+  } while (0)
+#else
+#define SPECQ_TRACE_INIT() \
+  do {                     \
+  } while (0)
+#define SPECQ_TRACE_POINT(slot, iter) \
+  do {                                \
+  } while (0)
+#endif
+
 // Record the first error code of a launch; later codes do not overwrite it.
 __device__ __forceinline__ void report_status(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
@@ -87,13 +114,40 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of phase `parity` (for loops that poll several barriers).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// try_wait with a suspend-time hint: the thread sleeps (instead of spinning and taking issue
+// slots from the working warps) until the phase completes or ~0.5 ms pass.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(500000u)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for phase `parity` of `bar`.  Returns false (and records `code` in the status
 // word) when the limit runs out; the caller then abandons its loop.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity)) return true;
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
       report_status(status, code);
       return false;
@@ -264,6 +318,11 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -290,6 +349,15 @@ __device__ __forceinline__ uint32_t dsmem_map(uint32_t local_saddr, uint32_t ran
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_saddr), "r"(rank));
   return r;
 }
+// Generic address of the same shared-memory object in CTA `rank` of the cluster; ordinary
+// loads through it can be scheduled (batched) by the compiler.
+template <typename T>
+__device__ __forceinline__ const T* dsmem_ptr(const T* local, uint32_t rank) {
+  uint64_t r;
+  asm("mapa.u64 %0, %1, %2;" : "=l"(r) : "l"(reinterpret_cast<uint64_t>(local)), "r"(rank));
+  return reinterpret_cast<const T*>(r);
+}
+
 __device__ __forceinline__ uint4 dsmem_ld_v4(uint32_t cluster_saddr) {
   uint4 v;
   asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"

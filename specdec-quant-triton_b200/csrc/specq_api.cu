@@ -97,9 +97,9 @@ int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int
   p.splits = S;
   p.kb_per_split = ceil_div(p.kb_total, S);
 
-  p.stage_bytes = kW8A8WTile + static_cast<uint32_t>(round_up(p.chunk, 32)) * 128u;
+  p.stage_bytes = kW8A8WTile + static_cast<uint32_t>(round_up(p.chunk, 16)) * 128u;
   const uint32_t red_bytes = (S > 1) ? 128u * (static_cast<uint32_t>(p.chunk) * 4u + 16u) : 0u;
-  const int overhead = 1024 + 256;
+  const int overhead = 1024 + 256 + 384 * 4;   // alignment slack, barriers, staged scales
   int stages = std::min(8, (kSmemLimit - overhead) / static_cast<int>(p.stage_bytes));
   if (stages < 2) return fail(SPECQ_ERR_UNSUPPORTED, "w8a8: token chunk %d does not fit shared memory", p.chunk);
   while (static_cast<uint32_t>(stages) * p.stage_bytes < red_bytes && stages < 8) ++stages;
@@ -121,7 +121,7 @@ int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int
     if (int rc = encode_tiled(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, dw, sw_, bw, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
     const uint64_t da[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
     const uint64_t sa_[1] = {static_cast<uint64_t>(lda)};
-    const uint32_t ba[2] = {128, 32};
+    const uint32_t ba[2] = {128, 16};
     if (int rc = encode_tiled(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a, da, sa_, ba, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
   } else {
     vec = common_vec_width({reinterpret_cast<uintptr_t>(a), reinterpret_cast<uintptr_t>(w),
@@ -204,16 +204,15 @@ int run_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const
   }
   p.splits = S;
   p.kb_per_split = ceil_div(p.kb_total, S);
-  p.dstages = 2;
-  const int cols_lo = (64 * p.kb_per_split + group - 1) / group + 1;
-  p.sc_cache_cols = static_cast<uint32_t>(2 * cols_lo);
-  const int sc_bytes = round_up(128 * static_cast<int>(p.sc_cache_cols) * 2, 16);
+  p.dstages = 3;
+  p.sc_cache_cols = 0;   // scales are prefetched into registers per K-block
+  const int sc_bytes = 0;
 
   int n_chunks = ceil_div(M, 256);
   int smem = 0;
   while (true) {
     p.chunk = round_up(ceil_div(M, n_chunks), 16);
-    p.stage_bytes = kW4A16PackTile + 2u * static_cast<uint32_t>(round_up(p.chunk, 32)) * 128u;
+    p.stage_bytes = kW4A16PackTile + 2u * static_cast<uint32_t>(round_up(p.chunk, 16)) * 128u;
     const int fixed = 1024 + p.dstages * static_cast<int>(kW4A16DSlot) + sc_bytes + 512;
     const uint32_t red_bytes = (S > 1) ? 128u * (static_cast<uint32_t>(p.chunk) * 4u + 16u) : 0u;
     int stages = std::min(6, (kSmemLimit - fixed) / static_cast<int>(p.stage_bytes));
@@ -241,7 +240,7 @@ int run_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const
   {
     const uint64_t d[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
     const uint64_t s_[1] = {static_cast<uint64_t>(lda) * 2u};
-    const uint32_t b[2] = {64, 32};
+    const uint32_t b[2] = {64, 16};
     if (int rc = encode_tiled(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, d, s_, b, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
   }
   const dim3 grid(static_cast<unsigned>(S), static_cast<unsigned>(n_tiles), static_cast<unsigned>(n_chunks));
@@ -307,17 +306,20 @@ const char* specq_last_error(void) { return last_error_ref().c_str(); }
 
 int specq_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int64_t ldw, const float* sw,
                void* out, int64_t ldo, int64_t ldo_n, const int32_t* plan, int M, int N, int K, void* stream) {
+  last_launch_ref() = LaunchRecord();
   return run_w8a8(a, lda, sa, w, ldw, sw, out, ldo, ldo_n, nullptr, 0, plan, M, N, K, stream);
 }
 
 int specq_w8a8_acc(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw, int32_t* acc, int64_t ldacc,
                    const int32_t* plan, int M, int N, int K, void* stream) {
+  last_launch_ref() = LaunchRecord();
   if (acc == nullptr) return fail(SPECQ_ERR_INVALID_ARG, "w8a8_acc: null accumulator pointer");
   return run_w8a8(a, lda, nullptr, w, ldw, nullptr, nullptr, 0, 1, acc, ldacc, plan, M, N, K, stream);
 }
 
 int specq_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const void* sc, int64_t ldsc, int group,
                 void* out, int64_t ldo, int64_t ldo_n, const int32_t* plan, int M, int N, int K, void* stream) {
+  last_launch_ref() = LaunchRecord();
   return run_w4a16(a, lda, wp, ldwp, sc, ldsc, group, out, ldo, ldo_n, plan, M, N, K, stream);
 }
 
@@ -327,6 +329,7 @@ int specq_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_t q_s
                           int64_t bt_sb, int bt_cols, const int32_t* ctx_len, void* out, int64_t o_sb, int64_t o_st,
                           int64_t o_sh, const int32_t* plan, int B, int n_seqs, int q_len, int ql_max, int H,
                           int H_KV, int D, int page, int qpp, void* stream) {
+  last_launch_ref() = LaunchRecord();
   return run_paged_attention(q, q_sb, q_st, q_sh, kc, vc, kv_sp, kv_so, kv_sh, n_pages, ks, vs, s_sp, s_so, s_sh,
                              scale_dtype, block_tbl, bt_sb, bt_cols, ctx_len, out, o_sb, o_st, o_sh, plan, B, n_seqs,
                              q_len, ql_max, H, H_KV, D, page, qpp, stream);
@@ -373,6 +376,19 @@ int specq_get_status(int* status, int clear) {
   }
   if (status) *status = v;
   return SPECQ_OK;
+}
+
+int specq_trace_configure(void* buffer, int cta) {
+#ifdef SPECQ_TRACE
+  unsigned long long* b = static_cast<unsigned long long*>(buffer);
+  SPECQ_CUDA_TRY(cudaMemcpyToSymbol(g_specq_trace_buf, &b, sizeof(b)));
+  SPECQ_CUDA_TRY(cudaMemcpyToSymbol(g_specq_trace_cta, &cta, sizeof(cta)));
+  return SPECQ_OK;
+#else
+  (void)buffer;
+  (void)cta;
+  return fail(SPECQ_ERR_UNSUPPORTED, "trace points are compiled in only with -DSPECQ_TRACE");
+#endif
 }
 
 int specq_selftest_wait_timeout(uint64_t limit_ns, void* stream) {

@@ -43,8 +43,9 @@ struct W4A16Params {
   uint32_t tmem_cols;
 };
 
-constexpr int kW4A16Threads = 320;          // warp 0 TMA, warp 1 MMA, warps 2..9 dequant (2..5 epilogue)
-constexpr int kW4A16DequantThreads = 256;
+constexpr int kW4A16DequantWarps = 16;
+constexpr int kW4A16DequantThreads = 32 * kW4A16DequantWarps;
+constexpr int kW4A16Threads = 64 + kW4A16DequantThreads;   // warp 0 TMA, warp 1 MMA, then dequant (2..5 epilogue)
 constexpr uint32_t kW4A16PackTile = 128 * 64;   // packed bytes per stage
 constexpr uint32_t kW4A16OpTile = 128 * 128;    // one fp16 [128 x 64] operand tile
 constexpr uint32_t kW4A16DSlot = 2 * kW4A16OpTile;
@@ -88,6 +89,7 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
     w4a16_kernel(const __grid_constant__ W4A16Params p, const __grid_constant__ CUtensorMap tmap_wp,
                  const __grid_constant__ CUtensorMap tmap_a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
+  SPECQ_TRACE_INIT();
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;                                              // TMA stages
   uint8_t* dring = ring + p.stages * p.stage_bytes;                  // dequantised operand slots
@@ -122,7 +124,7 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
   const int m_cnt = min(p.chunk, M - m0);
   if (m_cnt <= 0) return;                       // whole cluster shares (y, z)
   const uint32_t n_pad = static_cast<uint32_t>((m_cnt + 15) & ~15);
-  const int a_rows = (m_cnt + 31) & ~31;
+  const int a_rows = (m_cnt + 15) & ~15;                       // TMA boxes of 16 rows
   const uint32_t a_bytes = static_cast<uint32_t>(a_rows) * 128u;
 
   const int kb0 = split * p.kb_per_split;
@@ -131,14 +133,15 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
   const int glo0 = (kb0 * 64) / p.group;        // first cached low-half group
   const int ghi0 = (half_k + kb0 * 64) / p.group;
   const int nlo = (kb1 * 64 - 1) / p.group - glo0 + 1;
+  if (threadIdx.x == 0) SPECQ_TRACE_POINT(0, 0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full[s], 1u);
-      mbar_init(&empty[s], 9u);                 // 8 dequant warps + 1 MMA commit
+      mbar_init(&empty[s], kW4A16DequantWarps + 1u);   // dequant warps + 1 MMA commit
     }
     for (int d = 0; d < p.dstages; ++d) {
-      mbar_init(&dfull[d], 8u);
+      mbar_init(&dfull[d], kW4A16DequantWarps);
       mbar_init(&dempty[d], 1u);
     }
     mbar_init(acc_full, 1u);
@@ -157,6 +160,7 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_acc = *tmem_slot;
+  if (threadIdx.x == 0) SPECQ_TRACE_POINT(1, 0);
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -168,13 +172,14 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
         const int s = i % p.stages;
         const uint32_t ph = static_cast<uint32_t>(i / p.stages) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
+        SPECQ_TRACE_POINT(2, i);
         uint8_t* st = ring + s * p.stage_bytes;
         mbar_arrive_expect_tx(&full[s], kW4A16PackTile + 2u * a_bytes);
         const int kb = kb0 + i;
         tma_load_2d(st, &tmap_wp, &full[s], kb * 64, n0, pol_w);
         uint8_t* alo = st + kW4A16PackTile;
         uint8_t* ahi = alo + a_bytes;
-        for (int r = 0; r < a_rows; r += 32) {
+        for (int r = 0; r < a_rows; r += 16) {
           tma_load_2d(alo + r * 128, &tmap_a, &full[s], kb * 64, m0 + r, pol_a);
           tma_load_2d(ahi + r * 128, &tmap_a, &full[s], half_k + kb * 64, m0 + r, pol_a);
         }
@@ -199,6 +204,7 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
           break;
         }
         tc_fence_after();
+        SPECQ_TRACE_POINT(3, i);
         const uint32_t alo = smem_u32(ring + s * p.stage_bytes) + kW4A16PackTile;
         const uint32_t ahi = alo + a_bytes;
         const uint32_t wlo = smem_u32(dring + d * kW4A16DSlot);
@@ -213,24 +219,23 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
                       1u);
         umma_commit(&empty[s]);
         umma_commit(&dempty[d]);
+        SPECQ_TRACE_POINT(4, i);
       }
       umma_commit(acc_full);
     }
   } else {
     // ---------------- dequant warps ----------------
-    const int td = static_cast<int>(threadIdx.x) - 64;   // 0..255
-    const int cols = static_cast<int>(p.sc_cache_cols);
-    // cache the fp16 group scales this CTA needs: low groups [glo0, glo0+nlo), high groups after
-    for (int idx = td; idx < 128 * cols; idx += kW4A16DequantThreads) {
-      const int r = idx / cols;
-      const int c = idx % cols;
-      const int n = n0 + r;
-      const int g = (c < nlo) ? (glo0 + c) : (ghi0 + c - nlo);
-      __half v = __ushort_as_half(0);
-      if (n < p.N && g < p.K / p.group) v = p.sc[static_cast<int64_t>(n) * p.ldsc + g];
-      sc_cache[idx] = v;
-    }
-    named_barrier_sync(1, kW4A16DequantThreads);
+    const int td = static_cast<int>(threadIdx.x) - 64;   // 0..511
+    // This thread dequantises 16-byte chunk (td & 3) of row td / 4 of every packed tile; the
+    // row's two fp16 group scales for the next K-block are fetched one block ahead.
+    const int r0 = td >> 2;
+    const int64_t row0 = static_cast<int64_t>(min(n0 + r0, p.N - 1)) * p.ldsc;
+    auto fetch = [&](int kb, __half (&s2)[2]) {
+      s2[0] = p.sc[row0 + (kb * 64) / p.group];
+      s2[1] = p.sc[row0 + (half_k + kb * 64) / p.group];
+    };
+    __half sc_cur[2], sc_nxt[2];
+    fetch(kb0, sc_cur);
     for (int i = 0; i < nkb; ++i) {
       const int s = i % p.stages;
       const int d = i % p.dstages;
@@ -240,37 +245,33 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
         *abort_flag = 1;
         break;
       }
+      if (td == 0) SPECQ_TRACE_POINT(10, i);
       const uint8_t* pk = ring + s * p.stage_bytes;
       uint8_t* wlo = dring + d * kW4A16DSlot;
       uint8_t* whi = wlo + kW4A16OpTile;
-      const int kb = kb0 + i;
-      const int clo = (kb * 64) / p.group - glo0;
-      const int chi = nlo + (half_k + kb * 64) / p.group - ghi0;
-      uint4 raw[2];
-#pragma unroll
-      for (int pass = 0; pass < 2; ++pass) {
-        const int idx = td + pass * kW4A16DequantThreads;   // 0..511: (row, 16-byte chunk)
-        raw[pass] = *reinterpret_cast<const uint4*>(pk + idx * 16);
-      }
+      if (i + 1 < nkb) fetch(kb0 + i + 1, sc_nxt);
+      const uint4 raw = *reinterpret_cast<const uint4*>(pk + td * 16);   // (row td/4, chunk td%4)
+      if (td == 0) SPECQ_TRACE_POINT(12, raw.x == 0x12345678u ? 63 : i);
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);    // packed tile consumed (activations: MMA commit)
-#pragma unroll
-      for (int pass = 0; pass < 2; ++pass) {
-        const int idx = td + pass * kW4A16DequantThreads;
-        const int r = idx >> 2;
-        const int c = idx & 3;
-        const __half2 slo = __half2half2(sc_cache[r * cols + clo]);
-        const __half2 shi = __half2half2(sc_cache[r * cols + chi]);
+      {
+        const int r = td >> 2;
+        const int c = td & 3;
         uint4 lo[2], hi[2];
-        dequant_chunk(raw[pass], slo, shi, lo, hi);
+        dequant_chunk(raw, __half2half2(sc_cur[0]), __half2half2(sc_cur[1]), lo, hi);
         *reinterpret_cast<uint4*>(wlo + sw128_offset(r, 2 * c)) = lo[0];
         *reinterpret_cast<uint4*>(wlo + sw128_offset(r, 2 * c + 1)) = lo[1];
         *reinterpret_cast<uint4*>(whi + sw128_offset(r, 2 * c)) = hi[0];
         *reinterpret_cast<uint4*>(whi + sw128_offset(r, 2 * c + 1)) = hi[1];
       }
+      if (td == 0) SPECQ_TRACE_POINT(13, i);
       fence_proxy_async_smem();
+      if (td == 0) SPECQ_TRACE_POINT(14, i);
       __syncwarp();
       if (lane == 0) mbar_arrive(&dfull[d]);
+      if (td == 0) SPECQ_TRACE_POINT(11, i);
+      sc_cur[0] = sc_nxt[0];
+      sc_cur[1] = sc_nxt[1];
     }
   }
   __syncwarp();
@@ -283,6 +284,7 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
   if (epi) {
     ok = mbar_wait(acc_full, 0u, p.status, SPECQ_STATUS_TIMEOUT_MMA) && (*abort_flag == 0);
     tc_fence_after();
+    if (warp == 2 && lane == 0) SPECQ_TRACE_POINT(5, 0);
   }
   if (p.splits == 1) {
     if (epi && ok) {
@@ -321,23 +323,28 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
     cluster_sync();
     if (epi) {
       const int S = p.splits;
-      const int R = 128 / S;
+      const int lgR = 7 - (31 - __clz(S));
+      const int R = 1 << lgR;
       const int nq = static_cast<int>(n_pad >> 2);
       const int te = static_cast<int>(threadIdx.x) - 64;
-      const uint32_t red_local = smem_u32(ring);
       for (int item = te; item < R * nq; item += 128) {
-        const int rl = item % R;
-        const int cq = item / R;
-        const int trow = split * R + rl;
+        const int cq = item >> lgR;
+        const int trow = split * R + (item & (R - 1));
         const int n = n0 + trow;
-        const uint32_t off = static_cast<uint32_t>(trow) * pitch + static_cast<uint32_t>(cq) * 16u;
+        const float4* src = reinterpret_cast<const float4*>(ring + trow * pitch + cq * 16);
+        float4 v[8];
+#pragma unroll
+        for (int pr = 0; pr < 8; ++pr)      // all peers' loads in flight together
+          if (pr < S) v[pr] = *dsmem_ptr(src, static_cast<uint32_t>(pr));
         float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-        for (int pr = 0; pr < S; ++pr) {     // fixed order: the same bits for any schedule
-          const uint4 v = dsmem_ld_v4(dsmem_map(red_local + off, static_cast<uint32_t>(pr)));
-          s0 += __uint_as_float(v.x);
-          s1 += __uint_as_float(v.y);
-          s2 += __uint_as_float(v.z);
-          s3 += __uint_as_float(v.w);
+#pragma unroll
+        for (int pr = 0; pr < 8; ++pr) {    // fixed order: the same bits for any schedule
+          if (pr < S) {
+            s0 += v[pr].x;
+            s1 += v[pr].y;
+            s2 += v[pr].z;
+            s3 += v[pr].w;
+          }
         }
         if (ok && n < p.N) {
           const float sv[4] = {s0, s1, s2, s3};
@@ -355,6 +362,7 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) SPECQ_TRACE_POINT(9, 0);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_acc, p.tmem_cols);

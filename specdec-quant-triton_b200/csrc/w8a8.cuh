@@ -56,6 +56,7 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
     w8a8_kernel(const __grid_constant__ W8A8Params p, const __grid_constant__ CUtensorMap tmap_w,
                 const __grid_constant__ CUtensorMap tmap_a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
+  SPECQ_TRACE_INIT();
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.stages * p.stage_bytes);
@@ -64,6 +65,8 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
   uint64_t* acc_full = bars + 2 * p.stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * p.stages + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* sa_s = reinterpret_cast<float*>(tmem_slot + 4);      // [256] token scales of this chunk
+  float* sw_s = sa_s + 256;                                   // [128] channel scales of this tile
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -87,12 +90,13 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
   // together and no cluster barrier is left waiting.
   if (m_cnt <= 0) return;
   const uint32_t n_pad = static_cast<uint32_t>((m_cnt + 15) & ~15);   // MMA N
-  const int a_rows = (m_cnt + 31) & ~31;                               // TMA boxes of 32 rows
+  const int a_rows = (m_cnt + 15) & ~15;                               // TMA boxes of 16 rows
   const uint32_t a_bytes = static_cast<uint32_t>(a_rows) * 128u;
 
   const int kb0 = split * p.kb_per_split;
   const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
   const int nkb = kb1 - kb0;                                          // >= 1 (host guarantees)
+  if (threadIdx.x == 0) SPECQ_TRACE_POINT(0, 0);
 
   // ---- setup ---------------------------------------------------------------------------
   if (threadIdx.x == 0) {
@@ -112,10 +116,16 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
     tmem_alloc(tmem_slot, p.tmem_cols);
     tmem_relinquish();
   }
+  if (warp >= 2 && p.acc_out == nullptr) {   // epilogue scales staged once, read from smem
+    const int te = static_cast<int>(threadIdx.x) - 64;
+    for (int i = te; i < m_cnt; i += 128) sa_s[i] = __ldg(p.sa + m0 + i);
+    sw_s[te] = (n0 + te < p.N) ? __ldg(p.sw + n0 + te) : 0.f;
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_acc = *tmem_slot;
+  if (threadIdx.x == 0) SPECQ_TRACE_POINT(1, 0);
 
   // ---- main loop -------------------------------------------------------------------------
   if (warp == 0) {
@@ -127,12 +137,13 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
         const int s = i % p.stages;
         const uint32_t ph = static_cast<uint32_t>(i / p.stages) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
+        SPECQ_TRACE_POINT(2, i);
         uint8_t* wt = ring + s * p.stage_bytes;
         uint8_t* at = wt + kW8A8WTile;
         mbar_arrive_expect_tx(&full[s], kW8A8WTile + a_bytes);
         const int kx = (kb0 + i) * 128;
         tma_load_2d(wt, &tmap_w, &full[s], kx, n0, pol_w);
-        for (int r = 0; r < a_rows; r += 32) tma_load_2d(at + r * 128, &tmap_a, &full[s], kx, m0 + r, pol_a);
+        for (int r = 0; r < a_rows; r += 16) tma_load_2d(at + r * 128, &tmap_a, &full[s], kx, m0 + r, pol_a);
         ++issued;
       }
       if (*abort_flag) {   // let copies in flight land before the CTA can exit
@@ -149,6 +160,7 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
         const uint32_t ph = static_cast<uint32_t>(i / p.stages) & 1u;
         if (!mbar_wait(&full[s], ph, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
         tc_fence_after();
+        SPECQ_TRACE_POINT(3, i);
         const uint32_t wt = smem_u32(ring + s * p.stage_bytes);
         const uint32_t at = wt + kW8A8WTile;
 #pragma unroll
@@ -158,6 +170,7 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
           umma_i8_ss(tmem_acc, ad, bd, idesc, (i > 0 || k > 0) ? 1u : 0u);
         }
         umma_commit(&empty[s]);   // stage is free once these MMAs have read it
+        SPECQ_TRACE_POINT(4, i);
       }
       umma_commit(acc_full);      // accumulator complete
     }
@@ -191,12 +204,13 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
   if (epi) {
     ok = mbar_wait(acc_full, 0u, p.status, SPECQ_STATUS_TIMEOUT_MMA) && (*abort_flag == 0);
     tc_fence_after();
+    if (warp == 2 && lane == 0) SPECQ_TRACE_POINT(5, 0);
   }
 
   if (p.splits == 1) {
     if (epi && ok) {
       const int n = n0 + row;
-      const float swn = (n < p.N && p.acc_out == nullptr) ? __ldg(p.sw + n) : 0.f;
+      const float swn = sw_s[row];
       for (uint32_t c0 = 0; c0 < n_pad; c0 += 16) {
         uint32_t r[16];
         tmem_ld16(tmem_acc + ((quad * 32u) << 16) + c0, r);
@@ -210,7 +224,7 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
               if (p.acc_out != nullptr) {
                 p.acc_out[static_cast<int64_t>(m) * p.ldacc + n] = acc;
               } else {
-                const float v = __fmul_rn(__fmul_rn(static_cast<float>(acc), __ldg(p.sa + m)), swn);
+                const float v = __fmul_rn(__fmul_rn(static_cast<float>(acc), sa_s[m - m0]), swn);
                 p.out[static_cast<int64_t>(m) * p.ldo + static_cast<int64_t>(n) * p.ldo_n] = __float2half_rn(v);
               }
             }
@@ -237,30 +251,45 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
       }
     }
     cluster_sync();
+    if (warp == 2 && lane == 0) SPECQ_TRACE_POINT(6, 0);
     if (epi) {
       const int S = p.splits;
-      const int R = 128 / S;                     // rows owned by this CTA
+      const int lgR = 7 - (31 - __clz(S));       // rows owned by this CTA: R = 128 / S
+      const int R = 1 << lgR;
       const int nq = static_cast<int>(n_pad >> 2);
       const int te = static_cast<int>(threadIdx.x) - 64;
-      const uint32_t red_local = smem_u32(ring);
-      // every rank's status is folded in: if any peer aborted its partial is garbage
-      for (int item = te; item < R * nq; item += 128) {
-        const int rl = item % R;
-        const int cq = item / R;
-        const int trow = split * R + rl;
-        const int n = n0 + trow;
-        const uint32_t off = static_cast<uint32_t>(trow) * pitch + static_cast<uint32_t>(cq) * 16u;
-        int32_t s0 = 0, s1 = 0, s2 = 0, s3 = 0;
-        for (int pr = 0; pr < S; ++pr) {
-          const uint4 v = dsmem_ld_v4(dsmem_map(red_local + off, static_cast<uint32_t>(pr)));
-          s0 += static_cast<int32_t>(v.x);
-          s1 += static_cast<int32_t>(v.y);
-          s2 += static_cast<int32_t>(v.z);
-          s3 += static_cast<int32_t>(v.w);
+      // Two items per thread per pass and all peers' loads unrolled: the DSMEM round trips
+      // overlap instead of running one after another.
+      for (int it0 = te; it0 < R * nq; it0 += 256) {
+        int4 acc[2] = {make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0)};
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int item = it0 + u * 128;
+          if (item < R * nq) {
+            const int trow = split * R + (item & (R - 1));
+            const uint4* src = reinterpret_cast<const uint4*>(ring + trow * pitch + (item >> lgR) * 16);
+#pragma unroll
+            for (int pr = 0; pr < 8; ++pr) {
+              if (pr < S) {
+                const uint4 v = *dsmem_ptr(src, static_cast<uint32_t>(pr));
+                acc[u].x += static_cast<int32_t>(v.x);
+                acc[u].y += static_cast<int32_t>(v.y);
+                acc[u].z += static_cast<int32_t>(v.z);
+                acc[u].w += static_cast<int32_t>(v.w);
+              }
+            }
+          }
         }
+        if (warp == 2 && lane == 0) SPECQ_TRACE_POINT(12, it0 >> 8);
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+        const int item = it0 + u * 128;
+        if (item >= R * nq) break;
+        const int cq = item >> lgR;
+        const int n = n0 + split * R + (item & (R - 1));
         if (ok && n < p.N) {
-          const int32_t sv[4] = {s0, s1, s2, s3};
-          const float swn = (p.acc_out == nullptr) ? __ldg(p.sw + n) : 0.f;
+          const int32_t sv[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
+          const float swn = sw_s[n - n0];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int m = m0 + cq * 4 + j;
@@ -268,20 +297,24 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
               if (p.acc_out != nullptr) {
                 p.acc_out[static_cast<int64_t>(m) * p.ldacc + n] = sv[j];
               } else {
-                const float v = __fmul_rn(__fmul_rn(static_cast<float>(sv[j]), __ldg(p.sa + m)), swn);
+                const float v = __fmul_rn(__fmul_rn(static_cast<float>(sv[j]), sa_s[m - m0]), swn);
                 p.out[static_cast<int64_t>(m) * p.ldo + static_cast<int64_t>(n) * p.ldo_n] = __float2half_rn(v);
               }
             }
           }
         }
+        }
       }
     }
+    if (warp == 2 && lane == 0) SPECQ_TRACE_POINT(7, 0);
     cluster_sync();   // peers may still be reading this CTA's partial tile
+    if (warp == 2 && lane == 0) SPECQ_TRACE_POINT(8, 0);
   }
 
   // ---- teardown ----------------------------------------------------------------------------
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) SPECQ_TRACE_POINT(9, 0);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_acc, p.tmem_cols);

@@ -9,7 +9,9 @@ import ctypes as C
 import os
 import threading
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libspecq.so")
+# SPECQ_LIB selects another build of the same ABI (e.g. libspecq_trace.so, built with
+# `build.py --trace`, whose kernels record pipeline timestamps).
+LIB_PATH = os.environ.get("SPECQ_LIB") or os.path.join(os.path.dirname(os.path.abspath(__file__)), "libspecq.so")
 
 SPECQ_OK = 0
 SPECQ_ERR_INVALID_ARG = 1
@@ -42,6 +44,7 @@ SIGNATURES = {
     "specq_last_launch": (_i32, [_pi32, _pi32, _pi32, _pi32, _pi32, _pi32, _pi32]),
     "specq_get_status": (_i32, [_pi32, _i32]),
     "specq_selftest_wait_timeout": (_i32, [_u64, _vp]),
+    "specq_trace_configure": (_i32, [_vp, _i32]),
 }
 
 _lock = threading.Lock()

@@ -32,7 +32,9 @@ class KernelHandle:
     """What a launch used: variant, registers, local (spill) bytes, shared memory, grid."""
 
     def __init__(self, which: int, launch: dict, hints: dict):
-        info = _kernel_info_cached(which, launch["variant"])
+        # variant < 0: the call launched nothing (an empty problem)
+        info = (_kernel_info_cached(which, launch["variant"]) if launch["variant"] >= 0 else
+                {"n_regs": 0, "local_bytes": 0, "static_smem": 0})
         self.kernel = ("w8a8", "w4a16", "paged_attention")[which]
         self.variant = launch["variant"]
         self.n_regs = info["n_regs"]
@@ -146,7 +148,8 @@ def w8a8_matmul(a_q, sa, w_q, sw, out=None, BLOCK_M=16, BLOCK_N=64, BLOCK_K=128,
                               sw.data_ptr(), out.data_ptr(), out.stride(0), out.stride(1), _plan_ptr(plan),
                               m_rows, N, K, _stream()))
     launch = _lib.last_launch()
-    _w8a8_kernel.record(launch["variant"])
+    if launch["variant"] >= 0:
+        _w8a8_kernel.record(launch["variant"])
     ck = KernelHandle(W8A8, launch, dict(BLOCK_M=BLOCK_M, BLOCK_N=BLOCK_N, BLOCK_K=BLOCK_K, num_warps=num_warps,
                                          num_stages=num_stages))
     return out, ck
@@ -197,7 +200,8 @@ def w4a16_matmul(a, wp, sc, group=128, out=None, BLOCK_M=16, BLOCK_N=64, BLOCK_K
                                group, out.data_ptr(), out.stride(0), out.stride(1), _plan_ptr(plan), m_rows, N, K,
                                _stream()))
     launch = _lib.last_launch()
-    _w4a16_kernel.record(launch["variant"])
+    if launch["variant"] >= 0:
+        _w4a16_kernel.record(launch["variant"])
     ck = KernelHandle(W4A16, launch, dict(BLOCK_M=BLOCK_M, BLOCK_N=BLOCK_N, BLOCK_K=BLOCK_K, num_warps=num_warps,
                                           num_stages=num_stages))
     return out, ck
@@ -245,7 +249,8 @@ def paged_attention(q, kc, vc, ks, vs, block_tbl, ctx_len, q_len, QPP=None, BLOC
         out_k.data_ptr(), out_k.stride(0), out_k.stride(1), out_k.stride(2),
         _plan_ptr(plan), B, n_seqs, q_len, QLMAX, H, H_KV, D, PAGE, QPP, _stream()))
     launch = _lib.last_launch()
-    _paged_attn_kernel.record(launch["variant"])
+    if launch["variant"] >= 0:
+        _paged_attn_kernel.record(launch["variant"])
     ck = KernelHandle(PAGED_ATTN, launch, dict(QPP=QPP, BLOCK_N=BLOCK_N, num_warps=num_warps,
                                                num_stages=num_stages))
     return out, ck
