@@ -396,6 +396,8 @@ def run_ours(args):
         torch.cuda.synchronize()
         # long enough (~0.7 s) for the clock sampler to see the GPU under load
         reps = max(5, min(20000, int(700.0 / max(step_ms, 1e-3) / n_copies)))
+        if args.per_kernel_reps:
+            reps = args.per_kernel_reps
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(reps):
@@ -505,6 +507,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--per-kernel-reps", type=int, default=0,
+                    help="replays per kernel for the per-kernel durations (0: ~0.7 s each); small values "
+                         "keep the launch count low for a profiler's launch list")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

@@ -10,23 +10,32 @@
 //     rows (all heads of the GQA group) share every K/V byte it reads.
 //   * Transposed products put the 128 tokens of a KV block on the tcgen05 M=128 axis and the
 //     query rows (padded to a multiple of 16) on N:  S^T = K . Q^T  and  O^T = V^T . P^T.  No
-//     tensor-core lane is wasted on padding query rows; the V tile is read MN-major straight
-//     from the layout the K tile uses.
-//   * K/V pages are gathered through the block table by TMA (one box per page run of one
-//     head), into a multi-stage int8 ring; eight converter warps dequantise to fp16 operand
-//     tiles (K exact, V with its per-token scale folded in).
+//     tensor-core lane is wasted on padding query rows.
+//   * K/V rows are gathered through the block table by two warps with 16-byte cp.async copies
+//     (four whole 128-byte rows per warp instruction) into a 3-stage int8 ring; the same warps
+//     fetch each token's K and V scales into the stage.  K lands in the 128B-swizzled layout
+//     the tensor core reads and feeds an INT8 MMA as it is: each query row is quantised once
+//     per CTA to int16 (scale amax/32639, 16x finer than the fp16 query itself) and split as
+//     hi*256 + lo with hi, lo int8, so one kind::i8 MMA with N = 2*NQ gives both integer
+//     partial products exactly in int32.  Five warps dequantise V to fp16 with its per-token
+//     scale folded in; the V tile is read MN-major by the PV product.
 //   * Softmax runs one thread per token row of S^T (TMEM lane = token): the per-token K scale
-//     is a per-thread scalar.  The running max is "lazy": a block is exponentiated against the
+//     is a per-thread scalar, the query-row scale a per-column one; the arithmetic runs on
+//     packed fp32 pairs.  The running max is "lazy": a block is exponentiated against the
 //     current max and only when some score exceeds it by more than 2^8 does the CTA reduce
-//     the block max, rescale O^T and the normaliser, and recompute.  The normaliser
-//     l = sum_t p is produced by the tensor core itself (a ones operand in TMEM times P^T).
-//   * Long contexts are split across a thread-block cluster; the partial (m, l, O) of every
-//     split are combined through distributed shared memory in fixed rank order.  The split
-//     count depends only on the block-table width, so plan mode and eager mode give the same
-//     bits.
+//     the block max, rescale O^T and the normaliser, and recompute.  Blocks that lie wholly
+//     inside every query row's causal window take a mask-free path.  P is written MN-major
+//     (one 16-byte store per 8 query rows).  The normaliser l = sum_t p is produced by the
+//     tensor core itself (a ones operand in TMEM times P).
+//   * Long contexts are split across a thread-block cluster (a power of two, from the
+//     block-table width only, so plan mode and eager mode give the same bits).  Each CTA
+//     pushes its partial (m, l, O) for the head dims a peer owns into that peer's shared
+//     memory; every CTA then combines its own head dims in fixed split order.
 //   * Plan mode reads (n_seqs, q_len) on the device; CTAs outside them return, nothing outside
 //     them is written.
 #pragma once
+
+#include <type_traits>
 
 #include "sm100.cuh"
 #include "specq_host.cuh"
@@ -36,6 +45,9 @@ namespace specq {
 struct AttnParams {
   const __half* q;
   int64_t q_sb, q_st, q_sh;
+  const int8_t* kc;
+  const int8_t* vc;
+  int64_t kv_sp, kv_so, kv_sh;
   const void* ks;
   const void* vs;
   int64_t s_sp, s_so, s_sh;
@@ -51,28 +63,28 @@ struct AttnParams {
   int n_pages;
   int b_grid, n_seqs, q_len, ql_max;
   int h_kv, g, page, qpp, nq, n_qc;
-  int box_rows;
+  int g_shift, page_shift;  // log2 of g / page when they are powers of two, else -1
   int splits, stages;
   float sm_scale_log2;     // log2(e) / sqrt(D)
-  uint32_t tmem_cols, col_stride;
+  uint32_t tmem_cols;
+  uint32_t col_stride;     // TMEM columns of one score buffer (2 * nq int32, rounded to 32)
+  uint32_t o_cols;         // TMEM columns of O^T and of the normaliser (nq, rounded to 32)
+  int out_vec;             // out rows are 16-byte aligned: 8 head dims per store
 };
 
-constexpr int kAttnConvWarps = 6;
+// warps [0, 8) softmax, [8, 10) K/V gather, 10 MMA issue + TMEM owner, [11, 16) V conversion
+constexpr int kAttnLoadWarps = 2;
+constexpr int kAttnMmaWarp = 8 + kAttnLoadWarps;
+constexpr int kAttnConvWarps = 5;
 constexpr int kAttnConvThreads = 32 * kAttnConvWarps;
-constexpr int kAttnThreads = 320 + kAttnConvThreads;   // warps 0-7 softmax, 8 TMA, 9 MMA, 10-15 convert
+constexpr int kAttnThreads = 32 * (kAttnMmaWarp + 1) + kAttnConvThreads;
 constexpr uint32_t kAttnKV8 = 128 * 128;       // int8 K (or V) block: 128 tokens x 128 B
-constexpr uint32_t kAttnStage = 2 * kAttnKV8;  // K + V
-constexpr uint32_t kAttnOp = 128 * 256;        // fp16 operand tile: 128 tokens x 128 d
+constexpr uint32_t kAttnScl = 2 * kAttnKV8;    // stage offset of the per-token scales
+constexpr uint32_t kAttnStage = kAttnScl + 1024;   // K + V + scales (f32 K scale, f16 V scale)
+constexpr uint32_t kAttnOp = 128 * 256;        // fp16 V tile: 128 tokens x 128 d
+constexpr int kAttnStages = 3;
+constexpr uint32_t kAttnPTile = 128 * 128;     // fp16 P tile: 128 tokens x 64 query rows
 constexpr float kLazyMaxLog2 = 8.0f;           // rescale once a score exceeds the max by 2^8
-
-__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,
-                                            int w, uint64_t cache_hint) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w), "l"(cache_hint)
-      : "memory");
-}
 
 // D[tmem] (+)= A[tmem] * B[smem]^T, FP16 -> FP32 (A read from tensor memory).
 __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
@@ -100,7 +112,7 @@ __device__ __forceinline__ bool named_barrier_or(uint32_t id, uint32_t nthreads,
 
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
-  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
@@ -143,36 +155,80 @@ __device__ __forceinline__ float load_scale(const void* base, int scale_f32, int
                    : __half2float(__ldg(static_cast<const __half*>(base) + idx));
 }
 
-__global__ void __launch_bounds__(kAttnThreads, 1)
-    paged_attn_kernel(const __grid_constant__ AttnParams p, const __grid_constant__ CUtensorMap tmap_k,
-                      const __grid_constant__ CUtensorMap tmap_v) {
+// cp.async 16 bytes global -> shared; src_size 0 zero-fills the destination.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_size) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_size) : "memory");
+}
+
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: two lanes of work per instruction).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// The score accumulators start every block at the bit pattern of 1.5 * 2^23 (kScoreBias), so
+// the int8 MMA leaves 1.5 * 2^23 + S in each column: read as a float that is S plus a constant
+// (|S| < 2^22), with no integer-to-float conversion.  256 * hi + lo then comes out of one
+// fused multiply-add and one exact subtraction of 257 * 1.5 * 2^23 (the sum rounds to a
+// multiple of 256 near 2^31.6: an error of at most 128 units of the int16-scaled query,
+// below the query's own quantisation error).
+constexpr uint32_t kScoreBias = 0x4B400000u;
+constexpr float kScoreBias257 = 3233808384.f;   // 257 * 1.5 * 2^23, exact in fp32
+
+__global__ void __launch_bounds__(kAttnThreads, 1) paged_attn_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   SPECQ_TRACE_INIT();
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int NQ = p.nq;
-  uint8_t* ring = smem;                                           // stages x (K int8 | V int8)
-  uint8_t* kop = ring + p.stages * kAttnStage;                    // fp16 K tile      [2][128][128 B]
-  uint8_t* vop = kop + kAttnOp;                                   // fp16 V tiles  x2 [2][128][128 B]
-  uint8_t* qop = vop + 2 * kAttnOp;                               // fp16 Q           [2][NQ][128 B]
-  uint8_t* pop = qop + NQ * 256;                                  // fp16 P^T      x2 [2][NQ][128 B]
-  float* scl_c = reinterpret_cast<float*>(pop + 2 * NQ * 256);    // [2][128] ks * log2e / sqrt(D)
-  __half* scl_vh = reinterpret_cast<__half*>(scl_c + 256);       // [2][128] vs (fp16)
-  float* m_s = scl_c + 512;                                       // [64] running max (log2 units)
+  // ring stage: [K int8, 128 tokens x 128 B, 128B-swizzled (a tcgen05 operand as it lands)]
+  //             [V int8, 128 tokens x 128 B, plain rows (converted to fp16 by the V warps)]
+  //             [K scale x log2(e)/sqrt(D), f32 x 128][V scale, f16 x 128]
+  uint8_t* ring = smem;
+  uint8_t* vop = ring + kAttnStages * kAttnStage;                   // fp16 V tiles x2 [2][128][128 B]
+  uint8_t* qop = vop + 2 * kAttnOp;                               // int8 Q: hi rows [0,NQ), lo rows [NQ,2NQ)
+  uint8_t* pop = qop + NQ * 256;                                  // fp16 P x2 [2][128 tokens][128 B]
+  float* m_s = reinterpret_cast<float*>(pop + 2 * kAttnPTile);      // [64] running max (log2 units)
   float* alpha_s = m_s + 64;                                      // [64]
   float* l_s = alpha_s + 64;                                      // [64]
-  float* wmax = l_s + 64;                                         // [4][64]
-  int* pgs = reinterpret_cast<int*>(wmax + 256);                  // [stages][128] page of each box
-  uint64_t* bars = reinterpret_cast<uint64_t*>(pgs + p.stages * 128);
+  float* qs_s = l_s + 64;                                         // [64] query-row scale of the int16 Q
+  float* nm_s = qs_s + 64;                                        // [64] -m_s
+  float* wmax = nm_s + 64;                                        // [4][64]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(wmax + 256);
   uint64_t* stage_full = bars;
-  uint64_t* stage_empty = stage_full + p.stages;
-  uint64_t* k_full = stage_empty + p.stages;
-  uint64_t* v_full = k_full + 1;         // [2]
-  uint64_t* scl_full = v_full + 2;       // [2]
-  uint64_t* scl_empty = scl_full + 2;    // [2]
-  uint64_t* s_full = scl_empty + 2;      // [2]
-  uint64_t* s_empty = s_full + 2;        // [2]
-  uint64_t* p_full = s_empty + 2;        // [2]
-  uint64_t* pv_done = p_full + 2;        // [2]  PV(j) done: frees P and V buffer j % 2
+  uint64_t* stage_empty = stage_full + kAttnStages;
+  uint64_t* v_full = stage_empty + kAttnStages;   // [2]
+  uint64_t* s_full = v_full + 2;               // [2]
+  uint64_t* s_empty = s_full + 2;              // [2]
+  uint64_t* p_full = s_empty + 2;              // [2]
+  uint64_t* pv_done = p_full + 2;              // [2]  PV(j) done: frees P and V buffer j % 2
   uint64_t* q_full = pv_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_full + 1);
 
@@ -212,20 +268,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int t_end = min(kv_end, t_begin + tchunk);
   const int nblk = (t_end > t_begin) ? (t_end - t_begin + 127) / 128 : 0;
 
-  const uint32_t cs = p.col_stride;
-  const uint32_t O_col = 2 * cs, L_col = 3 * cs, ONES_col = 4 * cs;
+  const uint32_t cs2 = p.col_stride;                   // S buffer: int32 hi columns then lo columns
+  const uint32_t O_col = 2 * cs2;
+  const uint32_t L_col = O_col + p.o_cols;
+  const uint32_t ONES_col = L_col + p.o_cols;
+  auto page_of = [&](int tok) { return p.page_shift >= 0 ? (tok >> p.page_shift) : (tok / p.page); };
+  auto slot_of = [&](int tok) { return p.page_shift >= 0 ? (tok & (p.page - 1)) : (tok % p.page); };
 
   // ---- setup ---------------------------------------------------------------------------------
   if (threadIdx.x == 0) {
-    for (int s = 0; s < p.stages; ++s) {
-      mbar_init(&stage_full[s], 1u);
-      mbar_init(&stage_empty[s], kAttnConvWarps);
+    for (int s = 0; s < kAttnStages; ++s) {
+      // gather lanes' cp.async arrivals + one arrival per gather warp for the scales it stored
+      mbar_init(&stage_full[s], 33u * kAttnLoadWarps);
+      // V warps + the QK commit + the softmax warps (K scales read)
+      mbar_init(&stage_empty[s], kAttnConvWarps + 1u + 8u);
     }
-    mbar_init(k_full, kAttnConvWarps);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&v_full[i], kAttnConvWarps);
-      mbar_init(&scl_full[i], kAttnConvWarps);
-      mbar_init(&scl_empty[i], 8u);
       mbar_init(&s_full[i], 1u);
       mbar_init(&s_empty[i], 8u);
       mbar_init(&p_full[i], 8u);
@@ -234,11 +293,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     mbar_init(q_full, 8u);
     fence_barrier_init();
   }
-  if (warp == 8 && lane == 0) {
-    tma_prefetch_desc(&tmap_k);
-    tma_prefetch_desc(&tmap_v);
-  }
-  if (warp == 9) {
+  if (warp == kAttnMmaWarp) {
     tmem_alloc(tmem_slot, p.tmem_cols);
     tmem_relinquish();
   }
@@ -261,28 +316,77 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int col0 = grp * nqh;
     const uint32_t quad = warp & 3u;
     const uint32_t lane_base = tmem + ((quad * 32u) << 16);
-    // Q rows -> fp16 operand [2 atom columns][NQ rows][128 B], 128B-swizzled; padding rows = 0
-    for (int c = t; c < NQ * 16; c += 256) {
-      const int row = c >> 4;
-      const int piece = c & 15;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    // Q rows -> int16 per row (scale amax / 32639), split as hi * 256 + lo with hi, lo int8:
+    // two int8 operand rows each, so QK^T runs on the INT8 tensor core against the raw K bytes.
+    for (int it = t; it < NQ * 8; it += 256) {
+      const int row = it >> 3;
+      const int piece = it & 7;                              // 16 head dims
+      float qv[16];
       if (row < rows_valid) {
-        const int qi = q_lo + row / p.g;
-        const int head = kvh * p.g + row % p.g;
-        const __half* src = p.q + b * p.q_sb + static_cast<int64_t>(qi) * p.q_st + static_cast<int64_t>(head) * p.q_sh;
-        v = __ldg(reinterpret_cast<const uint4*>(src) + piece);
+        const int qi = q_lo + (p.g_shift >= 0 ? (row >> p.g_shift) : (row / p.g));
+        const int head = kvh * p.g + (p.g_shift >= 0 ? (row & (p.g - 1)) : (row % p.g));
+        const uint4* src = reinterpret_cast<const uint4*>(p.q + b * p.q_sb + static_cast<int64_t>(qi) * p.q_st +
+                                                          static_cast<int64_t>(head) * p.q_sh) + 2 * piece;
+        const uint4 u0 = __ldg(src), u1 = __ldg(src + 1);
+        const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+          qv[2 * i] = f.x;
+          qv[2 * i + 1] = f.y;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) qv[i] = 0.f;
       }
-      *reinterpret_cast<uint4*>(qop + (piece >> 3) * (NQ * 128) + sw128_offset(row, piece & 7)) = v;
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(qv[i]));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+      const float inv = amax > 0.f ? 32639.f / amax : 0.f;
+      uint32_t hw[4] = {0u, 0u, 0u, 0u}, lw[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int v16 = __float2int_rn(qv[i] * inv);        // |v16| <= 32639
+        const int hi = (v16 + 128) >> 8;                     // in [-127, 127]
+        const int lo = v16 - (hi << 8);                      // in [-128, 127]
+        hw[i >> 2] |= (static_cast<uint32_t>(hi) & 0xFFu) << (8 * (i & 3));
+        lw[i >> 2] |= (static_cast<uint32_t>(lo) & 0xFFu) << (8 * (i & 3));
+      }
+      *reinterpret_cast<uint4*>(qop + sw128_offset(row, piece)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(qop + sw128_offset(NQ + row, piece)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+      if (piece == 0) qs_s[row] = amax / 32639.f;
     }
-    if (t < 64) { m_s[t] = -INFINITY; alpha_s[t] = 1.f; l_s[t] = 0.f; }
-    {   // ones operand for the normaliser MMA (fp16 1.0 pairs; 128 columns cover 8 K-steps)
+    // padding rows (all-zero queries, never stored) start at max 0: their scores are exactly 0,
+    // so they never trigger a rescale and the interior blocks need no column mask
+    if (t < 64) {
+      m_s[t] = t < rows_valid ? -INFINITY : 0.f;
+      nm_s[t] = t < rows_valid ? INFINITY : 0.f;
+      alpha_s[t] = 1.f;
+      l_s[t] = 0.f;
+    }
+    uint32_t bias8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) bias8[i] = kScoreBias;
+    // this thread's hi and lo columns of score buffer sb back to the bias
+    auto rebias = [&](uint32_t sb) {
+      for (int c0 = 0; c0 < nqh; c0 += 8) {
+        tmem_st8(lane_base + sb * cs2 + col0 + c0, bias8);
+        tmem_st8(lane_base + sb * cs2 + NQ + col0 + c0, bias8);
+      }
+    };
+    rebias(0u);
+    rebias(1u);
+    {   // ones operand of the normaliser MMA: fp16 1.0 pairs, 8 columns per 16-token K-step
       uint32_t ones[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) ones[i] = 0x3C003C00u;
 #pragma unroll
-      for (int c = 0; c < 64; c += 16) tmem_st16(lane_base + ONES_col + grp * 64 + c, ones);
-      tmem_wait_st();
+      for (int c = 0; c < 32; c += 16) tmem_st16(lane_base + ONES_col + grp * 32 + c, ones);
     }
+    tmem_wait_st();
     fence_proxy_async_smem();
     tc_fence_before();
     named_barrier_sync(3, 256);
@@ -296,47 +400,79 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const uint32_t sb = static_cast<uint32_t>(j & 1);
       const uint32_t par2 = static_cast<uint32_t>(j >> 1) & 1u;
       // query rows q >= q_first may see this token (causal window), rows >= q_stop never do
-      const int q_first = max(0, (t_abs - qpos0) * p.g);
       const int q_stop = (t_abs < t_end) ? rows_valid : 0;
-      ok = ok && mbar_wait(&scl_full[sb], par2, status, SPECQ_STATUS_TIMEOUT_PIPELINE);
-      if (t == 0) SPECQ_TRACE_POINT(20, j);
-      const float c_t = scl_c[sb * 128 + tl];
+      const int q_first = min(max(0, (t_abs - qpos0) * p.g), q_stop);
+      // this token's K scale (log2(e) / sqrt(D) folded in), from the ring stage of block j
+      const int st = j % kAttnStages;
+      ok = ok && mbar_wait(&stage_full[st], static_cast<uint32_t>(j / kAttnStages) & 1u, status,
+                           SPECQ_STATUS_TIMEOUT_PIPELINE);
+      const float c_t = reinterpret_cast<const float*>(ring + st * kAttnStage + kAttnScl)[tl];
       __syncwarp();
-      if (lane == 0) mbar_arrive(&scl_empty[sb]);
+      if (lane == 0) mbar_arrive(&stage_empty[st]);
+      if (t == 0) SPECQ_TRACE_POINT(20, j);
       ok = ok && mbar_wait(&s_full[sb], par2, status, SPECQ_STATUS_TIMEOUT_MMA);
       // P buffer sb is free once PV(j-2) has read it
       if (j >= 2) ok = ok && mbar_wait(&pv_done[sb], par2 ^ 1u, status, SPECQ_STATUS_TIMEOUT_MMA);
       tc_fence_after();
       if (t == 0) SPECQ_TRACE_POINT(21, j);
-      const uint32_t s_addr = lane_base + sb * cs + col0;
-      uint8_t* prow = pop + sb * (NQ * 256) + (tl >> 6) * (NQ * 128) + (tl & 7) * 2;
-      const uint32_t tch = static_cast<uint32_t>((tl & 63) >> 3);
+      const uint32_t s_addr = lane_base + sb * cs2 + col0;
+      uint8_t* prow = pop + sb * kAttnPTile;   // P[token][query], MN-major, 128B-swizzled rows
+      // every token of the block is visible to every query row: no column mask
+      const int t_last = t_begin + j * 128 + 127;
+      const bool interior = t_last < t_end && t_last <= qpos0;
 
+      // scaled score of query column q: (256 * hi + lo) * qs[q] * ks_t * log2e / sqrt(D)
+      auto score = [&](uint32_t hb, uint32_t lb, int q) {
+        return (fmaf(__uint_as_float(hb), 256.f, __uint_as_float(lb)) - kScoreBias257) * (qs_s[q] * c_t);
+      };
+      const float2 c2 = make_float2(c_t, c_t);
       // one optimistic pass: P against the current max, noting whether any score exceeds it
       // by more than 2^8 (then the block is redone below with a raised max)
       auto write_p = [&](float& xmax) {
-        // every TMEM load of the pass is issued before a single wait (one round trip)
-        uint32_t r[32];
+        for (int c0 = 0; c0 < nqh; c0 += 16) {   // 16 columns per TMEM round trip (hi and lo)
+          uint32_t rh[16], rl[16];
+          const bool two = c0 + 8 < nqh;
+          if (t == 0 && c0 == 0) SPECQ_TRACE_POINT(23, j);
+          tmem_ld8(s_addr + c0, *reinterpret_cast<uint32_t(*)[8]>(rh));
+          tmem_ld8(s_addr + NQ + c0, *reinterpret_cast<uint32_t(*)[8]>(rl));
+          if (two) {
+            tmem_ld8(s_addr + c0 + 8, *reinterpret_cast<uint32_t(*)[8]>(rh + 8));
+            tmem_ld8(s_addr + NQ + c0 + 8, *reinterpret_cast<uint32_t(*)[8]>(rl + 8));
+          }
+          tmem_wait_ld();
+          if (t == 0 && c0 == 0) SPECQ_TRACE_POINT(25, j);
 #pragma unroll
-        for (int c0 = 0; c0 < 32; c0 += 8)
-          if (c0 < nqh) tmem_ld8(s_addr + c0, *reinterpret_cast<uint32_t(*)[8]>(r + c0));
-        tmem_wait_ld();
+          for (int h = 0; h < 2; ++h) {
+            if (h == 1 && !two) break;
+            const int qb = col0 + c0 + 8 * h;
+            const float4 qs0 = *reinterpret_cast<const float4*>(qs_s + qb);
+            const float4 qs1 = *reinterpret_cast<const float4*>(qs_s + qb + 4);
+            const float4 n0 = *reinterpret_cast<const float4*>(nm_s + qb);
+            const float4 n1 = *reinterpret_cast<const float4*>(nm_s + qb + 4);
+            const float2 qsv[4] = {make_float2(qs0.x, qs0.y), make_float2(qs0.z, qs0.w), make_float2(qs1.x, qs1.y),
+                                   make_float2(qs1.z, qs1.w)};
+            const float2 nmv[4] = {make_float2(n0.x, n0.y), make_float2(n0.z, n0.w), make_float2(n1.x, n1.y),
+                                   make_float2(n1.z, n1.w)};
+            uint32_t pk[4];
 #pragma unroll
-        for (int c0 = 0; c0 < 32; c0 += 8) {
-          if (c0 < nqh) {
-            const float4* mv = reinterpret_cast<const float4*>(m_s + col0 + c0);
-            const float4 m0 = mv[0], m1 = mv[1];
-            const float mq[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int q = col0 + c0 + i;
-              const bool valid = q >= q_first && q < q_stop;
-              const float x = __uint_as_float(r[c0 + i]) * c_t - mq[i];
-              xmax = valid ? fmaxf(xmax, x) : xmax;
-              const float pr = valid ? fast_exp2(x) : 0.f;
-              *reinterpret_cast<__half*>(prow + q * 128 + ((tch ^ (static_cast<uint32_t>(q) & 7u)) << 4)) =
-                  __float2half_rn(pr);
+            for (int i = 0; i < 8; i += 2) {
+              const int r0 = 8 * h + i;
+              const float2 hb = make_float2(__uint_as_float(rh[r0]), __uint_as_float(rh[r0 + 1]));
+              const float2 lb = make_float2(__uint_as_float(rl[r0]), __uint_as_float(rl[r0 + 1]));
+              const float2 sv = fadd2(ffma2(hb, make_float2(256.f, 256.f), lb),
+                                      make_float2(-kScoreBias257, -kScoreBias257));
+              float2 x = ffma2(sv, fmul2(qsv[i >> 1], c2), nmv[i >> 1]);
+              if (!interior) {   // causal window and split end; padding rows
+                const uint32_t span = static_cast<uint32_t>(q_stop - q_first);
+                x.x = static_cast<uint32_t>(qb + i - q_first) < span ? x.x : -INFINITY;
+                x.y = static_cast<uint32_t>(qb + i + 1 - q_first) < span ? x.y : -INFINITY;
+              }
+              xmax = fmax3(xmax, x.x, x.y);
+              const __half2 ph = __floats2half2_rn(fast_exp2(x.x), fast_exp2(x.y));
+              pk[i >> 1] = *reinterpret_cast<const uint32_t*>(&ph);
             }
+            *reinterpret_cast<uint4*>(prow + sw128_offset(static_cast<uint32_t>(tl), static_cast<uint32_t>(qb >> 3))) =
+                make_uint4(pk[0], pk[1], pk[2], pk[3]);
           }
         }
       };
@@ -353,13 +489,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tc_fence_after();
         // block max per query column: warp shuffles, then across the four lane quadrants
         for (int c0 = 0; c0 < nqh; c0 += 8) {
-          uint32_t r[8];
-          tmem_ld8(s_addr + c0, r);
+          uint32_t rh[8], rl[8];
+          tmem_ld8(s_addr + c0, rh);
+          tmem_ld8(s_addr + NQ + c0, rl);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const int q = col0 + c0 + i;
-            float y = (q >= q_first && q < q_stop) ? __uint_as_float(r[i]) * c_t : -INFINITY;
+            float y = (q >= q_first && q < q_stop) ? score(rh[i], rl[i], q) : -INFINITY;
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) y = fmaxf(y, __shfl_xor_sync(0xffffffffu, y, o));
             if (lane == 0) wmax[quad * 64 + q] = y;
@@ -372,6 +509,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const float mn = fmaxf(mo, mb);
           alpha_s[t] = (mn == -INFINITY) ? 1.f : fast_exp2(mo - mn);   // exp2(-inf) = 0
           m_s[t] = mn;
+          nm_s[t] = -mn;
         }
         named_barrier_sync(3, 256);
         if (j > 0) {   // rescale this group's columns of O^T (all lanes) and of the normaliser row
@@ -395,6 +533,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         float unused = -INFINITY;
         write_p(unused);
       }
+      rebias(sb);            // the next QK into this buffer accumulates onto the bias
+      tmem_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
@@ -410,6 +550,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const int jl = nblk - 1;
       ok = mbar_wait(&pv_done[jl & 1], static_cast<uint32_t>(jl >> 1) & 1u, status, SPECQ_STATUS_TIMEOUT_MMA) && ok;
       tc_fence_after();
+      if (t == 0) SPECQ_TRACE_POINT(60, 0);
       if (quad == 0) {
         for (int c0 = 0; c0 < nqh; c0 += 8) {
           uint32_t r[8];
@@ -423,200 +564,216 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
     }
     named_barrier_sync(3, 256);
-  } else if (warp == 8) {
-    // =================================== TMA producer ===================================
-    if (elect_one()) {
-      const uint64_t pol = policy_evict_first();
-      const int nbox = 128 / p.box_rows;
-      // page ids of the next block are loaded into registers one block ahead (independent
-      // loads, all in flight together), so the block-table latency overlaps the ring wait
-      int pgv[16];
-      auto load_pages = [&](int j) {
-        const int tok0 = t_begin + j * 128;
-        const int nb = (min(tok0 + 128, t_end) - tok0 + p.box_rows - 1) / p.box_rows;
+  } else if (warp < kAttnMmaWarp) {
+    // =================================== K/V gather ===================================
+    // 16-byte cp.async copies through the block table; gather warp lw owns token rows
+    // [64 lw, 64 lw + 64) of every block.  Lane l looks up the pages of rows l and l + 32 of
+    // that range two blocks ahead (the loads land while a block is issued); the copies go 8
+    // lanes per token row (lane l copies chunk l % 8), so every warp instruction moves four
+    // whole 128-byte rows.  K lands in the 128B-swizzled layout the tensor core reads; rows
+    // past the split end or on an invalid page are zero-filled.
+    const int lw = static_cast<int>(warp) - 8;
+    const int l = static_cast<int>(lane);
+    const int ch = l & 7;
+    const int8_t* kc = p.kc + ch * 16;
+    const int8_t* vc = p.vc + ch * 16;
+    auto load_pages = [&](int j, int (&pg)[2]) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          pgv[i] = (i < nb) ? __ldg(p.bt + b * p.bt_sb + (tok0 + i * p.box_rows) / p.page) : -1;
-      };
-      int issued = 0;
-      if (nblk > 0) load_pages(0);
-      for (int j = 0; j < nblk; ++j) {
-        const int s = j % p.stages;
-        if (!mbar_wait(&stage_empty[s], (static_cast<uint32_t>(j / p.stages) & 1u) ^ 1u, status,
-                       SPECQ_STATUS_TIMEOUT_PIPELINE)) {
-          ok = false;
-          break;
-        }
-        const int tok0 = t_begin + j * 128;
-        const int nb = (min(tok0 + 128, t_end) - tok0 + p.box_rows - 1) / p.box_rows;
-        int* pg = pgs + s * 128;
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          if (i < nbox) pg[i] = pgv[i];
-        for (int i = 16; i < nbox; ++i)      // page sizes below 8 tokens: more than 16 boxes
-          pg[i] = (i < nb) ? __ldg(p.bt + b * p.bt_sb + (tok0 + i * p.box_rows) / p.page) : -1;
-        SPECQ_TRACE_POINT(50, j);
-        mbar_arrive_expect_tx(&stage_full[s], static_cast<uint32_t>(nb * p.box_rows * 128 * 2));
-        uint8_t* kdst = ring + s * kAttnStage;
-        uint8_t* vdst = kdst + kAttnKV8;
-        for (int i = 0; i < nb; ++i) {
-          const int tok = tok0 + i * p.box_rows;
-          const int off = tok % p.page;
-          tma_load_4d(kdst + i * p.box_rows * 128, &tmap_k, &stage_full[s], 0, kvh, off, pg[i], pol);
-          tma_load_4d(vdst + i * p.box_rows * 128, &tmap_v, &stage_full[s], 0, kvh, off, pg[i], pol);
-        }
-        SPECQ_TRACE_POINT(51, j);
-        ++issued;
-        if (j + 1 < nblk) load_pages(j + 1);
+      for (int rr = 0; rr < 2; ++rr) {
+        const int tok = t_begin + j * 128 + 64 * lw + 32 * rr + l;
+        pg[rr] = (j < nblk && tok < t_end) ? __ldg(p.bt + b * p.bt_sb + page_of(tok)) : -1;
       }
-      if (!ok) {
-        for (int j = max(0, issued - p.stages); j < issued; ++j)
-          mbar_wait(&stage_full[j % p.stages], static_cast<uint32_t>(j / p.stages) & 1u, status,
-                    SPECQ_STATUS_TIMEOUT_PIPELINE);
+    };
+    int64_t src_off[2];   // byte offset of the token row, -1 when there is nothing to read
+    auto offsets = [&](int j, const int (&pg)[2]) {
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int tok = t_begin + j * 128 + 64 * lw + 32 * rr + l;
+        src_off[rr] = (pg[rr] >= 0 && pg[rr] < p.n_pages)
+                          ? static_cast<int64_t>(pg[rr]) * p.kv_sp + static_cast<int64_t>(slot_of(tok)) * p.kv_so +
+                                static_cast<int64_t>(kvh) * p.kv_sh
+                          : int64_t(-1);
+      }
+    };
+    // per-token scales of the rows this lane looks up, loaded one block ahead
+    float ksr[2], vsr[2];
+    auto scales = [&](int j, const int (&pg)[2]) {
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        ksr[rr] = 0.f;
+        vsr[rr] = 0.f;
+        if (pg[rr] >= 0 && pg[rr] < p.n_pages) {
+          const int tok = t_begin + j * 128 + 64 * lw + 32 * rr + l;
+          const int64_t idx = static_cast<int64_t>(pg[rr]) * p.s_sp + static_cast<int64_t>(slot_of(tok)) * p.s_so +
+                              static_cast<int64_t>(kvh) * p.s_sh;
+          ksr[rr] = load_scale(p.ks, p.scale_f32, idx);
+          vsr[rr] = load_scale(p.vs, p.scale_f32, idx);
+        }
+      }
+    };
+    int pg_cur[2], pg_next[2];
+    load_pages(0, pg_cur);
+    load_pages(1, pg_next);
+    offsets(0, pg_cur);
+    scales(0, pg_cur);
+    int s = 0;
+    uint32_t phase = 0;
+    for (int j = 0; j < nblk; ++j) {
+      int pg_after[2];
+      load_pages(j + 2, pg_after);
+      if (!mbar_wait(&stage_empty[s], phase ^ 1u, status, SPECQ_STATUS_TIMEOUT_PIPELINE)) {
+        ok = false;
+        break;
+      }
+      if (lw == 0) SPECQ_TRACE_POINT(50, j);
+      const uint32_t kst = smem_u32(ring + s * kAttnStage);
+      const uint32_t vst = kst + kAttnKV8;
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int src_lane = 4 * i + (l >> 3);
+          const int row = 64 * lw + 32 * rr + src_lane;
+          const int64_t off = __shfl_sync(0xffffffffu, src_off[rr], src_lane);
+          const uint32_t sz = off >= 0 ? 16u : 0u;
+          const int64_t o = off >= 0 ? off : 0;
+          cp_async16(kst + sw128_offset(static_cast<uint32_t>(row), static_cast<uint32_t>(ch)), kc + o, sz);
+          cp_async16(vst + static_cast<uint32_t>(row * 128 + ch * 16), vc + o, sz);
+        }
+      }
+      cp_async_mbar_arrive(&stage_full[s]);
+      {   // the scales: K scale with log2(e) / sqrt(D) folded in, V scale in fp16 (exact for
+          // fp16 scales, one rounding for fp32 ones) for the fp16 multiply of the V warps
+        float* ksc = reinterpret_cast<float*>(ring + s * kAttnStage + kAttnScl);
+        __half* vsc = reinterpret_cast<__half*>(ksc + 128);
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          ksc[64 * lw + 32 * rr + l] = ksr[rr] * p.sm_scale_log2;
+          vsc[64 * lw + 32 * rr + l] = __float2half_rn(vsr[rr]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&stage_full[s]);   // release: the scales are visible
+      }
+      if (lw == 0) SPECQ_TRACE_POINT(51, j);
+      offsets(j + 1, pg_next);
+      scales(j + 1, pg_next);
+      pg_next[0] = pg_after[0];
+      pg_next[1] = pg_after[1];
+      if (++s == kAttnStages) {
+        s = 0;
+        phase ^= 1u;
       }
     }
-  } else if (warp == 9) {
+    // copies in flight must land before the CTA can exit
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  } else if (warp == kAttnMmaWarp) {
     // =================================== MMA issuer ===================================
     if (elect_one()) {
-      const uint32_t id_qk = idesc_f16(128, static_cast<uint32_t>(NQ));
-      const uint32_t id_pv = idesc_f16(128, static_cast<uint32_t>(NQ), 1u, 0u);   // A (V^T) MN-major
-      const uint32_t kop_a = smem_u32(kop), vop_a = smem_u32(vop), qop_a = smem_u32(qop), pop_a = smem_u32(pop);
-      const uint32_t half_q = static_cast<uint32_t>(NQ) * 128u;
+      const uint32_t id_qk = idesc_i8(128, static_cast<uint32_t>(2 * NQ));       // hi and lo columns
+      // V^T (A) and P (B) both MN-major
+      const uint32_t id_pv = idesc_f16(128, static_cast<uint32_t>(NQ), 1u, 1u);
+      const uint32_t id_l = idesc_f16(128, static_cast<uint32_t>(NQ), 0u, 1u);
+      const uint32_t ring_a = smem_u32(ring), vop_a = smem_u32(vop), qop_a = smem_u32(qop), pop_a = smem_u32(pop);
+      auto issue_qk = [&](int j, int s) {
+        const uint32_t sb = static_cast<uint32_t>(j & 1);
+        fence_proxy_async_smem();   // the K bytes were written by cp.async (generic proxy)
+        tc_fence_after();
+        SPECQ_TRACE_POINT(30, j);
+        const uint32_t ka = ring_a + static_cast<uint32_t>(s) * kAttnStage;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {   // 32 of the 128 head dims per step
+          const uint64_t ak = sdesc_sw128(ka + k * 32u, 16u, 1024u);
+          const uint64_t bq = sdesc_sw128(qop_a + k * 32u, 16u, 1024u);
+          umma_i8_ss(tmem + sb * cs2, ak, bq, id_qk, 1u);   // onto the bias the softmax left
+        }
+        umma_commit(&s_full[sb]);
+        umma_commit(&stage_empty[s]);   // the K half of the stage is consumed
+        SPECQ_TRACE_POINT(31, j);
+      };
       auto issue_pv = [&](int i) {
         const uint32_t bi = static_cast<uint32_t>(i & 1);
         tc_fence_after();
         SPECQ_TRACE_POINT(32, i);
         const uint32_t vb = vop_a + bi * kAttnOp;
-        const uint32_t pb = pop_a + bi * (2u * half_q);
+        const uint32_t pb = pop_a + bi * kAttnPTile;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {   // 16 tokens per step
           const uint64_t av = sdesc_sw128(vb + k * 2048u, 16384u, 1024u);
-          const uint64_t bp = sdesc_sw128(pb + (k >> 2) * half_q + (k & 3) * 32u, 16u, 1024u);
+          const uint64_t bp = sdesc_sw128(pb + k * 2048u, 16384u, 1024u);
           const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
           umma_f16_ss(tmem + O_col, av, bp, id_pv, acc);
-          umma_f16_ts(tmem + L_col, tmem + ONES_col + 8u * k, bp, id_qk, acc);
+          umma_f16_ts(tmem + L_col, tmem + ONES_col + 8u * k, bp, id_l, acc);
         }
         umma_commit(&pv_done[bi]);
         SPECQ_TRACE_POINT(33, i);
       };
-      auto issue_qk = [&](int j) {
-        const uint32_t sb = static_cast<uint32_t>(j & 1);
-        tc_fence_after();
-        SPECQ_TRACE_POINT(30, j);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {   // 16 of the 128 head dims per step
-          const uint64_t ak = sdesc_sw128(kop_a + (k >> 2) * 16384u + (k & 3) * 32u, 16u, 1024u);
-          const uint64_t bq = sdesc_sw128(qop_a + (k >> 2) * half_q + (k & 3) * 32u, 16u, 1024u);
-          umma_f16_ss(tmem + sb * cs, ak, bq, id_qk, k > 0 ? 1u : 0u);
+      // Fixed issue order QK(0), QK(1), then per block i: QK(i+2), PV(i).  Both wait for the
+      // softmax to finish block i (its S buffer, its P tile), so neither delays the other; the
+      // blocking waits keep this thread off the issue slots the softmax warps need.
+      int qk_stage = 0;
+      uint32_t qk_phase = 0;
+      auto qk = [&](int j) {
+        if (!mbar_wait(&stage_full[qk_stage], qk_phase, status, SPECQ_STATUS_TIMEOUT_PIPELINE)) return false;
+        if (!mbar_wait(&s_empty[j & 1], (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u, status, SPECQ_STATUS_TIMEOUT_MMA))
+          return false;
+        issue_qk(j, qk_stage);
+        if (++qk_stage == kAttnStages) {
+          qk_stage = 0;
+          qk_phase ^= 1u;
         }
-        umma_commit(&s_full[sb]);
-        SPECQ_TRACE_POINT(31, j);
+        return true;
       };
       if (nblk > 0) ok = mbar_wait(q_full, 0u, status, SPECQ_STATUS_TIMEOUT_PIPELINE);
-      // Event loop: QK(j) and PV(j) use disjoint TMEM, so each is issued as soon as its own
-      // inputs are ready (PV(j) never waits behind the conversion of the next K tile).
-      int nqk = 0, npv = 0;
-      uint64_t idle_since = 0;
-      while (ok && npv < nblk) {
-        bool progressed = false;
-        if (nqk < nblk && mbar_test_wait(k_full, static_cast<uint32_t>(nqk) & 1u) &&
-            mbar_test_wait(&s_empty[nqk & 1], (static_cast<uint32_t>(nqk >> 1) & 1u) ^ 1u)) {
-          issue_qk(nqk++);
-          progressed = true;
-        }
-        if (npv < nqk) {
-          const uint32_t bi = static_cast<uint32_t>(npv & 1);
-          const uint32_t par = static_cast<uint32_t>(npv >> 1) & 1u;
-          if (mbar_test_wait(&p_full[bi], par) && mbar_test_wait(&v_full[bi], par)) {
-            issue_pv(npv++);
-            progressed = true;
-          }
-        }
-        if (progressed) {
-          idle_since = 0;
-        } else if (idle_since == 0) {
-          idle_since = globaltimer_ns();
-        } else if (globaltimer_ns() - idle_since > kWaitLimitNs) {
-          report_status(status, SPECQ_STATUS_TIMEOUT_PIPELINE);
-          ok = false;
-        }
+      for (int j = 0; ok && j < min(2, nblk); ++j) ok = qk(j);
+      for (int i = 0; ok && i < nblk; ++i) {
+        if (i + 2 < nblk) ok = qk(i + 2);
+        const uint32_t bi = static_cast<uint32_t>(i & 1);
+        const uint32_t par = static_cast<uint32_t>(i >> 1) & 1u;
+        ok = ok && mbar_wait(&p_full[bi], par, status, SPECQ_STATUS_TIMEOUT_MMA) &&
+             mbar_wait(&v_full[bi], par, status, SPECQ_STATUS_TIMEOUT_PIPELINE);
+        if (ok) issue_pv(i);
       }
     }
   } else {
-    // =================================== converters ===================================
-    const int c = static_cast<int>(threadIdx.x) - 320;   // 0..kAttnConvThreads-1
-    float ks_cur = 0.f, vs_cur = 0.f;
-    auto fetch_scales = [&](int j, float& ksv, float& vsv) -> bool {
-      ksv = 0.f;
-      vsv = 0.f;
-      const int s = j % p.stages;
-      if (!mbar_wait(&stage_full[s], static_cast<uint32_t>(j / p.stages) & 1u, status, SPECQ_STATUS_TIMEOUT_PIPELINE))
-        return false;
-      if (c < 128) {
-        const int tok = t_begin + j * 128 + c;
-        const int page = pgs[s * 128 + c / p.box_rows];
-        if (tok < t_end && page >= 0 && page < p.n_pages) {
-          const int64_t idx = static_cast<int64_t>(page) * p.s_sp + static_cast<int64_t>(tok % p.page) * p.s_so +
-                              static_cast<int64_t>(kvh) * p.s_sh;
-          ksv = load_scale(p.ks, p.scale_f32, idx);
-          vsv = load_scale(p.vs, p.scale_f32, idx);
-        }
-      }
-      return true;
-    };
-    if (nblk > 0) ok = fetch_scales(0, ks_cur, vs_cur);
+    // =================================== V warps ===================================
+    const int c = static_cast<int>(threadIdx.x) - 32 * (kAttnMmaWarp + 1);   // 0..kAttnConvThreads-1
     for (int j = 0; j < nblk; ++j) {
-      const int s = j % p.stages;
+      const int s = j % kAttnStages;
       const uint32_t sb = static_cast<uint32_t>(j & 1);
       const uint32_t par2 = static_cast<uint32_t>(j >> 1) & 1u;
-      if (c == 0) SPECQ_TRACE_POINT(40, j);
-      const uint8_t* k8 = ring + s * kAttnStage;
-      const uint8_t* v8 = k8 + kAttnKV8;
-      // ---- K: the single fp16 K tile is free once QK(j-1) has completed
-      if (j > 0)
-        ok = ok && mbar_wait(&s_full[sb ^ 1u], static_cast<uint32_t>((j - 1) >> 1) & 1u, status,
-                             SPECQ_STATUS_TIMEOUT_MMA);
-      // 1024 16-byte chunks per tile: (token row = idx / 8, chunk = idx % 8)
-      for (int idx = c; idx < 1024; idx += kAttnConvThreads) {
-        const int row = idx >> 3;
-        const int ch = idx & 7;
-        const uint4 v = *reinterpret_cast<const uint4*>(k8 + row * 128 + ch * 16);
-        uint32_t h[8];
-        i8x16_to_f16(v, h);
-        store_f16_chunk_pair(kop, row, ch, h);
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(k_full);
-      if (c == 0) SPECQ_TRACE_POINT(42, j);
-      // ---- per-token scales of this block
-      ok = ok && mbar_wait(&scl_empty[sb], par2 ^ 1u, status, SPECQ_STATUS_TIMEOUT_PIPELINE);
-      if (c < 128) {
-        scl_c[sb * 128 + c] = ks_cur * p.sm_scale_log2;
-        scl_vh[sb * 128 + c] = __float2half_rn(vs_cur);
-      }
-      named_barrier_sync(1, kAttnConvThreads);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&scl_full[sb]);
-      if (c == 0) SPECQ_TRACE_POINT(43, j);
       // ---- V (scale folded in) into buffer sb, free once PV(j-2) has completed
+      ok = ok && mbar_wait(&stage_full[s], static_cast<uint32_t>(j / kAttnStages) & 1u, status,
+                           SPECQ_STATUS_TIMEOUT_PIPELINE);
+      if (c == 0) SPECQ_TRACE_POINT(40, j);
       if (j >= 2) ok = ok && mbar_wait(&pv_done[sb], par2 ^ 1u, status, SPECQ_STATUS_TIMEOUT_MMA);
+      const uint8_t* v8 = ring + s * kAttnStage + kAttnKV8;
+      const __half* vsc = reinterpret_cast<const __half*>(ring + s * kAttnStage + kAttnScl + 512);
       uint8_t* vdst = vop + sb * kAttnOp;
-      for (int idx = c; idx < 1024; idx += kAttnConvThreads) {
-        const int row = idx >> 3;
-        const int ch = idx & 7;
-        const uint4 v = *reinterpret_cast<const uint4*>(v8 + row * 128 + ch * 16);
-        uint32_t h[8];
-        i8x16_to_f16(v, h);
-        // the token's V scale in fp16 (exact for fp16 scales; one rounding for fp32 scales), so
-        // the per-element multiply stays on the fp16 pipe
-        const __half2 s2 = __half2half2(scl_vh[sb * 128 + row]);
+      constexpr int kPer = (1024 + kAttnConvThreads - 1) / kAttnConvThreads;
+      uint4 raw[kPer];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          __half2 o = __hmul2(*reinterpret_cast<__half2*>(&h[i]), s2);
-          h[i] = *reinterpret_cast<uint32_t*>(&o);
+      for (int k = 0; k < kPer; ++k) {   // all loads first, then convert and store
+        const int idx = c + k * kAttnConvThreads;
+        if (idx < 1024) raw[k] = *reinterpret_cast<const uint4*>(v8 + idx * 16);
+      }
+#pragma unroll
+      for (int k = 0; k < kPer; ++k) {
+        const int idx = c + k * kAttnConvThreads;
+        if (idx < 1024) {
+          const int row = idx >> 3;
+          const int ch = idx & 7;
+          uint32_t h[8];
+          i8x16_to_f16(raw[k], h);
+          // the token's V scale in fp16 (exact for fp16 scales; one rounding for fp32 scales),
+          // so the per-element multiply stays on the fp16 pipe
+          const __half2 s2 = __half2half2(vsc[row]);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            __half2 o = __hmul2(*reinterpret_cast<__half2*>(&h[i]), s2);
+            h[i] = *reinterpret_cast<uint32_t*>(&o);
+          }
+          store_f16_chunk_pair(vdst, row, ch, h);
         }
-        store_f16_chunk_pair(vdst, row, ch, h);
       }
       fence_proxy_async_smem();
       __syncwarp();
@@ -625,7 +782,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         mbar_arrive(&stage_empty[s]);
       }
       if (c == 0) SPECQ_TRACE_POINT(45, j);
-      if (j + 1 < nblk) ok = (ok && fetch_scales(j + 1, ks_cur, vs_cur)) && ok;
     }
   }
   __syncwarp();
@@ -652,8 +808,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int i = 0; i < 8; ++i) {
           const int q = col0 + c0 + i;
           if (q < rows_valid) {
-            const int qi = q_lo + q / p.g;
-            const int head = kvh * p.g + q % p.g;
+            const int qi = q_lo + (p.g_shift >= 0 ? (q >> p.g_shift) : (q / p.g));
+            const int head = kvh * p.g + (p.g_shift >= 0 ? (q & (p.g - 1)) : (q % p.g));
             const float l = l_s[q];
             const float o = __uint_as_float(r[i]) / (l == 0.f ? 1.f : l);
             p.out[b * p.o_sb + static_cast<int64_t>(qi) * p.o_st + static_cast<int64_t>(head) * p.o_sh + tl] =
@@ -663,8 +819,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
     }
   } else {
-    float* comb = reinterpret_cast<float*>(ring);   // [NQ][128] partial O (ring is idle now)
+    // Split combine, push model.  CTA r of the cluster owns head dims [r*dr, (r+1)*dr); every
+    // CTA stores its partial O^T for those dims, and its (m, l), straight into CTA r's shared
+    // memory (fire-and-forget st.shared::cluster), then each CTA combines its own dims
+    // locally.  The first cluster barrier makes sure every ring is idle before it is written.
+    const int S = p.splits;
+    const int lgdr = 7 - (31 - __clz(S));   // head dims per rank: 128 / S
+    const int dr = 1 << lgdr;
+    float* comb = reinterpret_cast<float*>(ring);   // [S][NQ][dr] partial O of every split
+    float* mlb = comb + NQ * 128;                   // [S][NQ] (m, l) of every split
+    float* wts = mlb + S * NQ * 2;                  // [S][NQ] combine weights
+    if (threadIdx.x == 0) SPECQ_TRACE_POINT(61, 0);
+    cluster_sync();
+    if (threadIdx.x == 0) SPECQ_TRACE_POINT(62, 0);
     if (soft) {
+      const uint32_t dst = dsmem_map(smem_u32(comb), static_cast<uint32_t>(tl >> lgdr)) +
+                           4u * static_cast<uint32_t>(split * NQ * dr + (tl & (dr - 1)));
       for (int c0 = 0; c0 < (NQ >> 1); c0 += 8) {
         uint32_t r[8];
         if (nblk > 0 && ok) {
@@ -675,56 +845,92 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           for (int i = 0; i < 8; ++i) r[i] = 0u;
         }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) comb[(col0 + c0 + i) * 128 + tl] = __uint_as_float(r[i]);
+        for (int i = 0; i < 8; ++i) dsmem_st_f32(dst + 4u * static_cast<uint32_t>((col0 + c0 + i) * dr), __uint_as_float(r[i]));
       }
-      if (nblk == 0 && t < 64) { m_s[t] = -INFINITY; l_s[t] = 0.f; }
+      if (t < NQ) {
+        const float mv = nblk > 0 ? m_s[t] : -INFINITY;
+        const float lv = nblk > 0 ? l_s[t] : 0.f;
+        const uint32_t ml = smem_u32(mlb + 2 * (split * NQ + t));
+        for (int pr = 0; pr < S; ++pr) dsmem_st_v2f32(dsmem_map(ml, static_cast<uint32_t>(pr)), mv, lv);
+      }
     }
-    cluster_sync();
-    if (soft) {
-      const int S = p.splits;
-      const int lgdr = 7 - (31 - __clz(S));   // d columns per rank: 128 / S
-      const int dr = 1 << lgdr;
-      const int d0 = split * dr;
-      for (int item = t; item < rows_valid * dr; item += 256) {
-        const int q = item >> lgdr;
-        const int d = d0 + (item & (dr - 1));
-        float mp[8], lp[8], op[8];
-#pragma unroll
-        for (int pr = 0; pr < 8; ++pr) {     // every peer's loads in flight together
-          if (pr < S) {
-            mp[pr] = *dsmem_ptr(m_s + q, static_cast<uint32_t>(pr));
-            lp[pr] = *dsmem_ptr(l_s + q, static_cast<uint32_t>(pr));
-            op[pr] = *dsmem_ptr(comb + q * 128 + d, static_cast<uint32_t>(pr));
-          }
-        }
+    if (threadIdx.x == 0) SPECQ_TRACE_POINT(63, 0);
+    cluster_sync();   // every partial has landed; nothing remote is touched after this
+    if (threadIdx.x == 0) SPECQ_TRACE_POINT(63, 1);
+    // The combine with the split count as a compile-time constant: every loop over the splits
+    // unrolls, so each thread's loads are all in flight at once.
+    auto combine = [&](auto s_const) {
+      constexpr int kS = decltype(s_const)::value;
+      if (t < rows_valid) {   // weights of the kS partials of query row t, in fixed split order
+        float mp[kS], w[kS];
         float mmax = -INFINITY;
 #pragma unroll
-        for (int pr = 0; pr < 8; ++pr)
-          if (pr < S) mmax = fmaxf(mmax, mp[pr]);
-        float lsum = 0.f, osum = 0.f;
+        for (int pr = 0; pr < kS; ++pr) {
+          mp[pr] = mlb[2 * (pr * NQ + t)];
+          mmax = fmaxf(mmax, mp[pr]);
+        }
+        float lsum = 0.f;
 #pragma unroll
-        for (int pr = 0; pr < 8; ++pr) {     // fixed order: identical bits for any schedule
-          if (pr < S) {
-            const float w = (mp[pr] == -INFINITY) ? 0.f : fast_exp2(mp[pr] - mmax);
-            lsum += w * lp[pr];
-            osum += w * op[pr];
+        for (int pr = 0; pr < kS; ++pr) {
+          w[pr] = (mp[pr] == -INFINITY) ? 0.f : fast_exp2(mp[pr] - mmax);
+          lsum = fmaf(w[pr], mlb[2 * (pr * NQ + t) + 1], lsum);
+        }
+        const float inv = lsum == 0.f ? 1.f : __frcp_rn(lsum);
+#pragma unroll
+        for (int pr = 0; pr < kS; ++pr) wts[pr * NQ + t] = w[pr] * inv;
+      }
+      named_barrier_sync(3, 256);
+      if (t == 0) SPECQ_TRACE_POINT(63, 2);
+      if (!ok) return;
+      // one item = 8 consecutive head dims of one query row
+      constexpr int kG8 = 128 / kS / 8;
+      for (int item = t; item < rows_valid * kG8; item += 256) {
+        const int q = item / kG8;
+        const int d8 = item % kG8;
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll
+        for (int pr = 0; pr < kS; ++pr) {
+          const float wq = wts[pr * NQ + q];
+          const float4* src = reinterpret_cast<const float4*>(comb + (pr * NQ + q) * (128 / kS) + 8 * d8);
+          const float4 u = src[0], v = src[1];
+          acc[0] = fmaf(wq, u.x, acc[0]); acc[1] = fmaf(wq, u.y, acc[1]);
+          acc[2] = fmaf(wq, u.z, acc[2]); acc[3] = fmaf(wq, u.w, acc[3]);
+          acc[4] = fmaf(wq, v.x, acc[4]); acc[5] = fmaf(wq, v.y, acc[5]);
+          acc[6] = fmaf(wq, v.z, acc[6]); acc[7] = fmaf(wq, v.w, acc[7]);
+        }
+        const int qi = q_lo + (p.g_shift >= 0 ? (q >> p.g_shift) : (q / p.g));
+        const int head = kvh * p.g + (p.g_shift >= 0 ? (q & (p.g - 1)) : (q % p.g));
+        __half* dst = p.out + b * p.o_sb + static_cast<int64_t>(qi) * p.o_st + static_cast<int64_t>(head) * p.o_sh +
+                      split * (128 / kS) + 8 * d8;
+        __half2 h[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(acc[2 * i], acc[2 * i + 1]);
+        if (p.out_vec) {
+          *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(h);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            dst[2 * i] = __low2half(h[i]);
+            dst[2 * i + 1] = __high2half(h[i]);
           }
         }
-        if (ok) {
-          const int qi = q_lo + q / p.g;
-          const int head = kvh * p.g + q % p.g;
-          p.out[b * p.o_sb + static_cast<int64_t>(qi) * p.o_st + static_cast<int64_t>(head) * p.o_sh + d] =
-              __float2half_rn(osum / (lsum == 0.f ? 1.f : lsum));
-        }
       }
+    };
+    if (soft) {
+      if (S == 2) combine(std::integral_constant<int, 2>{});
+      else if (S == 4) combine(std::integral_constant<int, 4>{});
+      else combine(std::integral_constant<int, 8>{});
+      if (t == 0) SPECQ_TRACE_POINT(63, 3);
     }
-    cluster_sync();
   }
+  if (threadIdx.x == 256) SPECQ_TRACE_POINT(63, 4);
 
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) SPECQ_TRACE_POINT(9, 0);
-  if (warp == 9) {
+  if (warp == kAttnMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, p.tmem_cols);
   }
@@ -780,37 +986,35 @@ inline int run_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_
   p.n_pages = n_pages;
   p.b_grid = b_grid; p.n_seqs = n_seqs; p.q_len = q_len; p.ql_max = ql_max;
   p.h_kv = H_KV; p.g = G; p.page = page;
+  p.kc = kc; p.vc = vc;
+  p.out_vec = aligned(out, 16) && o_sb % 8 == 0 && o_st % 8 == 0 && o_sh % 8 == 0;
+  p.kv_sp = kv_sp; p.kv_so = kv_so; p.kv_sh = kv_sh;
   p.qpp = std::min(qpp, 64 / G);                 // QPP only changes the schedule
   p.nq = round_up(p.qpp * G, 16);
   p.n_qc = ceil_div(ql_grid, p.qpp);
-  int br = 1;
-  while (br < 16 && page % (br * 2) == 0) br *= 2;
-  p.box_rows = br;
+  p.page_shift = ((page & (page - 1)) == 0) ? __builtin_ctz(static_cast<unsigned>(page)) : -1;
+  p.g_shift = ((G & (G - 1)) == 0) ? __builtin_ctz(static_cast<unsigned>(G)) : -1;
   // Split count from the block-table width only (never from B or the plan), so eager and
   // plan-mode launches reduce identical partials.
   const int max_ctx = bt_cols * page;
-  p.splits = std::min(8, std::max(1, ceil_div(max_ctx, 2048)));
-  p.stages = 2;
+  // A power of two (each split owns 128 / splits head dims in the combine).
+  p.splits = std::min(8, next_pow2(std::max(1, ceil_div(max_ctx, 2048))));
+  p.stages = kAttnStages;
   p.sm_scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
-  p.col_stride = static_cast<uint32_t>(round_up(p.nq, 32));
-  p.tmem_cols = static_cast<uint32_t>(next_pow2(static_cast<int>(4 * p.col_stride + 128)));
+  // TMEM: two score buffers (hi and lo int32 columns), O^T, normaliser, 64 columns of ones
+  p.col_stride = static_cast<uint32_t>(round_up(2 * p.nq, 32));
+  p.o_cols = static_cast<uint32_t>(round_up(p.nq, 32));
+  p.tmem_cols = static_cast<uint32_t>(next_pow2(static_cast<int>(2 * p.col_stride + 2 * p.o_cols + 64)));
   if (p.tmem_cols > 512) return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: too many query rows per CTA");
   if (static_cast<int64_t>(b_grid) * p.n_qc > 65535)
     return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: grid too large");
 
-  // ring + fp16 K tile + two fp16 V tiles + Q + two P^T tiles + scales + softmax state + pages
-  const int smem = 1024 + p.stages * static_cast<int>(kAttnStage) + 3 * static_cast<int>(kAttnOp) + 3 * p.nq * 256 +
-                   512 * 4 + 448 * 4 + p.stages * 128 * 4 + (2 * p.stages + 16) * 8 + 64;
+  // ring + two fp16 V tiles + int8 Q (hi, lo) + two P^T tiles + scales/softmax state + barriers
+  const int smem = 1024 + p.stages * static_cast<int>(kAttnStage) + 2 * static_cast<int>(kAttnOp) +
+                   p.nq * 256 + 2 * static_cast<int>(kAttnPTile) + 4096 + (2 * p.stages + 17) * 8 + 16;
   if (smem > 232448) return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: shared memory %d too large", smem);
-  if (p.nq * 128 * 4 > p.stages * static_cast<int>(kAttnStage))
+  if ((p.nq * 128 + 3 * p.splits * p.nq) * 4 > p.stages * static_cast<int>(kAttnStage))
     return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: combine buffer does not fit");
-
-  CUtensorMap tk, tv;
-  const uint64_t dims[4] = {128u, static_cast<uint64_t>(H_KV), static_cast<uint64_t>(page), static_cast<uint64_t>(n_pages)};
-  const uint64_t strides[3] = {static_cast<uint64_t>(kv_sh), static_cast<uint64_t>(kv_so), static_cast<uint64_t>(kv_sp)};
-  const uint32_t box[4] = {128u, 1u, static_cast<uint32_t>(br), 1u};
-  if (int rc = encode_tiled(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, kc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE)) return rc;
-  if (int rc = encode_tiled(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, vc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE)) return rc;
 
   const dim3 grid(static_cast<unsigned>(p.splits), static_cast<unsigned>(H_KV),
                   static_cast<unsigned>(b_grid * p.n_qc));
@@ -827,7 +1031,7 @@ inline int run_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = p.splits > 1 ? 1 : 0;
-  SPECQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, paged_attn_kernel, p, tk, tv));
+  SPECQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, paged_attn_kernel, p));
   LaunchRecord& r = last_launch_ref();
   r.variant = 0;
   r.grid[0] = static_cast<int>(grid.x); r.grid[1] = static_cast<int>(grid.y); r.grid[2] = static_cast<int>(grid.z);

@@ -143,14 +143,21 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 
 // Bounded wait for phase `parity` of `bar`.  Returns false (and records `code` in the status
 // word) when the limit runs out; the caller then abandons its loop.
+// The timer is read once every 16 suspended tries: a waiting warp wakes often, and a timer read
+// on every wake costs the working warps issue slots.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  while (true) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait_sleep(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
-      report_status(status, code);
-      return false;
+    if ((it & 15u) == 0u) {
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitLimitNs) {
+        report_status(status, code);
+        return false;
+      }
     }
   }
 }
@@ -343,6 +350,23 @@ __device__ __forceinline__ uint32_t cluster_nctarank() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Cluster barrier in two halves: arrive early, wait only where the peers' state is needed.
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Atomically add `v` to the u32 at `remote` (a shared::cluster address in a peer CTA) and
+// count 4 bytes on that CTA's mbarrier `remote_bar` (complete_tx); fire-and-forget.
+__device__ __forceinline__ void red_async_add_u32(uint32_t remote, uint32_t v, uint32_t remote_bar) {
+  asm volatile(
+      "red.async.relaxed.cluster.shared::cluster.mbarrier::complete_tx::bytes.add.u32 [%0], %1, [%2];" ::"r"(remote),
+      "r"(v), "r"(remote_bar)
+      : "memory");
+}
+
 // Map a local shared-memory address to the same offset in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t dsmem_map(uint32_t local_saddr, uint32_t rank) {
   uint32_t r;
@@ -370,6 +394,13 @@ __device__ __forceinline__ float dsmem_ld_f32(uint32_t cluster_saddr) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_saddr) : "memory");
   return v;
+}
+
+__device__ __forceinline__ void dsmem_st_f32(uint32_t cluster_saddr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_saddr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void dsmem_st_v2f32(uint32_t cluster_saddr, float a, float b) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(cluster_saddr), "f"(a), "f"(b) : "memory");
 }
 
 // Named barrier for a subset of warps (ids 1..15; 0 is __syncthreads).

@@ -98,7 +98,8 @@ int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int
   p.kb_per_split = ceil_div(p.kb_total, S);
 
   p.stage_bytes = kW8A8WTile + static_cast<uint32_t>(round_up(p.chunk, 16)) * 128u;
-  const uint32_t red_bytes = (S > 1) ? 128u * (static_cast<uint32_t>(p.chunk) * 4u + 16u) : 0u;
+  // split-K partial tile [128][chunk] int32 (padded rows), parked in the idle ring
+  const uint32_t red_bytes = (S > 1) ? 128u * (static_cast<uint32_t>(round_up(p.chunk, 16)) * 4u + 16u) : 0u;
   const int overhead = 1024 + 256 + 384 * 4;   // alignment slack, barriers, staged scales
   int stages = std::min(8, (kSmemLimit - overhead) / static_cast<int>(p.stage_bytes));
   if (stages < 2) return fail(SPECQ_ERR_UNSUPPORTED, "w8a8: token chunk %d does not fit shared memory", p.chunk);
@@ -193,6 +194,7 @@ int run_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const
   p.status = dev->status;
   p.lda = lda; p.ldwp = ldwp; p.ldsc = ldsc; p.ldo = ldo; p.ldo_n = ldo_n;
   p.m_rows = M; p.N = N; p.K = K; p.group = group;
+  p.group_shift = ((group & (group - 1)) == 0) ? __builtin_ctz(static_cast<unsigned>(group)) : -1;
   p.kb_total = K / 128;
   const int n_tiles = ceil_div(N, 128);
   // The split depends on (N, K) only, never on M: plan and non-plan calls reduce the same
@@ -205,15 +207,19 @@ int run_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const
   p.splits = S;
   p.kb_per_split = ceil_div(p.kb_total, S);
   p.dstages = 3;
-  p.sc_cache_cols = 0;   // scales are prefetched into registers per K-block
-  const int sc_bytes = 0;
+  // Scale tile by TMA when its rows allow it (16-byte aligned, <= 32 KB); otherwise each
+  // K-block's two scales per row are prefetched into registers one block ahead.
+  const int G = K / group;
+  const bool sc_tma = (G % 8 == 0) && G <= 128 && aligned(sc, 16) && (ldsc * 2) % 16 == 0;
+  p.sc_cache_cols = sc_tma ? static_cast<uint32_t>(G) : 0u;
+  const int sc_bytes = sc_tma ? 128 * G * 2 : 0;
 
   int n_chunks = ceil_div(M, 256);
   int smem = 0;
   while (true) {
     p.chunk = round_up(ceil_div(M, n_chunks), 16);
     p.stage_bytes = kW4A16PackTile + 2u * static_cast<uint32_t>(round_up(p.chunk, 16)) * 128u;
-    const int fixed = 1024 + p.dstages * static_cast<int>(kW4A16DSlot) + sc_bytes + 512;
+    const int fixed = 1024 + p.dstages * static_cast<int>(kW4A16DSlot) + sc_bytes + 512 + 64;
     const uint32_t red_bytes = (S > 1) ? 128u * (static_cast<uint32_t>(p.chunk) * 4u + 16u) : 0u;
     int stages = std::min(6, (kSmemLimit - fixed) / static_cast<int>(p.stage_bytes));
     while (stages >= 2 && static_cast<uint32_t>(stages) * p.stage_bytes < red_bytes && stages < 6) ++stages;
@@ -228,9 +234,16 @@ int run_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const
   }
   p.tmem_cols = static_cast<uint32_t>(std::max(32, next_pow2(p.chunk)));
 
-  CUtensorMap tw, ta;
+  CUtensorMap tw, ta, tsc;
   memset(&tw, 0, sizeof(tw));
   memset(&ta, 0, sizeof(ta));
+  memset(&tsc, 0, sizeof(tsc));
+  if (sc_tma) {
+    const uint64_t d[2] = {static_cast<uint64_t>(G), static_cast<uint64_t>(N)};
+    const uint64_t s_[1] = {static_cast<uint64_t>(ldsc) * 2u};
+    const uint32_t b[2] = {static_cast<uint32_t>(G), 128};
+    if (int rc = encode_tiled(&tsc, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, sc, d, s_, b, CU_TENSOR_MAP_SWIZZLE_NONE)) return rc;
+  }
   {
     const uint64_t d[2] = {static_cast<uint64_t>(K / 2), static_cast<uint64_t>(N)};
     const uint64_t s_[1] = {static_cast<uint64_t>(ldwp)};
@@ -257,7 +270,7 @@ int run_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = S > 1 ? 1 : 0;
-  SPECQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, w4a16_kernel, p, tw, ta));
+  SPECQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, w4a16_kernel, p, tw, ta, tsc));
   LaunchRecord& r = last_launch_ref();
   r.variant = 0;
   r.grid[0] = static_cast<int>(grid.x); r.grid[1] = static_cast<int>(grid.y); r.grid[2] = static_cast<int>(grid.z);

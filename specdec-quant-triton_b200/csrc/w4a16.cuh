@@ -32,6 +32,7 @@ struct W4A16Params {
   int* status;
   int64_t lda, ldwp, ldsc, ldo, ldo_n;
   int m_rows, N, K, group;
+  int group_shift;     // log2(group) when group is a power of two, else -1
   int chunk;           // tokens per CTA (multiple of 16, <= 256)
   int kb_total;        // packed 64-byte blocks per row = K / 128
   int kb_per_split;
@@ -39,12 +40,18 @@ struct W4A16Params {
   int stages;          // TMA ring depth
   int dstages;         // dequantised-operand ring depth
   uint32_t stage_bytes;
-  uint32_t sc_cache_cols;  // fp16 scale columns cached per row (low range + high range)
+  uint32_t sc_cache_cols;  // groups per row of the TMA-loaded scale tile (0: prefetch per K-block)
   uint32_t tmem_cols;
 };
 
 constexpr int kW4A16DequantWarps = 16;
 constexpr int kW4A16DequantThreads = 32 * kW4A16DequantWarps;
+// The dequant warps form two groups that take alternate K-blocks, so two blocks are being
+// dequantised at any time (a single block's chain of smem load -> convert -> store -> fence
+// is latency-bound).
+constexpr int kW4A16Groups = 2;
+constexpr int kW4A16GroupWarps = kW4A16DequantWarps / kW4A16Groups;
+constexpr int kW4A16GroupThreads = 32 * kW4A16GroupWarps;
 constexpr int kW4A16Threads = 64 + kW4A16DequantThreads;   // warp 0 TMA, warp 1 MMA, then dequant (2..5 epilogue)
 constexpr uint32_t kW4A16PackTile = 128 * 64;   // packed bytes per stage
 constexpr uint32_t kW4A16OpTile = 128 * 128;    // one fp16 [128 x 64] operand tile
@@ -87,7 +94,7 @@ __device__ __forceinline__ void dequant_chunk(uint4 pk, __half2 slo, __half2 shi
 
 __global__ void __launch_bounds__(kW4A16Threads, 1)
     w4a16_kernel(const __grid_constant__ W4A16Params p, const __grid_constant__ CUtensorMap tmap_wp,
-                 const __grid_constant__ CUtensorMap tmap_a) {
+                 const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_sc) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   SPECQ_TRACE_INIT();
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -101,7 +108,8 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
   uint64_t* dfull = empty + p.stages;
   uint64_t* dempty = dfull + p.dstages;
   uint64_t* acc_full = dempty + p.dstages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint64_t* sc_full = acc_full + 1;                                  // scale tile landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sc_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const uint32_t warp = warp_id();
@@ -130,27 +138,26 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
   const int kb0 = split * p.kb_per_split;
   const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
   const int nkb = kb1 - kb0;
-  const int glo0 = (kb0 * 64) / p.group;        // first cached low-half group
-  const int ghi0 = (half_k + kb0 * 64) / p.group;
-  const int nlo = (kb1 * 64 - 1) / p.group - glo0 + 1;
   if (threadIdx.x == 0) SPECQ_TRACE_POINT(0, 0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full[s], 1u);
-      mbar_init(&empty[s], kW4A16DequantWarps + 1u);   // dequant warps + 1 MMA commit
+      mbar_init(&empty[s], kW4A16GroupWarps + 1u);   // the block's dequant group + 1 MMA commit
     }
     for (int d = 0; d < p.dstages; ++d) {
-      mbar_init(&dfull[d], kW4A16DequantWarps);
+      mbar_init(&dfull[d], kW4A16GroupWarps);
       mbar_init(&dempty[d], 1u);
     }
     mbar_init(acc_full, 1u);
+    mbar_init(sc_full, 1u);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_wp);
     tma_prefetch_desc(&tmap_a);
+    if (p.sc_cache_cols > 0) tma_prefetch_desc(&tmap_sc);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, p.tmem_cols);
@@ -167,6 +174,10 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
     if (elect_one()) {
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_a = policy_evict_last();
+      if (p.sc_cache_cols > 0) {   // the CTA's [128 x K/group] fp16 scale tile, once
+        mbar_arrive_expect_tx(sc_full, 128u * p.sc_cache_cols * 2u);
+        tma_load_2d(sc_cache, &tmap_sc, sc_full, 0, n0, pol_a);
+      }
       int issued = 0;
       for (int i = 0; i < nkb; ++i) {
         const int s = i % p.stages;
@@ -226,17 +237,32 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
   } else {
     // ---------------- dequant warps ----------------
     const int td = static_cast<int>(threadIdx.x) - 64;   // 0..511
-    // This thread dequantises 16-byte chunk (td & 3) of row td / 4 of every packed tile; the
-    // row's two fp16 group scales for the next K-block are fetched one block ahead.
-    const int r0 = td >> 2;
+    const int grp = td / kW4A16GroupThreads;               // K-blocks i with i % 2 == grp
+    const int tg = td % kW4A16GroupThreads;                // 0..255 within the group
+    // this thread dequantises 16-byte chunk (tg & 3) of rows r0 = tg / 4 and r0 + 64
+    const int r0 = tg >> 2;
+    const int c = tg & 3;
+    const int scc = static_cast<int>(p.sc_cache_cols);
     const int64_t row0 = static_cast<int64_t>(min(n0 + r0, p.N - 1)) * p.ldsc;
-    auto fetch = [&](int kb, __half (&s2)[2]) {
-      s2[0] = p.sc[row0 + (kb * 64) / p.group];
-      s2[1] = p.sc[row0 + (half_k + kb * 64) / p.group];
+    const int64_t row1 = static_cast<int64_t>(min(n0 + r0 + 64, p.N - 1)) * p.ldsc;
+    auto group_of = [&](int k) { return p.group_shift >= 0 ? (k >> p.group_shift) : (k / p.group); };
+    auto fetch = [&](int kb, __half (&s4)[4]) {
+      const int glo = group_of(kb * 64);
+      const int ghi = group_of(half_k + kb * 64);
+      if (scc > 0) {
+        s4[0] = sc_cache[r0 * scc + glo];
+        s4[1] = sc_cache[r0 * scc + ghi];
+        s4[2] = sc_cache[(r0 + 64) * scc + glo];
+        s4[3] = sc_cache[(r0 + 64) * scc + ghi];
+      } else {
+        s4[0] = p.sc[row0 + glo];
+        s4[1] = p.sc[row0 + ghi];
+        s4[2] = p.sc[row1 + glo];
+        s4[3] = p.sc[row1 + ghi];
+      }
     };
-    __half sc_cur[2], sc_nxt[2];
-    fetch(kb0, sc_cur);
-    for (int i = 0; i < nkb; ++i) {
+    if (scc > 0 && !mbar_wait(sc_full, 0u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) *abort_flag = 1;
+    for (int i = grp; i < nkb; i += kW4A16Groups) {
       const int s = i % p.stages;
       const int d = i % p.dstages;
       if (!mbar_wait(&full[s], static_cast<uint32_t>(i / p.stages) & 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE) ||
@@ -249,29 +275,29 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
       const uint8_t* pk = ring + s * p.stage_bytes;
       uint8_t* wlo = dring + d * kW4A16DSlot;
       uint8_t* whi = wlo + kW4A16OpTile;
-      if (i + 1 < nkb) fetch(kb0 + i + 1, sc_nxt);
-      const uint4 raw = *reinterpret_cast<const uint4*>(pk + td * 16);   // (row td/4, chunk td%4)
-      if (td == 0) SPECQ_TRACE_POINT(12, raw.x == 0x12345678u ? 63 : i);
+      __half sc4[4];
+      fetch(kb0 + i, sc4);
+      const uint4 raw0 = *reinterpret_cast<const uint4*>(pk + tg * 16);           // row r0
+      const uint4 raw1 = *reinterpret_cast<const uint4*>(pk + (tg + 256) * 16);   // row r0 + 64
+      if (td == 0) SPECQ_TRACE_POINT(12, raw0.x == 0x12345678u ? 63 : i);
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);    // packed tile consumed (activations: MMA commit)
-      {
-        const int r = td >> 2;
-        const int c = td & 3;
-        uint4 lo[2], hi[2];
-        dequant_chunk(raw, __half2half2(sc_cur[0]), __half2half2(sc_cur[1]), lo, hi);
-        *reinterpret_cast<uint4*>(wlo + sw128_offset(r, 2 * c)) = lo[0];
-        *reinterpret_cast<uint4*>(wlo + sw128_offset(r, 2 * c + 1)) = lo[1];
-        *reinterpret_cast<uint4*>(whi + sw128_offset(r, 2 * c)) = hi[0];
-        *reinterpret_cast<uint4*>(whi + sw128_offset(r, 2 * c + 1)) = hi[1];
-      }
+      uint4 lo[2], hi[2];
+      dequant_chunk(raw0, __half2half2(sc4[0]), __half2half2(sc4[1]), lo, hi);
+      *reinterpret_cast<uint4*>(wlo + sw128_offset(r0, 2 * c)) = lo[0];
+      *reinterpret_cast<uint4*>(wlo + sw128_offset(r0, 2 * c + 1)) = lo[1];
+      *reinterpret_cast<uint4*>(whi + sw128_offset(r0, 2 * c)) = hi[0];
+      *reinterpret_cast<uint4*>(whi + sw128_offset(r0, 2 * c + 1)) = hi[1];
+      dequant_chunk(raw1, __half2half2(sc4[2]), __half2half2(sc4[3]), lo, hi);
+      *reinterpret_cast<uint4*>(wlo + sw128_offset(r0 + 64, 2 * c)) = lo[0];
+      *reinterpret_cast<uint4*>(wlo + sw128_offset(r0 + 64, 2 * c + 1)) = lo[1];
+      *reinterpret_cast<uint4*>(whi + sw128_offset(r0 + 64, 2 * c)) = hi[0];
+      *reinterpret_cast<uint4*>(whi + sw128_offset(r0 + 64, 2 * c + 1)) = hi[1];
       if (td == 0) SPECQ_TRACE_POINT(13, i);
       fence_proxy_async_smem();
-      if (td == 0) SPECQ_TRACE_POINT(14, i);
       __syncwarp();
       if (lane == 0) mbar_arrive(&dfull[d]);
       if (td == 0) SPECQ_TRACE_POINT(11, i);
-      sc_cur[0] = sc_nxt[0];
-      sc_cur[1] = sc_nxt[1];
     }
   }
   __syncwarp();

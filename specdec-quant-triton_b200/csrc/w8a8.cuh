@@ -258,51 +258,57 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
       const int R = 1 << lgR;
       const int nq = static_cast<int>(n_pad >> 2);
       const int te = static_cast<int>(threadIdx.x) - 64;
-      // Two items per thread per pass and all peers' loads unrolled: the DSMEM round trips
-      // overlap instead of running one after another.
-      for (int it0 = te; it0 < R * nq; it0 += 256) {
-        int4 acc[2] = {make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0)};
+      // Up to four items per thread per pass with every peer's load in flight together: one
+      // DSMEM round trip per pass (a pull costs ~1 us here, so passes are what matters).
+      for (int it0 = te; it0 < R * nq; it0 += 512) {
+        int4 acc[4] = {make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0)};
+        uint4 v[4][8];
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
+        for (int u = 0; u < 4; ++u) {
           const int item = it0 + u * 128;
           if (item < R * nq) {
             const int trow = split * R + (item & (R - 1));
             const uint4* src = reinterpret_cast<const uint4*>(ring + trow * pitch + (item >> lgR) * 16);
 #pragma unroll
-            for (int pr = 0; pr < 8; ++pr) {
-              if (pr < S) {
-                const uint4 v = *dsmem_ptr(src, static_cast<uint32_t>(pr));
-                acc[u].x += static_cast<int32_t>(v.x);
-                acc[u].y += static_cast<int32_t>(v.y);
-                acc[u].z += static_cast<int32_t>(v.z);
-                acc[u].w += static_cast<int32_t>(v.w);
-              }
+            for (int pr = 0; pr < 8; ++pr)
+              if (pr < S) v[u][pr] = *dsmem_ptr(src, static_cast<uint32_t>(pr));
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+#pragma unroll
+          for (int pr = 0; pr < 8; ++pr) {
+            if (pr < S && it0 + u * 128 < R * nq) {
+              acc[u].x += static_cast<int32_t>(v[u][pr].x);
+              acc[u].y += static_cast<int32_t>(v[u][pr].y);
+              acc[u].z += static_cast<int32_t>(v[u][pr].z);
+              acc[u].w += static_cast<int32_t>(v[u][pr].w);
             }
           }
         }
-        if (warp == 2 && lane == 0) SPECQ_TRACE_POINT(12, it0 >> 8);
+        if (warp == 2 && lane == 0) SPECQ_TRACE_POINT(12, it0 >> 9);
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-        const int item = it0 + u * 128;
-        if (item >= R * nq) break;
-        const int cq = item >> lgR;
-        const int n = n0 + split * R + (item & (R - 1));
-        if (ok && n < p.N) {
-          const int32_t sv[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
-          const float swn = sw_s[n - n0];
+        for (int u = 0; u < 4; ++u) {
+          const int item = it0 + u * 128;
+          if (item >= R * nq) break;
+          const int cq = item >> lgR;
+          const int n = n0 + split * R + (item & (R - 1));
+          if (ok && n < p.N) {
+            const int32_t sv[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
+            const float swn = sw_s[n - n0];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int m = m0 + cq * 4 + j;
-            if (m < M) {
-              if (p.acc_out != nullptr) {
-                p.acc_out[static_cast<int64_t>(m) * p.ldacc + n] = sv[j];
-              } else {
-                const float v = __fmul_rn(__fmul_rn(static_cast<float>(sv[j]), sa_s[m - m0]), swn);
-                p.out[static_cast<int64_t>(m) * p.ldo + static_cast<int64_t>(n) * p.ldo_n] = __float2half_rn(v);
+            for (int j = 0; j < 4; ++j) {
+              const int m = m0 + cq * 4 + j;
+              if (m < M) {
+                if (p.acc_out != nullptr) {
+                  p.acc_out[static_cast<int64_t>(m) * p.ldacc + n] = sv[j];
+                } else {
+                  const float val = __fmul_rn(__fmul_rn(static_cast<float>(sv[j]), sa_s[m - m0]), swn);
+                  p.out[static_cast<int64_t>(m) * p.ldo + static_cast<int64_t>(n) * p.ldo_n] = __float2half_rn(val);
+                }
               }
             }
           }
-        }
         }
       }
     }

@@ -104,15 +104,18 @@ def test_config2_full_size(cuda, scale_dtype):
     assert ck.cluster >= 1
 
 
-@pytest.mark.parametrize("ctx", [[1, 17, 128, 129, 2048, 8192 - 3]])
-def test_context_lengths_and_splits(cuda, ctx):
+@pytest.mark.parametrize("ctx,cluster", [([1, 17, 128, 129, 2048, 8192 - 3], 4),   # 8192-token table
+                                         ([5, 300, 6000], 4),                       # 6000: 3 -> 4 splits
+                                         ([2, 3000, 4100], 4),
+                                         ([16000, 40, 1], 8)])
+def test_context_lengths_and_splits(cuda, ctx, cluster):
     import specq
     B, H, H_KV, D, ql = len(ctx), 16, 4, 128, 4
     kc, vc, ks, vs, bt, cl = specq.make_paged_kv(B, [max(c, ql) for c in ctx], H_KV, D, device="cuda", seed=3)
     q = torch.randn(B, ql, H, D, generator=torch.Generator().manual_seed(4)).half().cuda()
     out, ck = specq.paged_attention(q, kc, vc, ks, vs, bt, cl, ql)
     _check(out, _ref(q, kc, vc, ks, vs, bt, cl, ql))
-    assert ck.cluster > 1          # 8192-token table -> context split across a cluster
+    assert ck.cluster == cluster   # the context split across a cluster: a power of two
 
 
 @pytest.mark.parametrize("H,H_KV,page,qpp", [(64, 8, 16, 9), (8, 8, 16, 5), (32, 8, 8, 4), (32, 8, 32, 2),
