@@ -287,13 +287,18 @@ def _cpu_inputs(seed=0):
 
 
 def _cpu_step(x, frac_seqs=1.0):
-    """One verification step of the reference's exact path; `frac_seqs` < 1 samples the
-    attention over a prefix of the sequences (its cost is linear in them)."""
+    """One verification step of the reference's exact path, in seconds, scaled to the full
+    workload.  `frac_seqs` < 1 samples the attention over a prefix of the sequences (all have
+    the same context, so its cost is linear in their number) and scales that part back."""
     from oracle import cpu_reference as R
+    t0 = time.perf_counter()
     R.w8a8(x["a8"], x["sa"], x["w8"], x["sw"])
     R.w4a16(x["a4"], R.dequant_int4(x["wp"], x["sc"]))
+    t1 = time.perf_counter()
     nb = max(1, int(round(AT["B"] * frac_seqs)))
     R.paged_attention(x["q"][:nb], x["kc"], x["vc"], x["ks"], x["vs"], x["bt"][:nb], x["cl"][:nb], AT["k"] + 1)
+    t2 = time.perf_counter()
+    return (t1 - t0) + (t2 - t1) * AT["B"] / nb
 
 
 def _cpu_threads():
@@ -308,16 +313,28 @@ def cpu_baseline(budget_s=12.0):
     x = _cpu_inputs()
     _cpu_step(x)                      # warm-up (allocations, MKL init)
     t0 = time.perf_counter()
-    n = 0
+    n, total = 0, 0.0
     while True:
-        _cpu_step(x)
+        total += _cpu_step(x)
         n += 1
         if time.perf_counter() - t0 > budget_s or n >= 50:
             break
-    per = (time.perf_counter() - t0) / n
+    per = total / n
     return {"value": per * 1e6, "unit": "us", "cores": cores, "kind": "port",
             "sample": f"{n} full verification steps (W8A8 M=40 4096x4096, W4A16 M=72 14336x4096, "
                       f"attention B=8 ctx 4096 k=8) of the reference's exact PyTorch path on CPU"}
+
+
+def _config(world):
+    """The workload both arms report (the reference arm runs it on the host cores)."""
+    return {
+        "workload": ("verification step = W8A8 o_proj M=40 K=N=4096 (config 0) + W4A16 gate_proj M=72 "
+                     "K=4096 N=14336 (config 1) + INT8 paged attention B=8 ctx=4096 k=8 QPP=9 H=32/8 "
+                     "D=128 page 16 fp32 scales (config 2)"),
+        "sharding": f"GEMM columns and attention KV heads split {world} ways" if world > 1 else "none",
+        "l2": "rotating input copies > 2x L2 between timed steps (device arm)",
+        "parallelism": f"dp{world}-shard" if world > 1 else "single-gpu",
+    }
 
 
 # ----------------------------------------------------------------------------------------------
@@ -329,29 +346,23 @@ def run_reference(args):
         return 0
     cores = _cpu_threads()
     x = _cpu_inputs()
-    t0 = time.perf_counter()
-    _cpu_step(x)
-    one = time.perf_counter() - t0
+    one = _cpu_step(x)
     # bounded sample so that warmup + steps stay within ~3 minutes
     total = (args.warmup + args.steps) * one
     frac = 1.0 if total < 180 else max(1.0 / AT["B"], 180.0 / total)
     for _ in range(args.warmup):
         _cpu_step(x, frac)
-    ts = []
-    for _ in range(args.steps):
-        t = time.perf_counter()
-        _cpu_step(x, frac)
-        ts.append(time.perf_counter() - t)
-    # scale a sampled step back to the full step: attention is linear in the sequences
+    ts = [_cpu_step(x, frac) for _ in range(args.steps)]
     nb = max(1, int(round(AT["B"] * frac)))
     per_us = statistics.mean(ts) * 1e6
     sample = ("full verification step" if nb == AT["B"] else
-              f"verification step with attention over {nb} of {AT['B']} sequences")
+              f"verification step with attention timed over {nb} of {AT['B']} sequences and scaled "
+              f"to {AT['B']} (attention cost is linear in the sequences)")
     line = {"impl": "reference", "metric": _metric(), "value": per_us, "unit": "us", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_us / 1e3, "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": "fp32 (reference PyTorch path)",
             "data": "synthetic",
-            "config": {"workload": "verification step on CPU: reference exact PyTorch path", "parallelism": "cpu"},
+            "config": _config(args.gpus),
             "cpu_baseline": {"value": per_us, "unit": "us", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": per_us, "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -476,15 +487,10 @@ def run_ours(args):
         "vs_baseline": None,
         "dtype": "int8 (W8A8, int32 accumulate) + fp16 (W4A16, attention; fp32 accumulate)",
         "data": "synthetic (BASELINE config value distributions, seeded, generated on device)",
-        "config": {
-            "workload": ("verification step = W8A8 o_proj M=40 K=N=4096 (config 0) + W4A16 gate_proj M=72 "
-                         "K=4096 N=14336 (config 1) + INT8 paged attention B=8 ctx=4096 k=8 QPP=9 H=32/8 "
-                         "D=128 page 16 fp32 scales (config 2)"),
-            "sharding": f"GEMM columns and attention KV heads split {world} ways" if world > 1 else "none",
-            "l2": f"{n_copies} rotating input copies of {copy_bytes / 1e6:.1f} MB (> 2x L2)",
-            "timing": "CUDA events around K captured-graph replays; per-kernel: events around captured runs",
-            "parallelism": f"dp{world}-shard" if world > 1 else "single-gpu",
-        },
+        "config": _config(world),
+        "timing": {"l2": f"{n_copies} rotating input copies of {copy_bytes / 1e6:.1f} MB (> 2x L2)",
+                   "method": "CUDA events around K captured-graph replays; per-kernel: events around "
+                             "captured runs of that kernel over the copies"},
         "kernels": kern,
         "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": traffic,
