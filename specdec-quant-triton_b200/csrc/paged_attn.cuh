@@ -11,17 +11,18 @@
 //   * Transposed products put the 128 tokens of a KV block on the tcgen05 M=128 axis and the
 //     query rows (padded to a multiple of 16) on N:  S^T = K . Q^T  and  O^T = V^T . P^T.  No
 //     tensor-core lane is wasted on padding query rows.
-//   * K/V rows are gathered through the block table by two warps with 16-byte cp.async copies
-//     (four whole 128-byte rows per warp instruction) into a 3-stage int8 ring; the same warps
-//     fetch each token's K and V scales into the stage.  K lands in the 128B-swizzled layout
-//     the tensor core reads and feeds an INT8 MMA as it is: each query row is quantised once
-//     per CTA to int16 (scale amax/32639, 16x finer than the fp16 query itself) and split as
-//     hi*256 + lo with hi, lo int8, so one kind::i8 MMA with N = 2*NQ gives both integer
-//     partial products exactly in int32.  Five warps dequantise V to fp16 with its per-token
-//     scale folded in; the V tile is read MN-major by the PV product.
+//   * The CTA's slice of the block table is read once into shared memory.  K and V arrive by
+//     TMA (boxes of up to 16 slots of one page and one KV head, 128B-swizzled; K and V issued
+//     by two warps in parallel) into a 3-stage ring: bytes in flight cost no registers or
+//     load/store slots.  K feeds an INT8 MMA as it lands: the query rows are quantised once
+//     per CTA to int16 with one scale (amax/32639) and split hi*256 + lo into two int8 operand
+//     rows, so one kind::i8 MMA with N = 2*NQ gives both integer partial products exactly in
+//     int32.  Four warps (one thread per token row) dequantise V to fp16 with the token's
+//     scale folded in; the V tile is read MN-major by the PV product.  Per-token scales are
+//     loaded two blocks ahead by the threads that use them.
 //   * Softmax runs one thread per token row of S^T (TMEM lane = token): the per-token K scale
-//     is a per-thread scalar, the query-row scale a per-column one; the arithmetic runs on
-//     packed fp32 pairs.  The running max is "lazy": a block is exponentiated against the
+//     and the query scale fold into one per-thread scalar, the running max of each query column
+//     lives in registers; the arithmetic runs on packed fp32 pairs.  The running max is "lazy": a block is exponentiated against the
 //     current max and only when some score exceeds it by more than 2^8 does the CTA reduce
 //     the block max, rescale O^T and the normaliser, and recompute.  Blocks that lie wholly
 //     inside every query row's causal window take a mask-free path.  P is written MN-major
@@ -65,6 +66,7 @@ struct AttnParams {
   int h_kv, g, page, qpp, nq, n_qc;
   int g_shift, page_shift;  // log2 of g / page when they are powers of two, else -1
   int splits, stages;
+  int box_rows, box_shift; // K tiles arrive by TMA in boxes of box_rows slots of one page
   float sm_scale_log2;     // log2(e) / sqrt(D)
   uint32_t tmem_cols;
   uint32_t col_stride;     // TMEM columns of one score buffer (2 * nq int32, rounded to 32)
@@ -72,17 +74,17 @@ struct AttnParams {
   int out_vec;             // out rows are 16-byte aligned: 8 head dims per store
 };
 
-// warps [0, 8) softmax, [8, 10) K/V gather, 10 MMA issue + TMEM owner, [11, 16) V conversion
+// warps [0, 8) softmax, 8 K gather + 9 V gather (TMA), 10 MMA issue + TMEM owner,
+// [11, 15) V conversion
 constexpr int kAttnLoadWarps = 2;
 constexpr int kAttnMmaWarp = 8 + kAttnLoadWarps;
-constexpr int kAttnConvWarps = 5;
-constexpr int kAttnConvThreads = 32 * kAttnConvWarps;
-constexpr int kAttnThreads = 32 * (kAttnMmaWarp + 1) + kAttnConvThreads;
+constexpr int kAttnConvWarps = 4;              // one thread per token row of a block
+constexpr int kAttnThreads = 32 * (kAttnMmaWarp + 1) + 32 * kAttnConvWarps;
 constexpr uint32_t kAttnKV8 = 128 * 128;       // int8 K (or V) block: 128 tokens x 128 B
-constexpr uint32_t kAttnScl = 2 * kAttnKV8;    // stage offset of the per-token scales
-constexpr uint32_t kAttnStage = kAttnScl + 1024;   // K + V + scales (f32 K scale, f16 V scale)
+constexpr uint32_t kAttnStage = 2 * kAttnKV8;  // K + V, both 128B-swizzled
 constexpr uint32_t kAttnOp = 128 * 256;        // fp16 V tile: 128 tokens x 128 d
 constexpr int kAttnStages = 3;
+constexpr int kAttnMaxPages = 2048;            // block-table entries of one CTA's context range
 constexpr uint32_t kAttnPTile = 128 * 128;     // fp16 P tile: 128 tokens x 64 query rows
 constexpr float kLazyMaxLog2 = 8.0f;           // rescale once a score exceeds the max by 2^8
 
@@ -155,11 +157,6 @@ __device__ __forceinline__ float load_scale(const void* base, int scale_f32, int
                    : __half2float(__ldg(static_cast<const __half*>(base) + idx));
 }
 
-// cp.async 16 bytes global -> shared; src_size 0 zero-fills the destination.
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_size) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_size) : "memory");
-}
-
 // Packed fp32 pairs (sm_100 f32x2 arithmetic: two lanes of work per instruction).
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
   float2 d;
@@ -203,32 +200,45 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 constexpr uint32_t kScoreBias = 0x4B400000u;
 constexpr float kScoreBias257 = 3233808384.f;   // 257 * 1.5 * 2^23, exact in fp32
 
-__global__ void __launch_bounds__(kAttnThreads, 1) paged_attn_kernel(const __grid_constant__ AttnParams p) {
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,
+                                            int w, uint64_t cache_hint) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w), "l"(cache_hint)
+      : "memory");
+}
+
+template <int NQ>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    paged_attn_kernel(const __grid_constant__ AttnParams p, const __grid_constant__ CUtensorMap tmap_k,
+                      const __grid_constant__ CUtensorMap tmap_v) {
+  static_assert(NQ % 16 == 0 && NQ >= 16 && NQ <= 64, "query rows per CTA");
+  constexpr int NQH = NQ / 2;   // query columns per softmax thread
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   SPECQ_TRACE_INIT();
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int NQ = p.nq;
   // ring stage: [K int8, 128 tokens x 128 B, 128B-swizzled (a tcgen05 operand as it lands)]
-  //             [V int8, 128 tokens x 128 B, plain rows (converted to fp16 by the V warps)]
-  //             [K scale x log2(e)/sqrt(D), f32 x 128][V scale, f16 x 128]
+  //             [V int8, 128 tokens x 128 B, 128B-swizzled (read row-wise by the V warps)]
   uint8_t* ring = smem;
-  uint8_t* vop = ring + kAttnStages * kAttnStage;                   // fp16 V tiles x2 [2][128][128 B]
-  uint8_t* qop = vop + 2 * kAttnOp;                               // int8 Q: hi rows [0,NQ), lo rows [NQ,2NQ)
-  uint8_t* pop = qop + NQ * 256;                                  // fp16 P x2 [2][128 tokens][128 B]
-  float* m_s = reinterpret_cast<float*>(pop + 2 * kAttnPTile);      // [64] running max (log2 units)
-  float* alpha_s = m_s + 64;                                      // [64]
-  float* l_s = alpha_s + 64;                                      // [64]
-  float* qs_s = l_s + 64;                                         // [64] query-row scale of the int16 Q
-  float* nm_s = qs_s + 64;                                        // [64] -m_s
-  float* wmax = nm_s + 64;                                        // [4][64]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(wmax + 256);
+  uint8_t* vop = ring + kAttnStages * kAttnStage;                  // fp16 V tiles x2 [2][128][128 B]
+  uint8_t* qop = vop + 2 * kAttnOp;                                // int8 Q: hi rows [0,NQ), lo rows [NQ,2NQ)
+  uint8_t* pop = qop + NQ * 256;                                   // fp16 P x2 [2][128 tokens][128 B]
+  float* m_s = reinterpret_cast<float*>(pop + 2 * kAttnPTile);     // [64] running max (log2 units)
+  float* nm_s = m_s + 64;                                          // [64] -m_s
+  float* alpha_s = nm_s + 64;                                      // [64]
+  float* l_s = alpha_s + 64;                                       // [64]
+  float* qamax = l_s + 64;                                         // [64] |q| max per query row
+  float* wmax = qamax + 64;                                        // [4][64]
+  int* pages_s = reinterpret_cast<int*>(wmax + 256);                // [kAttnMaxPages] this CTA's page ids
+  uint64_t* bars = reinterpret_cast<uint64_t*>(pages_s + kAttnMaxPages);
   uint64_t* stage_full = bars;
   uint64_t* stage_empty = stage_full + kAttnStages;
   uint64_t* v_full = stage_empty + kAttnStages;   // [2]
-  uint64_t* s_full = v_full + 2;               // [2]
-  uint64_t* s_empty = s_full + 2;              // [2]
-  uint64_t* p_full = s_empty + 2;              // [2]
-  uint64_t* pv_done = p_full + 2;              // [2]  PV(j) done: frees P and V buffer j % 2
+  uint64_t* s_full = v_full + 2;                  // [2]
+  uint64_t* s_empty = s_full + 2;                 // [2]
+  uint64_t* p_full = s_empty + 2;                 // [2]
+  uint64_t* pv_done = p_full + 2;                 // [2]  PV(j) done: frees P and V buffer j % 2
   uint64_t* q_full = pv_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_full + 1);
 
@@ -268,20 +278,48 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attn_kernel(const __gri
   const int t_end = min(kv_end, t_begin + tchunk);
   const int nblk = (t_end > t_begin) ? (t_end - t_begin + 127) / 128 : 0;
 
-  const uint32_t cs2 = p.col_stride;                   // S buffer: int32 hi columns then lo columns
-  const uint32_t O_col = 2 * cs2;
-  const uint32_t L_col = O_col + p.o_cols;
-  const uint32_t ONES_col = L_col + p.o_cols;
+  constexpr uint32_t cs2 = static_cast<uint32_t>((2 * NQ + 31) & ~31);   // S buffer: hi columns, lo columns
+  constexpr uint32_t kOCols = static_cast<uint32_t>((NQ + 31) & ~31);
+  constexpr uint32_t O_col = 2 * cs2;
+  constexpr uint32_t L_col = O_col + kOCols;
+  constexpr uint32_t ONES_col = L_col + kOCols;
   auto page_of = [&](int tok) { return p.page_shift >= 0 ? (tok >> p.page_shift) : (tok / p.page); };
   auto slot_of = [&](int tok) { return p.page_shift >= 0 ? (tok & (p.page - 1)) : (tok % p.page); };
+  // The block-table entries of this CTA's token range, read once into shared memory: a page
+  // lookup is then a shared-memory read instead of a dependent global load (which takes
+  // longer than a whole block under full HBM load).
+  const int pg_first = page_of(t_begin);
+  const int pg_count = nblk > 0 ? page_of(t_end - 1) - pg_first + 1 : 0;
+  for (int i = static_cast<int>(threadIdx.x); i < pg_count; i += kAttnThreads)
+    pages_s[i] = __ldg(p.bt + b * p.bt_sb + pg_first + i);
+  // page id of token row `row` of block j (-1 past the split end)
+  auto token_page = [&](int j, int row) -> int {
+    const int tok = t_begin + j * 128 + row;
+    return (j < nblk && tok < t_end) ? pages_s[page_of(tok) - pg_first] : -1;
+  };
+  // element offset of that token's (page, slot, kv head) in the KV cache and in the scales
+  auto kv_offset = [&](int j, int row, int page) -> int64_t {
+    const int tok = t_begin + j * 128 + row;
+    return static_cast<int64_t>(page) * p.kv_sp + static_cast<int64_t>(slot_of(tok)) * p.kv_so +
+           static_cast<int64_t>(kvh) * p.kv_sh;
+  };
+  auto scale_offset = [&](int j, int row, int page) -> int64_t {
+    const int tok = t_begin + j * 128 + row;
+    return static_cast<int64_t>(page) * p.s_sp + static_cast<int64_t>(slot_of(tok)) * p.s_so +
+           static_cast<int64_t>(kvh) * p.s_sh;
+  };
+  auto page_ok = [&](int page) { return page >= 0 && page < p.n_pages; };
+  // per-token scale of token row `row` of block j (0 past the split end or on a bad page)
+  auto token_scale = [&](const void* base, int j, int row) -> float {
+    const int pg = token_page(j, row);
+    return page_ok(pg) ? load_scale(base, p.scale_f32, scale_offset(j, row, pg)) : 0.f;
+  };
 
   // ---- setup ---------------------------------------------------------------------------------
   if (threadIdx.x == 0) {
     for (int s = 0; s < kAttnStages; ++s) {
-      // gather lanes' cp.async arrivals + one arrival per gather warp for the scales it stored
-      mbar_init(&stage_full[s], 33u * kAttnLoadWarps);
-      // V warps + the QK commit + the softmax warps (K scales read)
-      mbar_init(&stage_empty[s], kAttnConvWarps + 1u + 8u);
+      mbar_init(&stage_full[s], 2u);                     // the K and the V gather lanes' expect_tx
+      mbar_init(&stage_empty[s], 1u + kAttnConvWarps);  // the QK commit + the V warps
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&v_full[i], kAttnConvWarps);
@@ -312,17 +350,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attn_kernel(const __gri
     const int t = static_cast<int>(threadIdx.x);             // 0..255
     const int tl = t & 127;                                  // token lane of S^T, d lane of O^T
     const int grp = t >> 7;
-    const int nqh = NQ >> 1;                                 // columns per group (multiple of 8)
-    const int col0 = grp * nqh;
+    const int col0 = grp * NQH;
     const uint32_t quad = warp & 3u;
     const uint32_t lane_base = tmem + ((quad * 32u) << 16);
-    // Q rows -> int16 per row (scale amax / 32639), split as hi * 256 + lo with hi, lo int8:
-    // two int8 operand rows each, so QK^T runs on the INT8 tensor core against the raw K bytes.
-    for (int it = t; it < NQ * 8; it += 256) {
+    // Q rows -> int16 with one scale for the CTA (gmax / 32639), split as hi * 256 + lo with
+    // hi, lo int8: two int8 operand rows each, so QK^T runs on the INT8 tensor core against
+    // the raw K bytes.  One scale makes the score scale a per-token scalar (no per-column
+    // constant); the rounding error of every row is relative to the CTA's largest |q|.
+    constexpr int kItems = (NQ * 8 + 255) / 256;   // (row, 16 head dims) pieces per thread
+    float qv[kItems][16];
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+      const int it = t + 256 * k;
       const int row = it >> 3;
-      const int piece = it & 7;                              // 16 head dims
-      float qv[16];
-      if (row < rows_valid) {
+      const int piece = it & 7;
+      float amax = 0.f;
+      if (it < NQ * 8 && row < rows_valid) {
         const int qi = q_lo + (p.g_shift >= 0 ? (row >> p.g_shift) : (row / p.g));
         const int head = kvh * p.g + (p.g_shift >= 0 ? (row & (p.g - 1)) : (row % p.g));
         const uint4* src = reinterpret_cast<const uint4*>(p.q + b * p.q_sb + static_cast<int64_t>(qi) * p.q_st +
@@ -332,24 +375,35 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attn_kernel(const __gri
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-          qv[2 * i] = f.x;
-          qv[2 * i + 1] = f.y;
+          qv[k][2 * i] = f.x;
+          qv[k][2 * i + 1] = f.y;
         }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(qv[k][i]));
       } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) qv[i] = 0.f;
+        for (int i = 0; i < 16; ++i) qv[k][i] = 0.f;
       }
-      float amax = 0.f;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(qv[i]));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-      const float inv = amax > 0.f ? 32639.f / amax : 0.f;
+      if (it < NQ * 8 && piece == 0) qamax[row] = amax;
+    }
+    named_barrier_sync(3, 256);
+    float gmax = 0.f;
+    for (int r = 0; r < NQ; ++r) gmax = fmaxf(gmax, qamax[r]);
+    const float q_inv = gmax > 0.f ? 32639.f / gmax : 0.f;
+    const float q_scale = gmax / 32639.f;
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+      const int it = t + 256 * k;
+      if (it >= NQ * 8) break;
+      const int row = it >> 3;
+      const int piece = it & 7;
       uint32_t hw[4] = {0u, 0u, 0u, 0u}, lw[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const int v16 = __float2int_rn(qv[i] * inv);        // |v16| <= 32639
+        const int v16 = __float2int_rn(qv[k][i] * q_inv);    // |v16| <= 32639
         const int hi = (v16 + 128) >> 8;                     // in [-127, 127]
         const int lo = v16 - (hi << 8);                      // in [-128, 127]
         hw[i >> 2] |= (static_cast<uint32_t>(hi) & 0xFFu) << (8 * (i & 3));
@@ -357,7 +411,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attn_kernel(const __gri
       }
       *reinterpret_cast<uint4*>(qop + sw128_offset(row, piece)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
       *reinterpret_cast<uint4*>(qop + sw128_offset(NQ + row, piece)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-      if (piece == 0) qs_s[row] = amax / 32639.f;
     }
     // padding rows (all-zero queries, never stored) start at max 0: their scores are exactly 0,
     // so they never trigger a rescale and the interior blocks need no column mask
@@ -372,7 +425,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attn_kernel(const __gri
     for (int i = 0; i < 8; ++i) bias8[i] = kScoreBias;
     // this thread's hi and lo columns of score buffer sb back to the bias
     auto rebias = [&](uint32_t sb) {
-      for (int c0 = 0; c0 < nqh; c0 += 8) {
+#pragma unroll
+      for (int c0 = 0; c0 < NQH; c0 += 8) {
         tmem_st8(lane_base + sb * cs2 + col0 + c0, bias8);
         tmem_st8(lane_base + sb * cs2 + NQ + col0 + c0, bias8);
       }
@@ -393,22 +447,26 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attn_kernel(const __gri
     __syncwarp();
     if (lane == 0) mbar_arrive(q_full);
 
+    // -max of this thread's query columns, kept in registers (changes only on a rescale)
+    float nmr[NQH];
+#pragma unroll
+    for (int i = 0; i < NQH; ++i) nmr[i] = nm_s[col0 + i];
+
     // Multi-thread roles never leave a loop early: after a wait runs out (ok = false) they skip
     // the remaining waits but still reach every named barrier, so no warp is stranded.
-    for (int j = 0; j < nblk; ++j) {
+    // Block j; `ksr` holds this token's K scale of block j (loaded two blocks ago) and is
+    // reloaded with that of block j + 2.  The loop runs in pairs with two scale registers, so
+    // a loaded value is used where it lies (a register copy would wait for the load).
+    auto soft_block = [&](int j, float& ksr) {
       const int t_abs = t_begin + j * 128 + tl;
       const uint32_t sb = static_cast<uint32_t>(j & 1);
       const uint32_t par2 = static_cast<uint32_t>(j >> 1) & 1u;
       // query rows q >= q_first may see this token (causal window), rows >= q_stop never do
       const int q_stop = (t_abs < t_end) ? rows_valid : 0;
       const int q_first = min(max(0, (t_abs - qpos0) * p.g), q_stop);
-      // this token's K scale (log2(e) / sqrt(D) folded in), from the ring stage of block j
-      const int st = j % kAttnStages;
-      ok = ok && mbar_wait(&stage_full[st], static_cast<uint32_t>(j / kAttnStages) & 1u, status,
-                           SPECQ_STATUS_TIMEOUT_PIPELINE);
-      const float c_t = reinterpret_cast<const float*>(ring + st * kAttnStage + kAttnScl)[tl];
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&stage_empty[st]);
+      // this token's score scale: K scale x log2(e) / sqrt(D) x the query scale
+      const float a_t = ksr * p.sm_scale_log2 * q_scale;
+      ksr = token_scale(p.ks, j + 2, tl);
       if (t == 0) SPECQ_TRACE_POINT(20, j);
       ok = ok && mbar_wait(&s_full[sb], par2, status, SPECQ_STATUS_TIMEOUT_MMA);
       // P buffer sb is free once PV(j-2) has read it
@@ -420,19 +478,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attn_kernel(const __gri
       // every token of the block is visible to every query row: no column mask
       const int t_last = t_begin + j * 128 + 127;
       const bool interior = t_last < t_end && t_last <= qpos0;
+      const float2 a2 = make_float2(a_t, a_t);
 
-      // scaled score of query column q: (256 * hi + lo) * qs[q] * ks_t * log2e / sqrt(D)
-      auto score = [&](uint32_t hb, uint32_t lb, int q) {
-        return (fmaf(__uint_as_float(hb), 256.f, __uint_as_float(lb)) - kScoreBias257) * (qs_s[q] * c_t);
+      // scaled score (log2 units) of query column q from its biased hi / lo accumulators
+      auto score = [&](uint32_t hb, uint32_t lb) {
+        return (fmaf(__uint_as_float(hb), 256.f, __uint_as_float(lb)) - kScoreBias257) * a_t;
       };
-      const float2 c2 = make_float2(c_t, c_t);
       // one optimistic pass: P against the current max, noting whether any score exceeds it
       // by more than 2^8 (then the block is redone below with a raised max)
       auto write_p = [&](float& xmax) {
-        for (int c0 = 0; c0 < nqh; c0 += 16) {   // 16 columns per TMEM round trip (hi and lo)
-          uint32_t rh[16], rl[16];
-          const bool two = c0 + 8 < nqh;
-          if (t == 0 && c0 == 0) SPECQ_TRACE_POINT(23, j);
+#pragma unroll
+        for (int c0 = 0; c0 < NQH; c0 += 16) {   // 16 columns per TMEM round trip (hi and lo)
+          constexpr int kW = 16;
+          uint32_t rh[kW], rl[kW];
+          const bool two = c0 + 8 < NQH;
           tmem_ld8(s_addr + c0, *reinterpret_cast<uint32_t(*)[8]>(rh));
           tmem_ld8(s_addr + NQ + c0, *reinterpret_cast<uint32_t(*)[8]>(rl));
           if (two) {
@@ -440,19 +499,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attn_kernel(const __gri
             tmem_ld8(s_addr + NQ + c0 + 8, *reinterpret_cast<uint32_t(*)[8]>(rl + 8));
           }
           tmem_wait_ld();
-          if (t == 0 && c0 == 0) SPECQ_TRACE_POINT(25, j);
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             if (h == 1 && !two) break;
             const int qb = col0 + c0 + 8 * h;
-            const float4 qs0 = *reinterpret_cast<const float4*>(qs_s + qb);
-            const float4 qs1 = *reinterpret_cast<const float4*>(qs_s + qb + 4);
-            const float4 n0 = *reinterpret_cast<const float4*>(nm_s + qb);
-            const float4 n1 = *reinterpret_cast<const float4*>(nm_s + qb + 4);
-            const float2 qsv[4] = {make_float2(qs0.x, qs0.y), make_float2(qs0.z, qs0.w), make_float2(qs1.x, qs1.y),
-                                   make_float2(qs1.z, qs1.w)};
-            const float2 nmv[4] = {make_float2(n0.x, n0.y), make_float2(n0.z, n0.w), make_float2(n1.x, n1.y),
-                                   make_float2(n1.z, n1.w)};
             uint32_t pk[4];
 #pragma unroll
             for (int i = 0; i < 8; i += 2) {
@@ -461,7 +511,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attn_kernel(const __gri
               const float2 lb = make_float2(__uint_as_float(rl[r0]), __uint_as_float(rl[r0 + 1]));
               const float2 sv = fadd2(ffma2(hb, make_float2(256.f, 256.f), lb),
                                       make_float2(-kScoreBias257, -kScoreBias257));
-              float2 x = ffma2(sv, fmul2(qsv[i >> 1], c2), nmv[i >> 1]);
+              float2 x = ffma2(sv, a2, make_float2(nmr[c0 + r0], nmr[c0 + r0 + 1]));
               if (!interior) {   // causal window and split end; padding rows
                 const uint32_t span = static_cast<uint32_t>(q_stop - q_first);
                 x.x = static_cast<uint32_t>(qb + i - q_first) < span ? x.x : -INFINITY;
@@ -488,7 +538,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attn_kernel(const __gri
                                SPECQ_STATUS_TIMEOUT_MMA);
         tc_fence_after();
         // block max per query column: warp shuffles, then across the four lane quadrants
-        for (int c0 = 0; c0 < nqh; c0 += 8) {
+#pragma unroll
+        for (int c0 = 0; c0 < NQH; c0 += 8) {
           uint32_t rh[8], rl[8];
           tmem_ld8(s_addr + c0, rh);
           tmem_ld8(s_addr + NQ + c0, rl);
@@ -496,7 +547,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attn_kernel(const __gri
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const int q = col0 + c0 + i;
-            float y = (q >= q_first && q < q_stop) ? score(rh[i], rl[i], q) : -INFINITY;
+            float y = (q >= q_first && q < q_stop) ? score(rh[i], rl[i]) : -INFINITY;
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) y = fmaxf(y, __shfl_xor_sync(0xffffffffu, y, o));
             if (lane == 0) wmax[quad * 64 + q] = y;
@@ -512,8 +563,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attn_kernel(const __gri
           nm_s[t] = -mn;
         }
         named_barrier_sync(3, 256);
+#pragma unroll
+        for (int i = 0; i < NQH; ++i) nmr[i] = nm_s[col0 + i];
         if (j > 0) {   // rescale this group's columns of O^T (all lanes) and of the normaliser row
-          for (int c0 = 0; c0 < nqh; c0 += 8) {
+#pragma unroll
+          for (int c0 = 0; c0 < NQH; c0 += 8) {
             uint32_t r[8];
             tmem_ld8(lane_base + O_col + col0 + c0, r);
             tmem_wait_ld();
@@ -543,6 +597,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attn_kernel(const __gri
         mbar_arrive(&p_full[sb]);
       }
       if (t == 0) SPECQ_TRACE_POINT(24, j);
+    };
+    float ks_even = token_scale(p.ks, 0, tl), ks_odd = token_scale(p.ks, 1, tl);
+    for (int j = 0; j < nblk; j += 2) {
+      soft_block(j, ks_even);
+      if (j + 1 < nblk) soft_block(j + 1, ks_odd);
     }
     // ---- final normaliser and accumulator ----
     if (nblk > 0) {
@@ -552,7 +611,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attn_kernel(const __gri
       tc_fence_after();
       if (t == 0) SPECQ_TRACE_POINT(60, 0);
       if (quad == 0) {
-        for (int c0 = 0; c0 < nqh; c0 += 8) {
+#pragma unroll
+        for (int c0 = 0; c0 < NQH; c0 += 8) {
           uint32_t r[8];
           tmem_ld8(lane_base + L_col + col0 + c0, r);
           tmem_wait_ld();
@@ -565,107 +625,53 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attn_kernel(const __gri
     }
     named_barrier_sync(3, 256);
   } else if (warp < kAttnMmaWarp) {
-    // =================================== K/V gather ===================================
-    // 16-byte cp.async copies through the block table; gather warp lw owns token rows
-    // [64 lw, 64 lw + 64) of every block.  Lane l looks up the pages of rows l and l + 32 of
-    // that range two blocks ahead (the loads land while a block is issued); the copies go 8
-    // lanes per token row (lane l copies chunk l % 8), so every warp instruction moves four
-    // whole 128-byte rows.  K lands in the 128B-swizzled layout the tensor core reads; rows
-    // past the split end or on an invalid page are zero-filled.
-    const int lw = static_cast<int>(warp) - 8;
+    // =================================== K / V gather ===================================
+    // K (warp 8) and V (warp 9) arrive by TMA in boxes of box_rows slots of one page and one
+    // KV head, both 128B-swizzled (K in the layout the tensor core reads, V so the V warps' row
+    // reads are free of bank conflicts); lane b issues box b of a block, the two warps in
+    // parallel.  Invalid pages map past the tensor, which the TMA fills with zeros.  Bytes in
+    // flight cost no registers here: the ring depth alone sets how much of the HBM latency is
+    // covered.
+    const bool is_v = warp == 9;
+    const CUtensorMap* tmap = is_v ? &tmap_v : &tmap_k;
+    const uint32_t half_off = is_v ? kAttnKV8 : 0u;
     const int l = static_cast<int>(lane);
-    const int ch = l & 7;
-    const int8_t* kc = p.kc + ch * 16;
-    const int8_t* vc = p.vc + ch * 16;
-    auto load_pages = [&](int j, int (&pg)[2]) {
-#pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const int tok = t_begin + j * 128 + 64 * lw + 32 * rr + l;
-        pg[rr] = (j < nblk && tok < t_end) ? __ldg(p.bt + b * p.bt_sb + page_of(tok)) : -1;
-      }
-    };
-    int64_t src_off[2];   // byte offset of the token row, -1 when there is nothing to read
-    auto offsets = [&](int j, const int (&pg)[2]) {
-#pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const int tok = t_begin + j * 128 + 64 * lw + 32 * rr + l;
-        src_off[rr] = (pg[rr] >= 0 && pg[rr] < p.n_pages)
-                          ? static_cast<int64_t>(pg[rr]) * p.kv_sp + static_cast<int64_t>(slot_of(tok)) * p.kv_so +
-                                static_cast<int64_t>(kvh) * p.kv_sh
-                          : int64_t(-1);
-      }
-    };
-    // per-token scales of the rows this lane looks up, loaded one block ahead
-    float ksr[2], vsr[2];
-    auto scales = [&](int j, const int (&pg)[2]) {
-#pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        ksr[rr] = 0.f;
-        vsr[rr] = 0.f;
-        if (pg[rr] >= 0 && pg[rr] < p.n_pages) {
-          const int tok = t_begin + j * 128 + 64 * lw + 32 * rr + l;
-          const int64_t idx = static_cast<int64_t>(pg[rr]) * p.s_sp + static_cast<int64_t>(slot_of(tok)) * p.s_so +
-                              static_cast<int64_t>(kvh) * p.s_sh;
-          ksr[rr] = load_scale(p.ks, p.scale_f32, idx);
-          vsr[rr] = load_scale(p.vs, p.scale_f32, idx);
-        }
-      }
-    };
-    int pg_cur[2], pg_next[2];
-    load_pages(0, pg_cur);
-    load_pages(1, pg_next);
-    offsets(0, pg_cur);
-    scales(0, pg_cur);
+    const int br = p.box_rows;
+    const int nbox = 128 >> p.box_shift;
+    const uint64_t hint = policy_evict_first();
+    if (l == 0) tma_prefetch_desc(tmap);
     int s = 0;
     uint32_t phase = 0;
+    int issued = 0;
     for (int j = 0; j < nblk; ++j) {
-      int pg_after[2];
-      load_pages(j + 2, pg_after);
       if (!mbar_wait(&stage_empty[s], phase ^ 1u, status, SPECQ_STATUS_TIMEOUT_PIPELINE)) {
         ok = false;
         break;
       }
-      if (lw == 0) SPECQ_TRACE_POINT(50, j);
-      const uint32_t kst = smem_u32(ring + s * kAttnStage);
-      const uint32_t vst = kst + kAttnKV8;
-#pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int src_lane = 4 * i + (l >> 3);
-          const int row = 64 * lw + 32 * rr + src_lane;
-          const int64_t off = __shfl_sync(0xffffffffu, src_off[rr], src_lane);
-          const uint32_t sz = off >= 0 ? 16u : 0u;
-          const int64_t o = off >= 0 ? off : 0;
-          cp_async16(kst + sw128_offset(static_cast<uint32_t>(row), static_cast<uint32_t>(ch)), kc + o, sz);
-          cp_async16(vst + static_cast<uint32_t>(row * 128 + ch * 16), vc + o, sz);
-        }
+      if (!is_v) SPECQ_TRACE_POINT(50, j);
+      uint8_t* dst = ring + s * kAttnStage + half_off;
+      if (l == 0) mbar_arrive_expect_tx(&stage_full[s], kAttnKV8);
+      __syncwarp();
+      for (int bx = l; bx < nbox; bx += 32) {   // box bx starts at token row bx * br
+        const int row = bx * br;
+        const int pg = token_page(j, row);
+        tma_load_4d(dst + row * 128, tmap, &stage_full[s], 0, kvh, slot_of(t_begin + j * 128 + row),
+                    page_ok(pg) ? pg : p.n_pages, hint);
       }
-      cp_async_mbar_arrive(&stage_full[s]);
-      {   // the scales: K scale with log2(e) / sqrt(D) folded in, V scale in fp16 (exact for
-          // fp16 scales, one rounding for fp32 ones) for the fp16 multiply of the V warps
-        float* ksc = reinterpret_cast<float*>(ring + s * kAttnStage + kAttnScl);
-        __half* vsc = reinterpret_cast<__half*>(ksc + 128);
-#pragma unroll
-        for (int rr = 0; rr < 2; ++rr) {
-          ksc[64 * lw + 32 * rr + l] = ksr[rr] * p.sm_scale_log2;
-          vsc[64 * lw + 32 * rr + l] = __float2half_rn(vsr[rr]);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&stage_full[s]);   // release: the scales are visible
-      }
-      if (lw == 0) SPECQ_TRACE_POINT(51, j);
-      offsets(j + 1, pg_next);
-      scales(j + 1, pg_next);
-      pg_next[0] = pg_after[0];
-      pg_next[1] = pg_after[1];
+      ++issued;
+      if (!is_v) SPECQ_TRACE_POINT(51, j);
       if (++s == kAttnStages) {
         s = 0;
         phase ^= 1u;
       }
     }
-    // copies in flight must land before the CTA can exit
-    asm volatile("cp.async.wait_all;" ::: "memory");
+    // the TMA copies of an abandoned loop land before the CTA exits: wait (bounded) for the
+    // stages this warp armed
+    if (!ok) {
+      for (int jj = max(0, issued - kAttnStages); jj < issued; ++jj)
+        (void)mbar_wait(&stage_full[jj % kAttnStages], static_cast<uint32_t>(jj / kAttnStages) & 1u, status,
+                        SPECQ_STATUS_TIMEOUT_PIPELINE);
+    }
   } else if (warp == kAttnMmaWarp) {
     // =================================== MMA issuer ===================================
     if (elect_one()) {
@@ -687,7 +693,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attn_kernel(const __gri
           umma_i8_ss(tmem + sb * cs2, ak, bq, id_qk, 1u);   // onto the bias the softmax left
         }
         umma_commit(&s_full[sb]);
-        umma_commit(&stage_empty[s]);   // the K half of the stage is consumed
+        umma_commit(&stage_empty[s]);   // the K tile is consumed
         SPECQ_TRACE_POINT(31, j);
       };
       auto issue_pv = [&](int i) {
@@ -736,52 +742,54 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attn_kernel(const __gri
     }
   } else {
     // =================================== V warps ===================================
-    const int c = static_cast<int>(threadIdx.x) - 32 * (kAttnMmaWarp + 1);   // 0..kAttnConvThreads-1
-    for (int j = 0; j < nblk; ++j) {
+    // Thread c owns token row c of every block: it reads the row's 128 V bytes from the ring
+    // (128B-swizzled, so eight consecutive rows hit eight distinct bank groups), converts them
+    // to fp16 with the token's V scale folded in and stores the row into the V operand tile.
+    const int c = static_cast<int>(threadIdx.x) - 32 * (kAttnMmaWarp + 1);   // 0..127
+    // block j; `vsr` holds this token's V scale of block j (loaded two blocks ago) and is
+    // reloaded with that of block j + 2 (pairs of blocks with two registers: no copies)
+    auto step = [&](int j, float& vsr) {
       const int s = j % kAttnStages;
       const uint32_t sb = static_cast<uint32_t>(j & 1);
       const uint32_t par2 = static_cast<uint32_t>(j >> 1) & 1u;
-      // ---- V (scale folded in) into buffer sb, free once PV(j-2) has completed
       ok = ok && mbar_wait(&stage_full[s], static_cast<uint32_t>(j / kAttnStages) & 1u, status,
                            SPECQ_STATUS_TIMEOUT_PIPELINE);
       if (c == 0) SPECQ_TRACE_POINT(40, j);
+      // the token's V scale in fp16 (exact for fp16 scales; one rounding for fp32 scales), so
+      // the per-element multiply stays on the fp16 pipe
+      const __half2 s2 = __half2half2(__float2half_rn(vsr));
+      vsr = token_scale(p.vs, j + 2, c);
+      const uint8_t* vrow = ring + s * kAttnStage + kAttnKV8 + c * 128;
+      uint4 raw[8];
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch)
+        raw[ch] = *reinterpret_cast<const uint4*>(vrow + ((static_cast<uint32_t>(ch) ^ (static_cast<uint32_t>(c) & 7u)) << 4));
+      // V buffer sb is free once PV(j-2) has completed
       if (j >= 2) ok = ok && mbar_wait(&pv_done[sb], par2 ^ 1u, status, SPECQ_STATUS_TIMEOUT_MMA);
-      const uint8_t* v8 = ring + s * kAttnStage + kAttnKV8;
-      const __half* vsc = reinterpret_cast<const __half*>(ring + s * kAttnStage + kAttnScl + 512);
       uint8_t* vdst = vop + sb * kAttnOp;
-      constexpr int kPer = (1024 + kAttnConvThreads - 1) / kAttnConvThreads;
-      uint4 raw[kPer];
 #pragma unroll
-      for (int k = 0; k < kPer; ++k) {   // all loads first, then convert and store
-        const int idx = c + k * kAttnConvThreads;
-        if (idx < 1024) raw[k] = *reinterpret_cast<const uint4*>(v8 + idx * 16);
-      }
+      for (int ch = 0; ch < 8; ++ch) {
+        uint32_t h[8];
+        i8x16_to_f16(raw[ch], h);
 #pragma unroll
-      for (int k = 0; k < kPer; ++k) {
-        const int idx = c + k * kAttnConvThreads;
-        if (idx < 1024) {
-          const int row = idx >> 3;
-          const int ch = idx & 7;
-          uint32_t h[8];
-          i8x16_to_f16(raw[k], h);
-          // the token's V scale in fp16 (exact for fp16 scales; one rounding for fp32 scales),
-          // so the per-element multiply stays on the fp16 pipe
-          const __half2 s2 = __half2half2(vsc[row]);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            __half2 o = __hmul2(*reinterpret_cast<__half2*>(&h[i]), s2);
-            h[i] = *reinterpret_cast<uint32_t*>(&o);
-          }
-          store_f16_chunk_pair(vdst, row, ch, h);
+        for (int i = 0; i < 8; ++i) {
+          __half2 o = __hmul2(*reinterpret_cast<__half2*>(&h[i]), s2);
+          h[i] = *reinterpret_cast<uint32_t*>(&o);
         }
+        store_f16_chunk_pair(vdst, c, ch, h);
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&v_full[sb]);
-        mbar_arrive(&stage_empty[s]);
+        mbar_arrive(&stage_empty[s]);   // the V half of the stage is consumed
       }
       if (c == 0) SPECQ_TRACE_POINT(45, j);
+    };
+    float vs_even = token_scale(p.vs, 0, c), vs_odd = token_scale(p.vs, 1, c);
+    for (int j = 0; j < nblk; j += 2) {
+      step(j, vs_even);
+      if (j + 1 < nblk) step(j + 1, vs_odd);
     }
   }
   __syncwarp();
@@ -930,9 +938,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attn_kernel(const __gri
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) SPECQ_TRACE_POINT(9, 0);
+  SPECQ_TRACE_CTA_END();
   if (warp == kAttnMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, p.tmem_cols);
+  }
+}
+
+inline const void* paged_attn_kernel_by_variant(int variant) {
+  switch (variant) {   // query rows per CTA = 16 * (variant + 1)
+    case 0: return reinterpret_cast<const void*>(paged_attn_kernel<16>);
+    case 1: return reinterpret_cast<const void*>(paged_attn_kernel<32>);
+    case 2: return reinterpret_cast<const void*>(paged_attn_kernel<48>);
+    case 3: return reinterpret_cast<const void*>(paged_attn_kernel<64>);
+    default: return nullptr;
   }
 }
 
@@ -987,6 +1006,12 @@ inline int run_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_
   p.b_grid = b_grid; p.n_seqs = n_seqs; p.q_len = q_len; p.ql_max = ql_max;
   p.h_kv = H_KV; p.g = G; p.page = page;
   p.kc = kc; p.vc = vc;
+  int br = 1;
+  while (br < 16 && page % (br * 2) == 0) br *= 2;
+  // 128B-swizzled TMA boxes land on 1024-byte boundaries only for boxes of >= 8 slots
+  if (br < 8) return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: page size %d is not a multiple of 8", page);
+  p.box_rows = br;
+  p.box_shift = __builtin_ctz(static_cast<unsigned>(br));
   p.out_vec = aligned(out, 16) && o_sb % 8 == 0 && o_st % 8 == 0 && o_sh % 8 == 0;
   p.kv_sp = kv_sp; p.kv_so = kv_so; p.kv_sh = kv_sh;
   p.qpp = std::min(qpp, 64 / G);                 // QPP only changes the schedule
@@ -1008,17 +1033,35 @@ inline int run_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_
   if (p.tmem_cols > 512) return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: too many query rows per CTA");
   if (static_cast<int64_t>(b_grid) * p.n_qc > 65535)
     return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: grid too large");
+  {   // one CTA's block-table slice must fit its shared-memory copy
+    const int tchunk_max = round_up(ceil_div(max_ctx, p.splits), 128);
+    if (tchunk_max / page + 2 > kAttnMaxPages)
+      return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: block table of %d pages per context split", tchunk_max / page);
+  }
 
-  // ring + two fp16 V tiles + int8 Q (hi, lo) + two P^T tiles + scales/softmax state + barriers
+  // K ring + two fp16 V tiles + int8 Q (hi, lo) + two P tiles + softmax state + barriers
   const int smem = 1024 + p.stages * static_cast<int>(kAttnStage) + 2 * static_cast<int>(kAttnOp) +
-                   p.nq * 256 + 2 * static_cast<int>(kAttnPTile) + 4096 + (2 * p.stages + 17) * 8 + 16;
+                   p.nq * 256 + 2 * static_cast<int>(kAttnPTile) + 4096 + kAttnMaxPages * 4 +
+                   (2 * p.stages + 17) * 8 + 16;
   if (smem > 232448) return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: shared memory %d too large", smem);
   if ((p.nq * 128 + 3 * p.splits * p.nq) * 4 > p.stages * static_cast<int>(kAttnStage))
     return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: combine buffer does not fit");
 
+  CUtensorMap tk, tv;
+  {
+    const uint64_t dims[4] = {128u, static_cast<uint64_t>(H_KV), static_cast<uint64_t>(page), static_cast<uint64_t>(n_pages)};
+    const uint64_t strides[3] = {static_cast<uint64_t>(kv_sh), static_cast<uint64_t>(kv_so), static_cast<uint64_t>(kv_sp)};
+    const uint32_t box[4] = {128u, 1u, static_cast<uint32_t>(br), 1u};
+    if (int rc = encode_tiled(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, kc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+    if (int rc = encode_tiled(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, vc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  }
+  const int variant = p.nq / 16 - 1;
+  const void* fn = paged_attn_kernel_by_variant(variant);
   const dim3 grid(static_cast<unsigned>(p.splits), static_cast<unsigned>(H_KV),
                   static_cast<unsigned>(b_grid * p.n_qc));
-  SPECQ_CUDA_TRY(cudaFuncSetAttribute(paged_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  SPECQ_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kAttnThreads, 1, 1);
@@ -1031,9 +1074,10 @@ inline int run_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = p.splits > 1 ? 1 : 0;
-  SPECQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, paged_attn_kernel, p));
+  void* args[] = {&p, &tk, &tv};
+  SPECQ_CUDA_TRY(cudaLaunchKernelExC(&cfg, fn, args));
   LaunchRecord& r = last_launch_ref();
-  r.variant = 0;
+  r.variant = variant;
   r.grid[0] = static_cast<int>(grid.x); r.grid[1] = static_cast<int>(grid.y); r.grid[2] = static_cast<int>(grid.z);
   r.cluster_x = p.splits;
   r.threads = kAttnThreads;
@@ -1041,8 +1085,6 @@ inline int run_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_
   return SPECQ_OK;
 }
 
-inline const void* paged_attn_kernel_by_variant(int variant) {
-  return variant == 0 ? reinterpret_cast<const void*>(paged_attn_kernel) : nullptr;
-}
+
 
 }  // namespace specq

@@ -48,14 +48,22 @@ __device__ int g_specq_trace_cta = 0;
 // Resolve once per kernel (at entry) whether this CTA records, so that each trace point is
 // only a clock read and a store.
 #define SPECQ_TRACE_INIT()                                                                    \
+  const int specq_cta_ = static_cast<int>(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)); \
   unsigned long long* specq_trace_ =                                                         \
-      (static_cast<int>(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)) ==   \
-       ::specq::g_specq_trace_cta)                                                           \
-          ? ::specq::g_specq_trace_buf                                                       \
-          : nullptr
+      (specq_cta_ == ::specq::g_specq_trace_cta) ? ::specq::g_specq_trace_buf : nullptr;    \
+  if (::specq::g_specq_trace_cta < 0 && ::specq::g_specq_trace_buf != nullptr && threadIdx.x == 0 && \
+      specq_cta_ < 2048)                                                                      \
+  ::specq::g_specq_trace_buf[2 * specq_cta_] = ::specq::globaltimer_ns()
 #define SPECQ_TRACE_POINT(slot, iter)                                                         \
   do {                                                                                        \
     if (specq_trace_ != nullptr) specq_trace_[(slot) * 64 + min(static_cast<int>(iter), 63)] = clock64(); \
+  } while (0)
+// All-CTA mode (trace CTA < 0): every CTA records its start and end in %globaltimer ns.
+#define SPECQ_TRACE_CTA_END()                                                                 \
+  do {                                                                                        \
+    if (::specq::g_specq_trace_cta < 0 && ::specq::g_specq_trace_buf != nullptr && threadIdx.x == 0 && \
+        specq_cta_ < 2048)                                                                    \
+      ::specq::g_specq_trace_buf[2 * specq_cta_ + 1] = ::specq::globaltimer_ns();            \
   } while (0)
 #else
 #define SPECQ_TRACE_INIT() \
@@ -63,6 +71,9 @@ __device__ int g_specq_trace_cta = 0;
   } while (0)
 #define SPECQ_TRACE_POINT(slot, iter) \
   do {                                \
+  } while (0)
+#define SPECQ_TRACE_CTA_END() \
+  do {                        \
   } while (0)
 #endif
 

@@ -107,7 +107,7 @@ inline PFN_encodeTiled get_encode_tiled() {
   return fn;
 }
 
-// Encode a tiled tensor map of rank 2 or 3.  dims/strides_bytes/box are innermost first;
+// Encode a tiled tensor map of rank 2 to 4.  dims/strides_bytes/box are innermost first;
 // strides_bytes[i] is the byte stride of dimension i+1.
 inline int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
                         const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,

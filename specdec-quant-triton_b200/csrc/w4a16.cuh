@@ -389,6 +389,7 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) SPECQ_TRACE_POINT(9, 0);
+  SPECQ_TRACE_CTA_END();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_acc, p.tmem_cols);
