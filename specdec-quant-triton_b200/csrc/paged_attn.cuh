@@ -88,16 +88,7 @@ constexpr int kAttnMaxPages = 2048;            // block-table entries of one CTA
 constexpr uint32_t kAttnPTile = 128 * 128;     // fp16 P tile: 128 tokens x 64 query rows
 constexpr float kLazyMaxLog2 = 8.0f;           // rescale once a score exceeds the max by 2^8
 
-// D[tmem] (+)= A[tmem] * B[smem]^T, FP16 -> FP32 (A read from tensor memory).
-__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
+
 
 __device__ __forceinline__ bool named_barrier_or(uint32_t id, uint32_t nthreads, bool v) {
   uint32_t r;

@@ -206,7 +206,6 @@ int run_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const
   }
   p.splits = S;
   p.kb_per_split = ceil_div(p.kb_total, S);
-  p.dstages = 3;
   // Scale tile by TMA when its rows allow it (16-byte aligned, <= 32 KB); otherwise each
   // K-block's two scales per row are prefetched into registers one block ahead.
   const int G = K / group;
@@ -218,25 +217,38 @@ int run_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const
   int smem = 0;
   while (true) {
     p.chunk = round_up(ceil_div(M, n_chunks), 16);
-    p.stage_bytes = kW4A16PackTile + 2u * static_cast<uint32_t>(round_up(p.chunk, 16)) * 128u;
-    const int fixed = 1024 + p.dstages * static_cast<int>(kW4A16DSlot) + sc_bytes + 512 + 64;
+    p.stage_bytes = 2u * static_cast<uint32_t>(round_up(p.chunk, 16)) * 128u;   // activations, lo + hi
+    const int fixed = 1024 + 2 * sc_bytes + 1024;   // + the scale tile and its transpose, barriers
     const uint32_t red_bytes = (S > 1) ? 128u * (static_cast<uint32_t>(p.chunk) * 4u + 16u) : 0u;
-    int stages = std::min(6, (kSmemLimit - fixed) / static_cast<int>(p.stage_bytes));
-    while (stages >= 2 && static_cast<uint32_t>(stages) * p.stage_bytes < red_bytes && stages < 6) ++stages;
-    if (stages >= 2 && static_cast<uint32_t>(stages) * p.stage_bytes >= red_bytes &&
-        fixed + stages * static_cast<int>(p.stage_bytes) <= kSmemLimit) {
-      p.stages = stages;
-      smem = fixed + stages * static_cast<int>(p.stage_bytes);
+    // activation ring 2..6 deep (L2-resident, held until the MMA has read it); the
+    // packed-weight ring (HBM, released as soon as dequant has read it) takes the rest, up
+    // to 16 stages
+    int xs = 6;
+    while (xs > 2 && fixed + xs * static_cast<int>(p.stage_bytes) + 8 * static_cast<int>(kW4A16PackTile) > kSmemLimit) --xs;
+    const int room = kSmemLimit - fixed - xs * static_cast<int>(p.stage_bytes);
+    int ws = std::min(16, room / static_cast<int>(kW4A16PackTile));
+    // the split-K partial tile is parked in the (then idle) rings
+    while (ws < 16 && static_cast<uint32_t>(ws * kW4A16PackTile + xs * p.stage_bytes) < red_bytes &&
+           fixed + (ws + 1) * static_cast<int>(kW4A16PackTile) + xs * static_cast<int>(p.stage_bytes) <= kSmemLimit)
+      ++ws;
+    if (ws >= 2 && static_cast<uint32_t>(ws * kW4A16PackTile + xs * p.stage_bytes) >= red_bytes) {
+      p.stages = ws;
+      p.xstages = xs;
+      smem = fixed + ws * static_cast<int>(kW4A16PackTile) + xs * static_cast<int>(p.stage_bytes);
       break;
     }
     if (p.chunk <= 16) return fail(SPECQ_ERR_UNSUPPORTED, "w4a16: shapes do not fit shared memory");
     ++n_chunks;
   }
-  p.tmem_cols = static_cast<uint32_t>(std::max(32, next_pow2(p.chunk)));
+  // accumulator columns [0, round_up(chunk, 32)), then as many 64-column A slots as fit
+  p.tmem_cols = 512;
+  p.aslots = std::min(kW4A16MaxSlots, (512 - round_up(p.chunk, 32)) / 64);
+  p.a_col = static_cast<uint32_t>(512 - 64 * p.aslots);
 
-  CUtensorMap tw, ta, tsc;
+  CUtensorMap tw, ta, tac, tsc;
   memset(&tw, 0, sizeof(tw));
   memset(&ta, 0, sizeof(ta));
+  memset(&tac, 0, sizeof(tac));
   memset(&tsc, 0, sizeof(tsc));
   if (sc_tma) {
     const uint64_t d[2] = {static_cast<uint64_t>(G), static_cast<uint64_t>(N)};
@@ -248,13 +260,15 @@ int run_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const
     const uint64_t d[2] = {static_cast<uint64_t>(K / 2), static_cast<uint64_t>(N)};
     const uint64_t s_[1] = {static_cast<uint64_t>(ldwp)};
     const uint32_t b[2] = {64, 128};
-    if (int rc = encode_tiled(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, wp, d, s_, b, CU_TENSOR_MAP_SWIZZLE_NONE)) return rc;
+    if (int rc = encode_tiled(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, wp, d, s_, b, CU_TENSOR_MAP_SWIZZLE_64B)) return rc;
   }
   {
     const uint64_t d[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
     const uint64_t s_[1] = {static_cast<uint64_t>(lda) * 2u};
     const uint32_t b[2] = {64, 16};
     if (int rc = encode_tiled(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, d, s_, b, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+    const uint32_t bc[2] = {64, static_cast<uint32_t>(p.chunk)};   // a whole token chunk
+    if (int rc = encode_tiled(&tac, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, d, s_, bc, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
   }
   const dim3 grid(static_cast<unsigned>(S), static_cast<unsigned>(n_tiles), static_cast<unsigned>(n_chunks));
   SPECQ_CUDA_TRY(cudaFuncSetAttribute(w4a16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -270,7 +284,7 @@ int run_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = S > 1 ? 1 : 0;
-  SPECQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, w4a16_kernel, p, tw, ta, tsc));
+  SPECQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, w4a16_kernel, p, tw, ta, tsc, tac));
   LaunchRecord& r = last_launch_ref();
   r.variant = 0;
   r.grid[0] = static_cast<int>(grid.x); r.grid[1] = static_cast<int>(grid.y); r.grid[2] = static_cast<int>(grid.z);

@@ -8,10 +8,13 @@
 //   * Swap-AB as in the W8A8 kernel: tensor-core M=128 over weight channels, N over the
 //     CTA's tokens (up to 256), FP32 accumulators in TMEM.
 //   * Per packed K-block (64 bytes = 64 "low" + 64 "high" K-elements) TMA brings the packed
-//     [128 x 64 B] weight tile and the two matching [tokens x 64] fp16 activation tiles
-//     (128-byte swizzle).  Eight dequant warps turn the packed tile into two fp16 operand
-//     tiles ONCE per K-block for all tokens of the CTA -- the reference redoes this for
-//     every BLOCK_M rows (kernels.py:112-133), which is the cost the rebuild removes.
+//     [128 x 64 B] weight tile (64-byte swizzle) into a deep weight ring and the two matching
+//     [tokens x 64] fp16 activation tiles (128-byte swizzle) into an activation ring.  Each
+//     dequant thread owns one weight row = one TMEM lane: it dequantises the row ONCE per
+//     K-block for all tokens of the CTA (the reference redoes this for every BLOCK_M rows,
+//     kernels.py:112-133) and writes the fp16 weights straight into tensor memory, where the
+//     MMA reads them as its A operand (tcgen05.mma with A in TMEM): the dequantised tile never
+//     passes through shared memory, whose bandwidth would otherwise bound the kernel.
 //   * Dequant = byte-permute + LOP3 into the fp16 exponent 2^10 ("1024 + nibble"), an exact
 //     subtract / fma to q, then one fp16 multiply by the group scale: the same single
 //     rounding as `lo.to(fp16) * sc` in the reference (kernels.py:126-127).
@@ -37,77 +40,80 @@ struct W4A16Params {
   int kb_total;        // packed 64-byte blocks per row = K / 128
   int kb_per_split;
   int splits;
-  int stages;          // TMA ring depth
-  int dstages;         // dequantised-operand ring depth
+  int stages;          // packed-weight ring depth (kW4A16PackTile per stage)
+  int xstages;         // activation ring depth (stage_bytes per stage)
+  int aslots;          // A slots in tensor memory (64 columns each, after the accumulator)
+  uint32_t a_col;      // first TMEM column of the A slots
   uint32_t stage_bytes;
   uint32_t sc_cache_cols;  // groups per row of the TMA-loaded scale tile (0: prefetch per K-block)
   uint32_t tmem_cols;
 };
 
-constexpr int kW4A16DequantWarps = 16;
-constexpr int kW4A16DequantThreads = 32 * kW4A16DequantWarps;
-// The dequant warps form two groups that take alternate K-blocks, so two blocks are being
-// dequantised at any time (a single block's chain of smem load -> convert -> store -> fence
-// is latency-bound).
-constexpr int kW4A16Groups = 2;
-constexpr int kW4A16GroupWarps = kW4A16DequantWarps / kW4A16Groups;
+// Dequant warps form kW4A16Groups groups of four (one warp per TMEM lane quadrant); group g
+// takes the K-blocks i with i % kW4A16Groups == g and writes them into A slots in tensor
+// memory, so several blocks are being dequantised at any time.
+constexpr int kW4A16Groups = 4;
+constexpr int kW4A16GroupWarps = 4;
 constexpr int kW4A16GroupThreads = 32 * kW4A16GroupWarps;
-constexpr int kW4A16Threads = 64 + kW4A16DequantThreads;   // warp 0 TMA, warp 1 MMA, then dequant (2..5 epilogue)
+constexpr int kW4A16DequantWarps = kW4A16Groups * kW4A16GroupWarps;
+constexpr int kW4A16DequantThreads = 32 * kW4A16DequantWarps;
+// warp 0 weight TMA, warp 1 MMA, warps 2.. dequant (2..5 also the epilogue), last warp activation TMA
+constexpr int kW4A16Threads = 64 + kW4A16DequantThreads + 32;
+constexpr int kW4A16ActWarp = kW4A16Threads / 32 - 1;
 constexpr uint32_t kW4A16PackTile = 128 * 64;   // packed bytes per stage
-constexpr uint32_t kW4A16OpTile = 128 * 128;    // one fp16 [128 x 64] operand tile
-constexpr uint32_t kW4A16DSlot = 2 * kW4A16OpTile;
+constexpr int kW4A16MaxSlots = 8;               // A slots of 64 TMEM columns (one K-block each)
 
-// 16 packed bytes (packed columns j..j+15 of one row) -> 16 low-half weights (k = j..j+15)
-// and 16 high-half weights (k = j+K/2 ..), each already multiplied by its fp16 group scale.
-__device__ __forceinline__ void dequant_chunk(uint4 pk, __half2 slo, __half2 shi, uint4 (&lo)[2], uint4 (&hi)[2]) {
+// 16 packed bytes (packed columns j..j+15 of one row) -> 16 fp16 weights of the low half
+// (k = j..j+15, low nibbles) or of the high half (k = K/2 + j.., high nibbles), multiplied by
+// the fp16 group scale, as 8 words of consecutive fp16 pairs.
+__device__ __forceinline__ void dequant_lo16(uint4 pk, __half2 sc, uint32_t (&o)[8]) {
   const uint32_t w[4] = {pk.x, pk.y, pk.z, pk.w};
   const __half2 k1032 = __half2half2(__ushort_as_half(0x6408));       // 1032.0
-  const __half2 k1_16 = __half2half2(__ushort_as_half(0x2C00));       // 0.0625
-  const __half2 km72 = __half2half2(__ushort_as_half(0xD480));        // -72.0
-  uint32_t ol[8], oh[8];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const uint32_t p01 = __byte_perm(w[i], 0u, 0x4140);   // [b0, 0, b1, 0]
-    const uint32_t p23 = __byte_perm(w[i], 0u, 0x4342);   // [b2, 0, b3, 0]
-    const uint32_t l01 = (p01 & 0x000F000Fu) | 0x64006400u;  // fp16 1024 + low nibble
-    const uint32_t l23 = (p23 & 0x000F000Fu) | 0x64006400u;
-    const uint32_t h01 = (p01 & 0x00F000F0u) | 0x64006400u;  // fp16 1024 + 16 * high nibble
-    const uint32_t h23 = (p23 & 0x00F000F0u) | 0x64006400u;
-    __half2 ql01 = __hsub2(*reinterpret_cast<const __half2*>(&l01), k1032);
-    __half2 ql23 = __hsub2(*reinterpret_cast<const __half2*>(&l23), k1032);
-    __half2 qh01 = __hfma2(*reinterpret_cast<const __half2*>(&h01), k1_16, km72);
-    __half2 qh23 = __hfma2(*reinterpret_cast<const __half2*>(&h23), k1_16, km72);
-    ql01 = __hmul2(ql01, slo);
-    ql23 = __hmul2(ql23, slo);
-    qh01 = __hmul2(qh01, shi);
-    qh23 = __hmul2(qh23, shi);
-    ol[2 * i] = *reinterpret_cast<uint32_t*>(&ql01);
-    ol[2 * i + 1] = *reinterpret_cast<uint32_t*>(&ql23);
-    oh[2 * i] = *reinterpret_cast<uint32_t*>(&qh01);
-    oh[2 * i + 1] = *reinterpret_cast<uint32_t*>(&qh23);
+    const uint32_t l01 = (__byte_perm(w[i], 0u, 0x4140) & 0x000F000Fu) | 0x64006400u;  // 1024 + nibble
+    const uint32_t l23 = (__byte_perm(w[i], 0u, 0x4342) & 0x000F000Fu) | 0x64006400u;
+    const __half2 q01 = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&l01), k1032), sc);
+    const __half2 q23 = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&l23), k1032), sc);
+    o[2 * i] = *reinterpret_cast<const uint32_t*>(&q01);
+    o[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&q23);
   }
-  lo[0] = make_uint4(ol[0], ol[1], ol[2], ol[3]);
-  lo[1] = make_uint4(ol[4], ol[5], ol[6], ol[7]);
-  hi[0] = make_uint4(oh[0], oh[1], oh[2], oh[3]);
-  hi[1] = make_uint4(oh[4], oh[5], oh[6], oh[7]);
+}
+__device__ __forceinline__ void dequant_hi16(uint4 pk, __half2 sc, uint32_t (&o)[8]) {
+  const uint32_t w[4] = {pk.x, pk.y, pk.z, pk.w};
+  const __half2 k1_16 = __half2half2(__ushort_as_half(0x2C00));       // 0.0625
+  const __half2 km72 = __half2half2(__ushort_as_half(0xD480));        // -72.0
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t h01 = (__byte_perm(w[i], 0u, 0x4140) & 0x00F000F0u) | 0x64006400u;  // 1024 + 16 nibble
+    const uint32_t h23 = (__byte_perm(w[i], 0u, 0x4342) & 0x00F000F0u) | 0x64006400u;
+    const __half2 q01 = __hmul2(__hfma2(*reinterpret_cast<const __half2*>(&h01), k1_16, km72), sc);
+    const __half2 q23 = __hmul2(__hfma2(*reinterpret_cast<const __half2*>(&h23), k1_16, km72), sc);
+    o[2 * i] = *reinterpret_cast<const uint32_t*>(&q01);
+    o[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&q23);
+  }
 }
 
 __global__ void __launch_bounds__(kW4A16Threads, 1)
     w4a16_kernel(const __grid_constant__ W4A16Params p, const __grid_constant__ CUtensorMap tmap_wp,
-                 const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_sc) {
+                 const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_sc,
+                 const __grid_constant__ CUtensorMap tmap_a_chunk) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   SPECQ_TRACE_INIT();
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ring = smem;                                              // TMA stages
-  uint8_t* dring = ring + p.stages * p.stage_bytes;                  // dequantised operand slots
-  __half* sc_cache = reinterpret_cast<__half*>(dring + p.dstages * kW4A16DSlot);
+  uint8_t* ring = smem;                                              // packed weights [stages][128 x 64 B]
+  uint8_t* xring = ring + p.stages * kW4A16PackTile;                 // activations [xstages][lo | hi]
+  __half* sc_cache = reinterpret_cast<__half*>(xring + p.xstages * p.stage_bytes);   // [128][G] as loaded
+  __half* sc_t = sc_cache + 128u * p.sc_cache_cols;                  // [G][128] transposed
   uint64_t* bars = reinterpret_cast<uint64_t*>(
-      reinterpret_cast<uint8_t*>(sc_cache) + ((128u * p.sc_cache_cols * 2u + 15u) & ~15u));
-  uint64_t* full = bars;
-  uint64_t* empty = full + p.stages;
-  uint64_t* dfull = empty + p.stages;
-  uint64_t* dempty = dfull + p.dstages;
-  uint64_t* acc_full = dempty + p.dstages;
+      reinterpret_cast<uint8_t*>(sc_t) + ((128u * p.sc_cache_cols * 2u + 15u) & ~15u));
+  uint64_t* full = bars;                                             // packed tile landed
+  uint64_t* empty = full + p.stages;                                 // packed tile read by its dequant group
+  uint64_t* xfull = empty + p.stages;                                // activation tile landed
+  uint64_t* xempty = xfull + p.xstages;                              // activation tile read by the MMA
+  uint64_t* afull = xempty + p.xstages;                              // [aslots] A slot written
+  uint64_t* aempty = afull + kW4A16MaxSlots;                         // [aslots] A slot read
+  uint64_t* acc_full = aempty + kW4A16MaxSlots;
   uint64_t* sc_full = acc_full + 1;                                  // scale tile landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sc_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -138,16 +144,26 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
   const int kb0 = split * p.kb_per_split;
   const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
   const int nkb = kb1 - kb0;
+  // Each N tile walks its K range from a different starting block, so the CTAs do not all
+  // read the same activation lines (one set of L2 slices) at the same time.  The order depends
+  // only on the tile, never on M: plan and non-plan launches add the same partial products in
+  // the same order.
+  const int rot = nkb > 0 ? static_cast<int>((static_cast<int64_t>(blockIdx.y) * 5) % nkb) : 0;
+  auto kblock = [&](int i) { return kb0 + (i + rot < nkb ? i + rot : i + rot - nkb); };
   if (threadIdx.x == 0) SPECQ_TRACE_POINT(0, 0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full[s], 1u);
-      mbar_init(&empty[s], kW4A16GroupWarps + 1u);   // the block's dequant group + 1 MMA commit
+      mbar_init(&empty[s], kW4A16GroupWarps);        // the block's dequant group
     }
-    for (int d = 0; d < p.dstages; ++d) {
-      mbar_init(&dfull[d], kW4A16GroupWarps);
-      mbar_init(&dempty[d], 1u);
+    for (int s = 0; s < p.xstages; ++s) {
+      mbar_init(&xfull[s], 1u);
+      mbar_init(&xempty[s], 1u);                     // the MMA commit
+    }
+    for (int d = 0; d < p.aslots; ++d) {
+      mbar_init(&afull[d], kW4A16GroupWarps);        // the dequant group that filled it
+      mbar_init(&aempty[d], 1u);                     // the MMA commit
     }
     mbar_init(acc_full, 1u);
     mbar_init(sc_full, 1u);
@@ -157,6 +173,7 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_wp);
     tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_a_chunk);
     if (p.sc_cache_cols > 0) tma_prefetch_desc(&tmap_sc);
   }
   if (warp == 1) {
@@ -166,17 +183,17 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem_acc = *tmem_slot;
+  const uint32_t tmem_acc = *tmem_slot;             // fp32 accumulator: columns [0, n_pad)
+  const uint32_t tmem_a = tmem_acc + p.a_col;       // A slots: aslots x 64 columns
   if (threadIdx.x == 0) SPECQ_TRACE_POINT(1, 0);
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- weight TMA producer (runs up to `stages` K-blocks ahead) ----------------
     if (elect_one()) {
       const uint64_t pol_w = policy_evict_first();
-      const uint64_t pol_a = policy_evict_last();
       if (p.sc_cache_cols > 0) {   // the CTA's [128 x K/group] fp16 scale tile, once
         mbar_arrive_expect_tx(sc_full, 128u * p.sc_cache_cols * 2u);
-        tma_load_2d(sc_cache, &tmap_sc, sc_full, 0, n0, pol_a);
+        tma_load_2d(sc_cache, &tmap_sc, sc_full, 0, n0, policy_evict_last());
       }
       int issued = 0;
       for (int i = 0; i < nkb; ++i) {
@@ -184,16 +201,8 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
         const uint32_t ph = static_cast<uint32_t>(i / p.stages) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
         SPECQ_TRACE_POINT(2, i);
-        uint8_t* st = ring + s * p.stage_bytes;
-        mbar_arrive_expect_tx(&full[s], kW4A16PackTile + 2u * a_bytes);
-        const int kb = kb0 + i;
-        tma_load_2d(st, &tmap_wp, &full[s], kb * 64, n0, pol_w);
-        uint8_t* alo = st + kW4A16PackTile;
-        uint8_t* ahi = alo + a_bytes;
-        for (int r = 0; r < a_rows; r += 16) {
-          tma_load_2d(alo + r * 128, &tmap_a, &full[s], kb * 64, m0 + r, pol_a);
-          tma_load_2d(ahi + r * 128, &tmap_a, &full[s], half_k + kb * 64, m0 + r, pol_a);
-        }
+        mbar_arrive_expect_tx(&full[s], kW4A16PackTile);
+        tma_load_2d(ring + s * kW4A16PackTile, &tmap_wp, &full[s], kblock(i) * 64, n0, pol_w);   // 64B-swizzled rows
         ++issued;
       }
       if (*abort_flag) {   // let copies in flight land before the CTA can exit
@@ -202,101 +211,132 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
                     SPECQ_STATUS_TIMEOUT_PIPELINE);
       }
     }
+  } else if (warp == kW4A16ActWarp) {
+    // ---------------- activation TMA producer ----------------
+    if (elect_one()) {
+      const uint64_t pol_a = policy_evict_last();
+      int issued = 0;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % p.xstages;
+        const uint32_t ph = static_cast<uint32_t>(i / p.xstages) & 1u;
+        if (!mbar_wait(&xempty[s], ph ^ 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
+        uint8_t* alo = xring + s * p.stage_bytes;
+        uint8_t* ahi = alo + a_bytes;
+        const int kb = kblock(i);
+        mbar_arrive_expect_tx(&xfull[s], 2u * a_bytes);
+        if (a_rows == p.chunk) {   // a full token chunk: one box per K half (TMA issue is serial)
+          tma_load_2d(alo, &tmap_a_chunk, &xfull[s], kb * 64, m0, pol_a);
+          tma_load_2d(ahi, &tmap_a_chunk, &xfull[s], half_k + kb * 64, m0, pol_a);
+        } else {
+          for (int r = 0; r < a_rows; r += 16) {
+            tma_load_2d(alo + r * 128, &tmap_a, &xfull[s], kb * 64, m0 + r, pol_a);
+            tma_load_2d(ahi + r * 128, &tmap_a, &xfull[s], half_k + kb * 64, m0 + r, pol_a);
+          }
+        }
+        ++issued;
+      }
+      if (*abort_flag) {
+        for (int i = max(0, issued - p.xstages); i < issued; ++i)
+          mbar_wait(&xfull[i % p.xstages], static_cast<uint32_t>(i / p.xstages) & 1u, p.status,
+                    SPECQ_STATUS_TIMEOUT_PIPELINE);
+      }
+    }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
+    // A (the dequantised weights) from tensor memory, B (the activations) from shared memory.
     if (elect_one()) {
       const uint32_t idesc = idesc_f16(128, n_pad);
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % p.stages;
-        const int d = i % p.dstages;
-        if (!mbar_wait(&full[s], static_cast<uint32_t>(i / p.stages) & 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE) ||
-            !mbar_wait(&dfull[d], static_cast<uint32_t>(i / p.dstages) & 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) {
+        const int s = i % p.xstages;
+        const int d = i % p.aslots;
+        if (!mbar_wait(&xfull[s], static_cast<uint32_t>(i / p.xstages) & 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE) ||
+            !mbar_wait(&afull[d], static_cast<uint32_t>(i / p.aslots) & 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) {
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
         SPECQ_TRACE_POINT(3, i);
-        const uint32_t alo = smem_u32(ring + s * p.stage_bytes) + kW4A16PackTile;
+        const uint32_t alo = smem_u32(xring + s * p.stage_bytes);
         const uint32_t ahi = alo + a_bytes;
-        const uint32_t wlo = smem_u32(dring + d * kW4A16DSlot);
-        const uint32_t whi = wlo + kW4A16OpTile;
+        const uint32_t wa = tmem_a + 64u * static_cast<uint32_t>(d);
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          umma_f16_ss(tmem_acc, sdesc_sw128(wlo + 32u * k, 16u, 1024u), sdesc_sw128(alo + 32u * k, 16u, 1024u), idesc,
-                      (i > 0 || k > 0) ? 1u : 0u);
+        for (int k = 0; k < 4; ++k)   // 16 low-half K values per step
+          umma_f16_ts(tmem_acc, wa + 8u * k, sdesc_sw128(alo + 32u * k, 16u, 1024u), idesc, (i > 0 || k > 0) ? 1u : 0u);
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          umma_f16_ss(tmem_acc, sdesc_sw128(whi + 32u * k, 16u, 1024u), sdesc_sw128(ahi + 32u * k, 16u, 1024u), idesc,
-                      1u);
-        umma_commit(&empty[s]);
-        umma_commit(&dempty[d]);
+        for (int k = 0; k < 4; ++k)   // 16 high-half K values per step
+          umma_f16_ts(tmem_acc, wa + 32u + 8u * k, sdesc_sw128(ahi + 32u * k, 16u, 1024u), idesc, 1u);
+        umma_commit(&xempty[s]);
+        umma_commit(&aempty[d]);
         SPECQ_TRACE_POINT(4, i);
       }
       umma_commit(acc_full);
     }
   } else {
     // ---------------- dequant warps ----------------
-    const int td = static_cast<int>(threadIdx.x) - 64;   // 0..511
-    const int grp = td / kW4A16GroupThreads;               // K-blocks i with i % 2 == grp
-    const int tg = td % kW4A16GroupThreads;                // 0..255 within the group
-    // this thread dequantises 16-byte chunk (tg & 3) of rows r0 = tg / 4 and r0 + 64
-    const int r0 = tg >> 2;
-    const int c = tg & 3;
+    // Group g (warps 2+4g .. 5+4g, one per TMEM lane quadrant) takes K-blocks i with
+    // i % kW4A16Groups == g; thread = weight row r (its TMEM lane).  It reads the row's 64
+    // packed bytes (64B swizzle: eight consecutive rows hit eight distinct bank groups),
+    // applies the row's two group scales and writes the 128 fp16 weights into A slot
+    // i % aslots.
+    const int td = static_cast<int>(threadIdx.x) - 64;
+    const int grp = td / kW4A16GroupThreads;
+    const uint32_t quad = warp & 3u;
+    const int r = static_cast<int>(quad * 32u + lane);
+    const uint32_t lane_base = (quad * 32u) << 16;
     const int scc = static_cast<int>(p.sc_cache_cols);
-    const int64_t row0 = static_cast<int64_t>(min(n0 + r0, p.N - 1)) * p.ldsc;
-    const int64_t row1 = static_cast<int64_t>(min(n0 + r0 + 64, p.N - 1)) * p.ldsc;
+    const int64_t rowg = static_cast<int64_t>(min(n0 + r, p.N - 1)) * p.ldsc;
     auto group_of = [&](int k) { return p.group_shift >= 0 ? (k >> p.group_shift) : (k / p.group); };
-    auto fetch = [&](int kb, __half (&s4)[4]) {
-      const int glo = group_of(kb * 64);
-      const int ghi = group_of(half_k + kb * 64);
-      if (scc > 0) {
-        s4[0] = sc_cache[r0 * scc + glo];
-        s4[1] = sc_cache[r0 * scc + ghi];
-        s4[2] = sc_cache[(r0 + 64) * scc + glo];
-        s4[3] = sc_cache[(r0 + 64) * scc + ghi];
-      } else {
-        s4[0] = p.sc[row0 + glo];
-        s4[1] = p.sc[row0 + ghi];
-        s4[2] = p.sc[row1 + glo];
-        s4[3] = p.sc[row1 + ghi];
+    if (scc > 0) {
+      if (!mbar_wait(sc_full, 0u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) *abort_flag = 1;
+      // transpose the scale tile once: [g][row] reads are conflict-free in the loop below
+      for (int e = td; e < scc * 128; e += kW4A16DequantThreads) {
+        const int g = e >> 7, rr = e & 127;
+        sc_t[e] = sc_cache[rr * scc + g];
       }
-    };
-    if (scc > 0 && !mbar_wait(sc_full, 0u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) *abort_flag = 1;
+      named_barrier_sync(1, kW4A16DequantThreads);
+    }
     for (int i = grp; i < nkb; i += kW4A16Groups) {
       const int s = i % p.stages;
-      const int d = i % p.dstages;
+      const int d = i % p.aslots;   // more slots than groups when the accumulator is narrow
       if (!mbar_wait(&full[s], static_cast<uint32_t>(i / p.stages) & 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE) ||
-          !mbar_wait(&dempty[d], (static_cast<uint32_t>(i / p.dstages) & 1u) ^ 1u, p.status,
+          !mbar_wait(&aempty[d], (static_cast<uint32_t>(i / p.aslots) & 1u) ^ 1u, p.status,
                      SPECQ_STATUS_TIMEOUT_PIPELINE)) {
         *abort_flag = 1;
         break;
       }
       if (td == 0) SPECQ_TRACE_POINT(10, i);
-      const uint8_t* pk = ring + s * p.stage_bytes;
-      uint8_t* wlo = dring + d * kW4A16DSlot;
-      uint8_t* whi = wlo + kW4A16OpTile;
-      __half sc4[4];
-      fetch(kb0 + i, sc4);
-      const uint4 raw0 = *reinterpret_cast<const uint4*>(pk + tg * 16);           // row r0
-      const uint4 raw1 = *reinterpret_cast<const uint4*>(pk + (tg + 256) * 16);   // row r0 + 64
-      if (td == 0) SPECQ_TRACE_POINT(12, raw0.x == 0x12345678u ? 63 : i);
+      const uint8_t* pk = ring + s * kW4A16PackTile + r * 64;
+      const uint32_t sw = (static_cast<uint32_t>(r) >> 1) & 3u;
+      uint4 raw[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) raw[c] = *reinterpret_cast<const uint4*>(pk + ((static_cast<uint32_t>(c) ^ sw) << 4));
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);    // packed tile consumed (activations: MMA commit)
-      uint4 lo[2], hi[2];
-      dequant_chunk(raw0, __half2half2(sc4[0]), __half2half2(sc4[1]), lo, hi);
-      *reinterpret_cast<uint4*>(wlo + sw128_offset(r0, 2 * c)) = lo[0];
-      *reinterpret_cast<uint4*>(wlo + sw128_offset(r0, 2 * c + 1)) = lo[1];
-      *reinterpret_cast<uint4*>(whi + sw128_offset(r0, 2 * c)) = hi[0];
-      *reinterpret_cast<uint4*>(whi + sw128_offset(r0, 2 * c + 1)) = hi[1];
-      dequant_chunk(raw1, __half2half2(sc4[2]), __half2half2(sc4[3]), lo, hi);
-      *reinterpret_cast<uint4*>(wlo + sw128_offset(r0 + 64, 2 * c)) = lo[0];
-      *reinterpret_cast<uint4*>(wlo + sw128_offset(r0 + 64, 2 * c + 1)) = lo[1];
-      *reinterpret_cast<uint4*>(whi + sw128_offset(r0 + 64, 2 * c)) = hi[0];
-      *reinterpret_cast<uint4*>(whi + sw128_offset(r0 + 64, 2 * c + 1)) = hi[1];
-      if (td == 0) SPECQ_TRACE_POINT(13, i);
-      fence_proxy_async_smem();
+      if (lane == 0) mbar_arrive(&empty[s]);   // the packed tile can be refilled
+      const int kb = kblock(i);
+      const int glo = group_of(kb * 64), ghi = group_of(half_k + kb * 64);
+      const __half slo = scc > 0 ? sc_t[glo * 128 + r] : p.sc[rowg + glo];
+      const __half shi = scc > 0 ? sc_t[ghi * 128 + r] : p.sc[rowg + ghi];
+      const uint32_t wa = tmem_a + lane_base + 64u * static_cast<uint32_t>(d);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {   // the low K half, then the high K half
+        uint32_t w[32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[8];
+          if (half == 0)
+            dequant_lo16(raw[c], __half2half2(slo), o);
+          else
+            dequant_hi16(raw[c], __half2half2(shi), o);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) w[8 * c + k] = o[k];
+        }
+        tmem_st16(wa + 32u * half, *reinterpret_cast<const uint32_t(*)[16]>(w));
+        tmem_st16(wa + 32u * half + 16u, *reinterpret_cast<const uint32_t(*)[16]>(w + 16));
+      }
+      tmem_wait_st();
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&dfull[d]);
+      if (lane == 0) mbar_arrive(&afull[d]);
       if (td == 0) SPECQ_TRACE_POINT(11, i);
     }
   }
