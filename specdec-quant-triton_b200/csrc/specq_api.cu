@@ -242,7 +242,9 @@ int run_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const
   }
   // accumulator columns [0, round_up(chunk, 32)), then as many 64-column A slots as fit
   p.tmem_cols = 512;
-  p.aslots = std::min(kW4A16MaxSlots, (512 - round_up(p.chunk, 32)) / 64);
+  // one A slot per dequant group measured fastest (more slots let the groups run ahead and
+  // compete with each other for issue slots without feeding the MMA any sooner)
+  p.aslots = std::min(kW4A16Groups, (512 - round_up(p.chunk, 32)) / 64);
   p.a_col = static_cast<uint32_t>(512 - 64 * p.aslots);
 
   CUtensorMap tw, ta, tac, tsc;
