@@ -182,9 +182,16 @@ class ClockSampler:
 # workload
 # ----------------------------------------------------------------------------------------------
 def _shard_sizes(world):
-    if 4096 % world or 14336 % world or AT["H_KV"] % world:
-        raise SystemExit(f"--gpus {world}: the step shards 4096/14336 columns and 8 KV heads evenly only")
-    return dict(n8=W8["N"] // world, n4=W4["N"] // world, h_kv=AT["H_KV"] // world, h=AT["H"] // world)
+    """Per-rank sizes of the step under the decomposition of specq.sharding (the same for
+    every rank: the ranges split evenly)."""
+    from specq.sharding import shard_plan
+    try:
+        plan = shard_plan(world, 0, n_w8a8=W8["N"], n_w4a16=W4["N"], h_kv=AT["H_KV"], h=AT["H"])
+    except ValueError as e:
+        raise SystemExit(f"--gpus {world}: {e}")
+    size = lambda s: s.stop - s.start  # noqa: E731
+    return dict(n8=size(plan["w8a8_cols"]), n4=size(plan["w4a16_cols"]), h_kv=size(plan["kv_heads"]),
+                h=size(plan["q_heads"]))
 
 
 def _make_inputs(sh, seed, dev):
