@@ -421,6 +421,11 @@ __device__ __forceinline__ float dsmem_ld_f32(uint32_t cluster_saddr) {
 __device__ __forceinline__ void dsmem_st_f32(uint32_t cluster_saddr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_saddr), "f"(v) : "memory");
 }
+__device__ __forceinline__ void dsmem_st_v4(uint32_t cluster_saddr, uint4 v) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_saddr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
 __device__ __forceinline__ void dsmem_st_v2f32(uint32_t cluster_saddr, float a, float b) {
   asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(cluster_saddr), "f"(a), "f"(b) : "memory");
 }

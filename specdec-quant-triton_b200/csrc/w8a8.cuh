@@ -233,87 +233,64 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
       }
     }
   } else {
-    // Split-K: every CTA parks its INT32 partial tile in its own (now idle) ring buffer,
-    // the cluster synchronises, then CTA r sums rows [r*R, (r+1)*R) over all ranks through
-    // DSMEM and writes them.  All warps take part in both cluster barriers.
+    // Split-K, push model: CTA r owns tile rows [r*R, (r+1)*R).  After a cluster barrier (every
+    // ring idle), each CTA stores the INT32 partial of every row straight into the owner's
+    // shared memory (st.shared::cluster, fire-and-forget), slot [source split][row]; after a
+    // second barrier each CTA sums its own rows locally -- INT32 addition is exact, so the
+    // bits do not depend on the order.  All warps take part in both cluster barriers.
+    const int S = p.splits;
+    const int lgR = 7 - (31 - __clz(S));       // rows owned by one CTA: R = 128 / S
+    const int R = 1 << lgR;
     const uint32_t pitch = n_pad * 4u + 16u;   // padded row pitch: conflict-free v4 access
+    cluster_sync();
+    if (warp == 2 && lane == 0) SPECQ_TRACE_POINT(6, 0);
     if (epi && ok) {
-      uint8_t* red = ring;
+      const uint32_t dst = dsmem_map(smem_u32(ring), static_cast<uint32_t>(row >> lgR)) +
+                           static_cast<uint32_t>(split * R + (row & (R - 1))) * pitch;
       for (uint32_t c0 = 0; c0 < n_pad; c0 += 16) {
         uint32_t r[16];
         tmem_ld16(tmem_acc + ((quad * 32u) << 16) + c0, r);
         tmem_wait_ld();
-        uint4* dst = reinterpret_cast<uint4*>(red + row * pitch + c0 * 4u);
-        dst[0] = make_uint4(r[0], r[1], r[2], r[3]);
-        dst[1] = make_uint4(r[4], r[5], r[6], r[7]);
-        dst[2] = make_uint4(r[8], r[9], r[10], r[11]);
-        dst[3] = make_uint4(r[12], r[13], r[14], r[15]);
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4)
+          dsmem_st_v4(dst + c0 * 4u + 16u * q4, make_uint4(r[4 * q4], r[4 * q4 + 1], r[4 * q4 + 2], r[4 * q4 + 3]));
       }
     }
-    cluster_sync();
-    if (warp == 2 && lane == 0) SPECQ_TRACE_POINT(6, 0);
-    if (epi) {
-      const int S = p.splits;
-      const int lgR = 7 - (31 - __clz(S));       // rows owned by this CTA: R = 128 / S
-      const int R = 1 << lgR;
+    cluster_sync();   // every partial has landed; nothing remote is touched after this
+    if (warp == 2 && lane == 0) SPECQ_TRACE_POINT(7, 0);
+    if (epi && ok) {
       const int nq = static_cast<int>(n_pad >> 2);
       const int te = static_cast<int>(threadIdx.x) - 64;
-      // Up to four items per thread per pass with every peer's load in flight together: one
-      // DSMEM round trip per pass (a pull costs ~1 us here, so passes are what matters).
-      for (int it0 = te; it0 < R * nq; it0 += 512) {
-        int4 acc[4] = {make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0)};
-        uint4 v[4][8];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int item = it0 + u * 128;
-          if (item < R * nq) {
-            const int trow = split * R + (item & (R - 1));
-            const uint4* src = reinterpret_cast<const uint4*>(ring + trow * pitch + (item >> lgR) * 16);
-#pragma unroll
-            for (int pr = 0; pr < 8; ++pr)
-              if (pr < S) v[u][pr] = *dsmem_ptr(src, static_cast<uint32_t>(pr));
-          }
+      for (int item = te; item < R * nq; item += 128) {
+        const int rl = item % R;          // consecutive threads: consecutive rows (pitch-padded)
+        const int cq = item / R;
+        int4 acc = make_int4(0, 0, 0, 0);
+        for (int pr = 0; pr < S; ++pr) {
+          const int4 v = *reinterpret_cast<const int4*>(ring + (pr * R + rl) * pitch + cq * 16);
+          acc.x += v.x;
+          acc.y += v.y;
+          acc.z += v.z;
+          acc.w += v.w;
         }
+        const int n = n0 + split * R + rl;
+        if (n < p.N) {
+          const int32_t sv[4] = {acc.x, acc.y, acc.z, acc.w};
+          const float swn = sw_s[n - n0];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-#pragma unroll
-          for (int pr = 0; pr < 8; ++pr) {
-            if (pr < S && it0 + u * 128 < R * nq) {
-              acc[u].x += static_cast<int32_t>(v[u][pr].x);
-              acc[u].y += static_cast<int32_t>(v[u][pr].y);
-              acc[u].z += static_cast<int32_t>(v[u][pr].z);
-              acc[u].w += static_cast<int32_t>(v[u][pr].w);
-            }
-          }
-        }
-        if (warp == 2 && lane == 0) SPECQ_TRACE_POINT(12, it0 >> 9);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int item = it0 + u * 128;
-          if (item >= R * nq) break;
-          const int cq = item >> lgR;
-          const int n = n0 + split * R + (item & (R - 1));
-          if (ok && n < p.N) {
-            const int32_t sv[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
-            const float swn = sw_s[n - n0];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int m = m0 + cq * 4 + j;
-              if (m < M) {
-                if (p.acc_out != nullptr) {
-                  p.acc_out[static_cast<int64_t>(m) * p.ldacc + n] = sv[j];
-                } else {
-                  const float val = __fmul_rn(__fmul_rn(static_cast<float>(sv[j]), sa_s[m - m0]), swn);
-                  p.out[static_cast<int64_t>(m) * p.ldo + static_cast<int64_t>(n) * p.ldo_n] = __float2half_rn(val);
-                }
+          for (int j = 0; j < 4; ++j) {
+            const int m = m0 + cq * 4 + j;
+            if (m < M) {
+              if (p.acc_out != nullptr) {
+                p.acc_out[static_cast<int64_t>(m) * p.ldacc + n] = sv[j];
+              } else {
+                const float val = __fmul_rn(__fmul_rn(static_cast<float>(sv[j]), sa_s[m - m0]), swn);
+                p.out[static_cast<int64_t>(m) * p.ldo + static_cast<int64_t>(n) * p.ldo_n] = __float2half_rn(val);
               }
             }
           }
         }
       }
     }
-    if (warp == 2 && lane == 0) SPECQ_TRACE_POINT(7, 0);
-    cluster_sync();   // peers may still be reading this CTA's partial tile
     if (warp == 2 && lane == 0) SPECQ_TRACE_POINT(8, 0);
   }
 
