@@ -95,6 +95,8 @@ int specq_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, con
  * `qpp` (queries per program) only changes the schedule: 1 = one query token per CTA,
  * q_len = all k+1 tokens of a GQA group in one CTA (the fused verification kernel).
  * In plan mode, plan[0] = n_seqs and plan[1] = q_len; the grid is (B, ..., ceil(ql_max/qpp)).
+ * q_sb = 0 (o_sb = 0) means packed token rows: sequence b's token t at row b * q_len + t of
+ * a [tokens x ...] tensor, with q_len the active one (a projection's output under a plan graph).
  */
 int specq_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh, const int8_t* kc,
                           const int8_t* vc, int64_t kv_sp, int64_t kv_so, int64_t kv_sh, int n_pages,
@@ -103,6 +105,37 @@ int specq_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_t q_s
                           const int32_t* ctx_len, void* out, int64_t o_sb, int64_t o_st, int64_t o_sh,
                           const int32_t* plan, int B, int n_seqs, int q_len, int ql_max, int H, int H_KV,
                           int D, int page, int qpp, void* stream);
+
+/* Per-token symmetric INT8 quantisation of a verification layer's activations.
+ * No reference counterpart as a kernel: it is the reference's quantize_act_int8
+ * (kernels.py:58-62, a torch function) run on the device, bit-exact:
+ *   s[m] = max(amax_n |y[m, n]|, 1e-8) * fp32(1/127)   (torch's `/ 127.0` on a CUDA tensor)
+ *   q[m, n] = clamp(rint(y[m, n] / s[m]), -127, 127)
+ * with, by `mode`,
+ *   0  y = x                             x fp16 [M, N], row stride ldx
+ *   1  y = x + r, and r <- fp16(x + r)    r fp16 [M, N] (the residual stream), row stride ldr
+ *   2  y = silu(x[:, :N]) * x[:, N:2N]    x fp16 [M, 2N] (an MLP's gate and up halves)
+ * q int8 [M, N] (row stride ldq), s fp32 [M].  plan (optional) = device int32, plan[0] = the
+ * active M; rows past it are not touched.
+ */
+int specq_quant_rows(const void* x, int64_t ldx, void* r, int64_t ldr, int8_t* q, int64_t ldq, float* s,
+                     const int32_t* plan, int M, int N, int mode, void* stream);
+
+/* Append the K and V of the q_len newest tokens of each sequence to an INT8 paged KV cache.
+ * No reference counterpart as a kernel: the reference builds its cache with the fixture
+ * make_paged_kv (kernels.py:265-286); this writes the same format for new tokens.
+ *   x        fp16 [tokens, ...] packed token rows (sequence b's token t at row b*q_len + t),
+ *            row stride ldx; K of KV head h at columns k_col + h*D .., V at v_col + h*D ..
+ *   kc, vc   int8 [P, PAGE, H_KV, D], ks, vs fp16 [P, PAGE, H_KV] (strides as for attention)
+ * Token t of sequence b goes to position ctx_len[b] - q_len + t through the block table, with
+ * per (token, head) scale s = max(amax|k|, 1e-8) / 127 (fp32; stored fp16) and values
+ * clamp(rint(k / s), -127, 127).  In plan mode plan[0] = n_seqs, plan[1] = q_len.
+ */
+int specq_kv_append(const void* x, int64_t ldx, int k_col, int v_col, int8_t* kc, int8_t* vc, int64_t kv_sp,
+                    int64_t kv_so, int64_t kv_sh, int n_pages, void* ks, void* vs, int64_t s_sp, int64_t s_so,
+                    int64_t s_sh, const int32_t* block_tbl, int64_t bt_sb, int bt_cols, const int32_t* ctx_len,
+                    const int32_t* plan, int B, int n_seqs, int q_len, int ql_max, int H_KV, int D, int page,
+                    void* stream);
 
 /*
  * Compiled-kernel metadata for the kernel variant a call with these arguments would launch

@@ -259,6 +259,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (threadIdx.x == 0 && split == 0) report_status(p.status, SPECQ_STATUS_PLAN_CLAMPED);
     L = min(max(L, 0), p.bt_cols * p.page);
   }
+  // A zero sequence stride means packed token rows (sequence b's token t at row
+  // b * q_len + t): the stride follows the active q_len, e.g. a projection's output under a
+  // plan-buffer graph.
+  const int64_t q_sb = p.q_sb != 0 ? p.q_sb : static_cast<int64_t>(q_len) * p.q_st;
+  const int64_t o_sb = p.o_sb != 0 ? p.o_sb : static_cast<int64_t>(q_len) * p.o_st;
   const int q_lo = qc * p.qpp;
   const int q_hi = min(q_lo + p.qpp, q_len);
   const int rows_valid = (q_hi - q_lo) * p.g;
@@ -359,7 +364,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (it < NQ * 8 && row < rows_valid) {
         const int qi = q_lo + (p.g_shift >= 0 ? (row >> p.g_shift) : (row / p.g));
         const int head = kvh * p.g + (p.g_shift >= 0 ? (row & (p.g - 1)) : (row % p.g));
-        const uint4* src = reinterpret_cast<const uint4*>(p.q + b * p.q_sb + static_cast<int64_t>(qi) * p.q_st +
+        const uint4* src = reinterpret_cast<const uint4*>(p.q + b * q_sb + static_cast<int64_t>(qi) * p.q_st +
                                                           static_cast<int64_t>(head) * p.q_sh) + 2 * piece;
         const uint4 u0 = __ldg(src), u1 = __ldg(src + 1);
         const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
@@ -811,7 +816,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const int head = kvh * p.g + (p.g_shift >= 0 ? (q & (p.g - 1)) : (q % p.g));
             const float l = l_s[q];
             const float o = __uint_as_float(r[i]) / (l == 0.f ? 1.f : l);
-            p.out[b * p.o_sb + static_cast<int64_t>(qi) * p.o_st + static_cast<int64_t>(head) * p.o_sh + tl] =
+            p.out[b * o_sb + static_cast<int64_t>(qi) * p.o_st + static_cast<int64_t>(head) * p.o_sh + tl] =
                 __float2half_rn(o);
           }
         }
@@ -901,7 +906,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         const int qi = q_lo + (p.g_shift >= 0 ? (q >> p.g_shift) : (q / p.g));
         const int head = kvh * p.g + (p.g_shift >= 0 ? (q & (p.g - 1)) : (q % p.g));
-        __half* dst = p.out + b * p.o_sb + static_cast<int64_t>(qi) * p.o_st + static_cast<int64_t>(head) * p.o_sh +
+        __half* dst = p.out + b * o_sb + static_cast<int64_t>(qi) * p.o_st + static_cast<int64_t>(head) * p.o_sh +
                       split * (128 / kS) + 8 * d8;
         __half2 h[4];
 #pragma unroll
@@ -1003,7 +1008,7 @@ inline int run_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_
   if (br < 8) return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: page size %d is not a multiple of 8", page);
   p.box_rows = br;
   p.box_shift = __builtin_ctz(static_cast<unsigned>(br));
-  p.out_vec = aligned(out, 16) && o_sb % 8 == 0 && o_st % 8 == 0 && o_sh % 8 == 0;
+  p.out_vec = aligned(out, 16) && o_sb % 8 == 0 && o_st % 8 == 0 && o_sh % 8 == 0;   // o_sb 0: packed rows
   p.kv_sp = kv_sp; p.kv_so = kv_so; p.kv_sh = kv_sh;
   p.qpp = std::min(qpp, 64 / G);                 // QPP only changes the schedule
   p.nq = round_up(p.qpp * G, 16);

@@ -1,0 +1,235 @@
+// rowops.cuh -- the per-token INT8 quantiser and the paged-KV append of a verification layer.
+//
+// quant_rows: dynamic per-token symmetric INT8 of an fp16 row, with the reference's formula
+// (kernels.py:58-62):  s = max(amax|y|, 1e-8) / 127,  q = clamp(rint(y / s), -127, 127),
+// evaluated the way torch evaluates it on a CUDA tensor -- the division by the Python scalar
+// 127 is a multiplication by the fp32 reciprocal 1/127, the division by the scale tensor an
+// IEEE division, round half to even -- so the int8 rows and the fp32 scales equal the
+// reference's bit for bit.  y is one of
+//   mode 0: y = x
+//   mode 1: y = x + r, and the fp16 sum is written back to r (the residual stream)
+//   mode 2: y = silu(g) * u with g = x[:, :N], u = x[:, N:2N]  (the MLP's gate / up halves)
+// One CTA per row; rows >= the plan's M are skipped (plan-buffer graphs).
+//
+// kv_append: the K and V of the q_len newest tokens of each sequence (columns [k_col,
+// k_col + H_KV*D) and [v_col, ..) of a packed [tokens x cols] fp16 projection output, token
+// row b*q_len + t) are quantised per (token, KV head) with the formula the reference's cache
+// fixture uses (kernels.py:280-283: fp32 scale amax/127 -- evaluated as above --, int8
+// values, fp16 stored scale) and
+// written to slot (ctx_len[b] - q_len + t) of the sequence's pages.  One warp per
+// (token, KV head, K or V).
+#pragma once
+
+#include "sm100.cuh"
+#include "specq_host.cuh"
+
+namespace specq {
+
+constexpr int kRowThreads = 256;
+constexpr float kInv127 = 1.0f / 127.0f;   // fp32 reciprocal, as torch forms it for `/ 127.0`
+constexpr int kRowMaxPerThread = 64;   // N up to 256 * 64 = 16384 per row
+
+struct QuantRowsParams {
+  const __half* x;     // [M, N] (mode 2: [M, 2N])
+  __half* r;           // mode 1: residual [M, N], updated in place
+  int8_t* q;           // [M, N]
+  float* s;            // [M]
+  const int32_t* plan; // plan[0] = active M
+  int* status;
+  int64_t ldx, ldr, ldq;
+  int M, N, mode;
+};
+
+__device__ __forceinline__ float silu_f32(float g) { return g / (1.f + expf(-g)); }
+
+template <int PER>
+__global__ void __launch_bounds__(kRowThreads) quant_rows_kernel(const __grid_constant__ QuantRowsParams p) {
+  __shared__ float red[kRowThreads / 32];
+  const int row = blockIdx.x;
+  int M = p.M;
+  if (p.plan != nullptr) {
+    const int pm = __ldg(p.plan);
+    if (pm < 0 || pm > p.M) {
+      if (threadIdx.x == 0 && row == 0) report_status(p.status, SPECQ_STATUS_PLAN_CLAMPED);
+    }
+    M = min(max(pm, 0), p.M);
+  }
+  if (row >= M) return;
+  const __half* x = p.x + static_cast<int64_t>(row) * p.ldx;
+  float y[PER];
+  float amax = 0.f;
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int c = static_cast<int>(threadIdx.x) + k * kRowThreads;
+    float v = 0.f;
+    if (c < p.N) {
+      if (p.mode == 0) {
+        v = __half2float(x[c]);
+      } else if (p.mode == 1) {
+        __half* r = p.r + static_cast<int64_t>(row) * p.ldr;
+        const __half h = __hadd(x[c], r[c]);   // the fp16 residual stream
+        r[c] = h;
+        v = __half2float(h);
+      } else {
+        v = silu_f32(__half2float(x[c])) * __half2float(x[c + p.N]);
+      }
+    }
+    y[k] = v;
+    amax = fmaxf(amax, fabsf(v));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  float m = 0.f;
+#pragma unroll
+  for (int w = 0; w < kRowThreads / 32; ++w) m = fmaxf(m, red[w]);
+  const float s = __fmul_rn(fmaxf(m, 1e-8f), kInv127);
+  int8_t* q = p.q + static_cast<int64_t>(row) * p.ldq;
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int c = static_cast<int>(threadIdx.x) + k * kRowThreads;
+    if (c < p.N) {
+      const float v = fminf(fmaxf(rintf(__fdiv_rn(y[k], s)), -127.f), 127.f);
+      q[c] = static_cast<int8_t>(v);
+    }
+  }
+  if (threadIdx.x == 0) p.s[row] = s;
+}
+
+struct KvAppendParams {
+  const __half* x;       // [M, ld] packed token rows b*q_len + t
+  int8_t* kc;
+  int8_t* vc;
+  __half* ks;
+  __half* vs;
+  const int32_t* bt;
+  const int32_t* ctx_len;
+  const int32_t* plan;   // plan[0] = n_seqs, plan[1] = q_len
+  int* status;
+  int64_t ldx, kv_sp, kv_so, kv_sh, s_sp, s_so, s_sh, bt_sb;
+  int k_col, v_col, n_seqs, q_len, b_grid, ql_max, h_kv, page, n_pages, bt_cols;
+};
+
+__global__ void __launch_bounds__(128) kv_append_kernel(const __grid_constant__ KvAppendParams p) {
+  // blockIdx.x = token slot (b * ql_max + t), warp = (KV head, K|V) pair index
+  const int warp = static_cast<int>(threadIdx.x >> 5);
+  const int lane = static_cast<int>(threadIdx.x & 31);
+  const int item = blockIdx.y * 4 + warp;            // (head, which) pairs, 2 * h_kv of them
+  if (item >= 2 * p.h_kv) return;
+  int n_seqs = p.n_seqs, q_len = p.q_len;
+  if (p.plan != nullptr) {
+    n_seqs = min(max(__ldg(p.plan), 0), p.b_grid);
+    q_len = min(max(__ldg(p.plan + 1), 0), p.ql_max);
+  }
+  const int b = blockIdx.x / p.ql_max;
+  const int t = blockIdx.x % p.ql_max;
+  if (b >= n_seqs || t >= q_len) return;
+  const int head = item >> 1;
+  const bool is_v = item & 1;
+  const int pos = __ldg(p.ctx_len + b) - q_len + t;
+  if (pos < 0 || pos >= p.bt_cols * p.page) {
+    if (lane == 0) report_status(p.status, SPECQ_STATUS_PLAN_CLAMPED);
+    return;
+  }
+  const int pg = __ldg(p.bt + b * p.bt_sb + pos / p.page);
+  if (pg < 0 || pg >= p.n_pages) {
+    if (lane == 0) report_status(p.status, SPECQ_STATUS_PLAN_CLAMPED);
+    return;
+  }
+  const int slot = pos % p.page;
+  // this lane's 4 of the head's 128 values
+  const __half* src = p.x + static_cast<int64_t>(b * q_len + t) * p.ldx + (is_v ? p.v_col : p.k_col) + head * 128 + 4 * lane;
+  const uint2 raw = *reinterpret_cast<const uint2*>(src);
+  const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+  const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+  const float v[4] = {f01.x, f01.y, f23.x, f23.y};
+  float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float s = __fmul_rn(fmaxf(amax, 1e-8f), kInv127);
+  uint32_t packed = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int qv = static_cast<int>(fminf(fmaxf(rintf(__fdiv_rn(v[i], s)), -127.f), 127.f));
+    packed |= (static_cast<uint32_t>(qv) & 0xFFu) << (8 * i);
+  }
+  const int64_t off = static_cast<int64_t>(pg) * p.kv_sp + static_cast<int64_t>(slot) * p.kv_so +
+                      static_cast<int64_t>(head) * p.kv_sh;
+  *reinterpret_cast<uint32_t*>((is_v ? p.vc : p.kc) + off + 4 * lane) = packed;
+  if (lane == 0) {
+    const int64_t so = static_cast<int64_t>(pg) * p.s_sp + static_cast<int64_t>(slot) * p.s_so +
+                       static_cast<int64_t>(head) * p.s_sh;
+    (is_v ? p.vs : p.ks)[so] = __float2half_rn(s);
+  }
+}
+
+inline int run_quant_rows(const void* x, int64_t ldx, void* r, int64_t ldr, int8_t* q, int64_t ldq, float* s,
+                          const int32_t* plan, int M, int N, int mode, void* stream) {
+  if (M < 0 || N <= 0) return fail(SPECQ_ERR_INVALID_ARG, "quant_rows: bad shape M=%d N=%d", M, N);
+  if (mode < 0 || mode > 2) return fail(SPECQ_ERR_INVALID_ARG, "quant_rows: mode %d", mode);
+  if (M == 0) return SPECQ_OK;
+  if (x == nullptr || q == nullptr || s == nullptr || (mode == 1 && r == nullptr))
+    return fail(SPECQ_ERR_INVALID_ARG, "quant_rows: null pointer");
+  if (ldx < (mode == 2 ? 2 * static_cast<int64_t>(N) : N) || ldq < N || (mode == 1 && ldr < N))
+    return fail(SPECQ_ERR_INVALID_ARG, "quant_rows: row strides too small");
+  if (N > kRowThreads * kRowMaxPerThread)
+    return fail(SPECQ_ERR_UNSUPPORTED, "quant_rows: N=%d > %d", N, kRowThreads * kRowMaxPerThread);
+  DeviceState* dev = nullptr;
+  if (int rc = get_device_state(&dev)) return rc;
+  QuantRowsParams p = {};
+  p.x = static_cast<const __half*>(x);
+  p.r = static_cast<__half*>(r);
+  p.q = q;
+  p.s = s;
+  p.plan = plan;
+  p.status = dev->status;
+  p.ldx = ldx; p.ldr = ldr; p.ldq = ldq;
+  p.M = M; p.N = N; p.mode = mode;
+  const int per = ceil_div(N, kRowThreads);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (per <= 8) quant_rows_kernel<8><<<M, kRowThreads, 0, st>>>(p);
+  else if (per <= 16) quant_rows_kernel<16><<<M, kRowThreads, 0, st>>>(p);
+  else if (per <= 32) quant_rows_kernel<32><<<M, kRowThreads, 0, st>>>(p);
+  else quant_rows_kernel<64><<<M, kRowThreads, 0, st>>>(p);
+  SPECQ_CUDA_TRY(cudaGetLastError());
+  return SPECQ_OK;
+}
+
+inline int run_kv_append(const void* x, int64_t ldx, int k_col, int v_col, int8_t* kc, int8_t* vc, int64_t kv_sp,
+                         int64_t kv_so, int64_t kv_sh, int n_pages, void* ks, void* vs, int64_t s_sp, int64_t s_so,
+                         int64_t s_sh, const int32_t* bt, int64_t bt_sb, int bt_cols, const int32_t* ctx_len,
+                         const int32_t* plan, int B, int n_seqs, int q_len, int ql_max, int H_KV, int D, int page,
+                         void* stream) {
+  if (B < 0 || n_seqs < 0 || q_len < 0 || ql_max < 0 || H_KV <= 0 || page <= 0 || n_pages < 0 || bt_cols < 0)
+    return fail(SPECQ_ERR_INVALID_ARG, "kv_append: negative size");
+  if (D != 128) return fail(SPECQ_ERR_UNSUPPORTED, "kv_append: head_dim %d (this build supports 128)", D);
+  if (x == nullptr || kc == nullptr || vc == nullptr || ks == nullptr || vs == nullptr || bt == nullptr ||
+      ctx_len == nullptr)
+    return fail(SPECQ_ERR_INVALID_ARG, "kv_append: null pointer");
+  if (!aligned(x, 8) || ldx % 4 || k_col % 4 || v_col % 4 || !aligned(kc, 4) || !aligned(vc, 4) || kv_sh % 4 ||
+      kv_so % 4 || kv_sp % 4)
+    return fail(SPECQ_ERR_UNSUPPORTED, "kv_append: rows must be 8-byte (x) / 4-byte (cache) aligned");
+  if (plan == nullptr && (n_seqs > B || q_len > ql_max))
+    return fail(SPECQ_ERR_INVALID_ARG, "kv_append: n_seqs/q_len exceed the grid");
+  const int b_grid = plan ? B : n_seqs;
+  const int ql_grid = plan ? ql_max : q_len;
+  if (b_grid == 0 || ql_grid == 0) return SPECQ_OK;
+  DeviceState* dev = nullptr;
+  if (int rc = get_device_state(&dev)) return rc;
+  KvAppendParams p = {};
+  p.x = static_cast<const __half*>(x);
+  p.kc = kc; p.vc = vc;
+  p.ks = static_cast<__half*>(ks); p.vs = static_cast<__half*>(vs);
+  p.bt = bt; p.ctx_len = ctx_len; p.plan = plan; p.status = dev->status;
+  p.ldx = ldx; p.kv_sp = kv_sp; p.kv_so = kv_so; p.kv_sh = kv_sh;
+  p.s_sp = s_sp; p.s_so = s_so; p.s_sh = s_sh; p.bt_sb = bt_sb;
+  p.k_col = k_col; p.v_col = v_col; p.n_seqs = n_seqs; p.q_len = q_len; p.b_grid = b_grid;
+  p.ql_max = ql_grid; p.h_kv = H_KV; p.page = page; p.n_pages = n_pages; p.bt_cols = bt_cols;
+  const dim3 grid(static_cast<unsigned>(b_grid * ql_grid), static_cast<unsigned>(ceil_div(2 * H_KV, 4)));
+  kv_append_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  SPECQ_CUDA_TRY(cudaGetLastError());
+  return SPECQ_OK;
+}
+
+}  // namespace specq

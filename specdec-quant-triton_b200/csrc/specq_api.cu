@@ -9,6 +9,7 @@
 #include "w8a8.cuh"
 #include "w4a16.cuh"
 #include "paged_attn.cuh"
+#include "rowops.cuh"
 
 namespace specq {
 
@@ -362,6 +363,22 @@ int specq_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_t q_s
   return run_paged_attention(q, q_sb, q_st, q_sh, kc, vc, kv_sp, kv_so, kv_sh, n_pages, ks, vs, s_sp, s_so, s_sh,
                              scale_dtype, block_tbl, bt_sb, bt_cols, ctx_len, out, o_sb, o_st, o_sh, plan, B, n_seqs,
                              q_len, ql_max, H, H_KV, D, page, qpp, stream);
+}
+
+int specq_quant_rows(const void* x, int64_t ldx, void* r, int64_t ldr, int8_t* q, int64_t ldq, float* s,
+                     const int32_t* plan, int M, int N, int mode, void* stream) {
+  last_launch_ref() = LaunchRecord();
+  return run_quant_rows(x, ldx, r, ldr, q, ldq, s, plan, M, N, mode, stream);
+}
+
+int specq_kv_append(const void* x, int64_t ldx, int k_col, int v_col, int8_t* kc, int8_t* vc, int64_t kv_sp,
+                    int64_t kv_so, int64_t kv_sh, int n_pages, void* ks, void* vs, int64_t s_sp, int64_t s_so,
+                    int64_t s_sh, const int32_t* block_tbl, int64_t bt_sb, int bt_cols, const int32_t* ctx_len,
+                    const int32_t* plan, int B, int n_seqs, int q_len, int ql_max, int H_KV, int D, int page,
+                    void* stream) {
+  last_launch_ref() = LaunchRecord();
+  return run_kv_append(x, ldx, k_col, v_col, kc, vc, kv_sp, kv_so, kv_sh, n_pages, ks, vs, s_sp, s_so, s_sh,
+                       block_tbl, bt_sb, bt_cols, ctx_len, plan, B, n_seqs, q_len, ql_max, H_KV, D, page, stream);
 }
 
 int specq_kernel_info(int which, int variant, int* num_regs, int* local_bytes, int* static_smem, int* dynamic_smem,

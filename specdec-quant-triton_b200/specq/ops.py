@@ -254,3 +254,84 @@ def paged_attention(q, kc, vc, ks, vs, block_tbl, ctx_len, q_len, QPP=None, BLOC
     ck = KernelHandle(PAGED_ATTN, launch, dict(QPP=QPP, BLOCK_N=BLOCK_N, num_warps=num_warps,
                                                num_stages=num_stages))
     return out, ck
+
+
+# ----------------------------------------------------------------------------------------------
+# Verification-layer glue on the device: per-token INT8 quantisation, paged-KV append and
+# attention over packed token rows.  No reference counterparts as kernels (the reference runs
+# quantize_act_int8 as a torch function and builds its KV cache with a fixture).
+# ----------------------------------------------------------------------------------------------
+QUANT_PLAIN, QUANT_RESIDUAL, QUANT_SILU_MUL = 0, 1, 2
+
+
+def quant_rows(x, mode=QUANT_PLAIN, residual=None, q=None, s=None, plan=None, grid_m_max=None):
+    """Per-token symmetric INT8 of fp16 rows on the device -> (q int8 [M, N], s fp32 [M]).
+
+    mode QUANT_PLAIN: quantise x [M, N] (kernels.py:58-62 bit for bit).
+    mode QUANT_RESIDUAL: residual <- fp16(x + residual), then quantise that sum.
+    mode QUANT_SILU_MUL: quantise silu(x[:, :N]) * x[:, N:] for x [M, 2N].
+    With `plan`, only the first plan[0] rows are computed (a plan-buffer graph)."""
+    if x.dtype != torch.float16 or x.dim() != 2:
+        raise TypeError("quant_rows: x must be a 2-D float16 tensor")
+    _require_cuda(x, residual, q, s)
+    x = _unit_inner(x)
+    M = x.shape[0]
+    N = x.shape[1] // 2 if mode == QUANT_SILU_MUL else x.shape[1]
+    if mode == QUANT_RESIDUAL:
+        if residual is None or residual.shape != (M, N) or residual.dtype != torch.float16 or residual.stride(-1) != 1:
+            raise ValueError("quant_rows: QUANT_RESIDUAL needs a float16 residual [M, N] with unit inner stride")
+    q = torch.empty((M, N), dtype=torch.int8, device=x.device) if q is None else q
+    s = torch.empty((M,), dtype=torch.float32, device=x.device) if s is None else s
+    m_rows = _row_extent(M, plan, grid_m_max, q.shape[0], s.shape[0])
+    lib = _lib.load()
+    _lib.check(lib.specq_quant_rows(x.data_ptr(), x.stride(0), _ptr(residual),
+                                    residual.stride(0) if residual is not None else 0, q.data_ptr(), q.stride(0),
+                                    s.data_ptr(), _plan_ptr(plan), m_rows, N, mode, _stream()))
+    return q, s
+
+
+def kv_append(x, k_col, v_col, kc, vc, ks, vs, block_tbl, ctx_len, q_len, n_seqs=None, plan=None, B=None,
+              ql_max=None):
+    """Write the K/V of the q_len newest tokens of each sequence (packed rows of x, sequence b's
+    token t at row b * q_len + t; K at columns k_col + h*D, V at v_col + h*D) into the INT8
+    paged cache at positions ctx_len[b] - q_len + t (scales fp16, as the reference's cache)."""
+    if x.dtype != torch.float16 or kc.dtype != torch.int8 or vc.dtype != torch.int8:
+        raise TypeError("kv_append: x float16, kc/vc int8")
+    if ks.dtype != torch.float16 or vs.dtype != torch.float16:
+        raise TypeError("kv_append: the cache scales must be float16")
+    _require_cuda(x, kc, vc, ks, vs, block_tbl, ctx_len)
+    B = block_tbl.shape[0] if B is None else B
+    n_seqs = B if n_seqs is None else n_seqs
+    ql_max = q_len if ql_max is None else ql_max
+    lib = _lib.load()
+    _lib.check(lib.specq_kv_append(
+        x.data_ptr(), x.stride(0), k_col, v_col, kc.data_ptr(), vc.data_ptr(), kc.stride(0), kc.stride(1),
+        kc.stride(2), kc.shape[0], ks.data_ptr(), vs.data_ptr(), ks.stride(0), ks.stride(1), ks.stride(2),
+        block_tbl.data_ptr(), block_tbl.stride(0), block_tbl.shape[1], ctx_len.data_ptr(), _plan_ptr(plan),
+        B, n_seqs, q_len, ql_max, kc.shape[2], kc.shape[3], kc.shape[1], _stream()))
+
+
+def paged_attention_packed(x, q_col, out, kc, vc, ks, vs, block_tbl, ctx_len, q_len, H, B=None, ql_max=None,
+                           QPP=None, plan=None, n_seqs=None):
+    """paged_attention with the queries read from, and the result written to, packed token rows:
+    sequence b's token t is row b * q_len + t of x (heads at columns q_col + h*D) and of out
+    (heads at columns h*D), for the active q_len (plan[1] under a plan-buffer graph)."""
+    if x.dtype != torch.float16 or out.dtype != torch.float16:
+        raise TypeError("paged_attention_packed: x and out must be float16")
+    _require_cuda(x, out, kc, vc, ks, vs, block_tbl, ctx_len)
+    H_KV, PAGE, D = kc.shape[2], kc.shape[1], kc.shape[3]
+    B = block_tbl.shape[0] if B is None else B
+    n_seqs = B if n_seqs is None else n_seqs
+    ql_max = q_len if ql_max is None else ql_max
+    QPP = ql_max if QPP is None else QPP
+    scale_dtype = _lib.SPECQ_DTYPE_F16 if ks.dtype == torch.float16 else _lib.SPECQ_DTYPE_F32
+    esz = x.element_size()
+    lib = _lib.load()
+    _lib.check(lib.specq_paged_attention(
+        x.data_ptr() + q_col * esz, 0, x.stride(0), D,
+        kc.data_ptr(), vc.data_ptr(), kc.stride(0), kc.stride(1), kc.stride(2), kc.shape[0],
+        ks.data_ptr(), vs.data_ptr(), ks.stride(0), ks.stride(1), ks.stride(2), scale_dtype,
+        block_tbl.data_ptr(), block_tbl.stride(0), block_tbl.shape[1], ctx_len.data_ptr(),
+        out.data_ptr(), 0, out.stride(0), D,
+        _plan_ptr(plan), B, n_seqs, q_len, ql_max, H, H_KV, D, PAGE, QPP, _stream()))
+    return out
