@@ -97,6 +97,89 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_kernel(const __grid_co
   if (threadIdx.x == 0) p.s[row] = s;
 }
 
+// The same with 16-byte accesses: thread t takes the 8-element chunks t, t + 256, ...
+// (CH of them) -- rows 16-byte aligned, N a multiple of 8.
+template <int CH>
+__global__ void __launch_bounds__(kRowThreads) quant_rows_vec_kernel(const __grid_constant__ QuantRowsParams p) {
+  __shared__ float red[kRowThreads / 32];
+  const int row = blockIdx.x;
+  int M = p.M;
+  if (p.plan != nullptr) {
+    const int pm = __ldg(p.plan);
+    if ((pm < 0 || pm > p.M) && threadIdx.x == 0 && row == 0) report_status(p.status, SPECQ_STATUS_PLAN_CLAMPED);
+    M = min(max(pm, 0), p.M);
+  }
+  if (row >= M) return;
+  const __half* x = p.x + static_cast<int64_t>(row) * p.ldx;
+  float y[CH][8];
+  float amax = 0.f;
+#pragma unroll
+  for (int k = 0; k < CH; ++k) {
+    const int c = (static_cast<int>(threadIdx.x) + k * kRowThreads) * 8;
+    if (c < p.N) {
+      const uint4 a = *reinterpret_cast<const uint4*>(x + c);
+      const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+      if (p.mode == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&aw[i]));
+          y[k][2 * i] = f.x;
+          y[k][2 * i + 1] = f.y;
+        }
+      } else if (p.mode == 1) {
+        __half* r = p.r + static_cast<int64_t>(row) * p.ldr + c;
+        const uint4 b = *reinterpret_cast<const uint4*>(r);
+        const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+        uint32_t hw[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const __half2 h = __hadd2(*reinterpret_cast<const __half2*>(&aw[i]), *reinterpret_cast<const __half2*>(&bw[i]));
+          hw[i] = *reinterpret_cast<const uint32_t*>(&h);
+          const float2 f = __half22float2(h);
+          y[k][2 * i] = f.x;
+          y[k][2 * i + 1] = f.y;
+        }
+        *reinterpret_cast<uint4*>(r) = make_uint4(hw[0], hw[1], hw[2], hw[3]);   // the residual stream
+      } else {
+        const uint4 b = *reinterpret_cast<const uint4*>(x + c + p.N);
+        const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 g = __half22float2(*reinterpret_cast<const __half2*>(&aw[i]));
+          const float2 u = __half22float2(*reinterpret_cast<const __half2*>(&bw[i]));
+          y[k][2 * i] = silu_f32(g.x) * u.x;
+          y[k][2 * i + 1] = silu_f32(g.y) * u.y;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(y[k][i]));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  float m = 0.f;
+#pragma unroll
+  for (int w = 0; w < kRowThreads / 32; ++w) m = fmaxf(m, red[w]);
+  const float s = __fmul_rn(fmaxf(m, 1e-8f), kInv127);
+  int8_t* q = p.q + static_cast<int64_t>(row) * p.ldq;
+#pragma unroll
+  for (int k = 0; k < CH; ++k) {
+    const int c = (static_cast<int>(threadIdx.x) + k * kRowThreads) * 8;
+    if (c < p.N) {
+      uint32_t w[2] = {0u, 0u};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int v = static_cast<int>(fminf(fmaxf(rintf(__fdiv_rn(y[k][i], s)), -127.f), 127.f));
+        w[i >> 2] |= (static_cast<uint32_t>(v) & 0xFFu) << (8 * (i & 3));
+      }
+      *reinterpret_cast<uint2*>(q + c) = make_uint2(w[0], w[1]);
+    }
+  }
+  if (threadIdx.x == 0) p.s[row] = s;
+}
+
 struct KvAppendParams {
   const __half* x;       // [M, ld] packed token rows b*q_len + t
   int8_t* kc;
@@ -186,8 +269,19 @@ inline int run_quant_rows(const void* x, int64_t ldx, void* r, int64_t ldr, int8
   p.status = dev->status;
   p.ldx = ldx; p.ldr = ldr; p.ldq = ldq;
   p.M = M; p.N = N; p.mode = mode;
-  const int per = ceil_div(N, kRowThreads);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool vec = N % 8 == 0 && aligned(x, 16) && ldx % 8 == 0 && aligned(q, 8) && ldq % 8 == 0 &&
+                   (mode != 1 || (aligned(r, 16) && ldr % 8 == 0));
+  if (vec) {
+    const int ch = ceil_div(N, 8 * kRowThreads);
+    if (ch <= 1) quant_rows_vec_kernel<1><<<M, kRowThreads, 0, st>>>(p);
+    else if (ch <= 2) quant_rows_vec_kernel<2><<<M, kRowThreads, 0, st>>>(p);
+    else if (ch <= 4) quant_rows_vec_kernel<4><<<M, kRowThreads, 0, st>>>(p);
+    else quant_rows_vec_kernel<8><<<M, kRowThreads, 0, st>>>(p);
+    SPECQ_CUDA_TRY(cudaGetLastError());
+    return SPECQ_OK;
+  }
+  const int per = ceil_div(N, kRowThreads);
   if (per <= 8) quant_rows_kernel<8><<<M, kRowThreads, 0, st>>>(p);
   else if (per <= 16) quant_rows_kernel<16><<<M, kRowThreads, 0, st>>>(p);
   else if (per <= 32) quant_rows_kernel<32><<<M, kRowThreads, 0, st>>>(p);

@@ -106,6 +106,7 @@ int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int
   if (stages < 2) return fail(SPECQ_ERR_UNSUPPORTED, "w8a8: token chunk %d does not fit shared memory", p.chunk);
   while (static_cast<uint32_t>(stages) * p.stage_bytes < red_bytes && stages < 8) ++stages;
   p.stages = stages;
+  p.ring_bytes = static_cast<uint32_t>(stages) * p.stage_bytes;
   const int smem = overhead + stages * static_cast<int>(p.stage_bytes);
   if (smem > kSmemLimit) return fail(SPECQ_ERR_UNSUPPORTED, "w8a8: shared memory %d > limit", smem);
   p.tmem_cols = static_cast<uint32_t>(std::max(32, next_pow2(p.chunk)));

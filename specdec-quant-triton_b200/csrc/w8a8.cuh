@@ -43,12 +43,14 @@ struct W8A8Params {
   int kb_per_split;    // 128-byte K blocks per split-K CTA
   int splits;          // cluster size along grid.x
   int stages;          // pipeline depth
-  uint32_t stage_bytes;
+  uint32_t stage_bytes;   // of the launch's largest token chunk
+  uint32_t ring_bytes;    // stages * stage_bytes: the ring, re-cut at run time for the active chunk
   uint32_t tmem_cols;
 };
 
 constexpr int kW8A8Threads = 192;  // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue (+ LDG producer)
 constexpr uint32_t kW8A8WTile = 128 * 128;  // bytes of one weight tile
+constexpr int kW8A8MaxStages = 8;
 
 // VEC = 0: TMA producer; VEC in {16, 8, 4, 2, 1}: register-staged loads of that width.
 template <int VEC>
@@ -59,11 +61,11 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
   SPECQ_TRACE_INIT();
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.stages * p.stage_bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.ring_bytes);
   uint64_t* full = bars;
-  uint64_t* empty = bars + p.stages;
-  uint64_t* acc_full = bars + 2 * p.stages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * p.stages + 1);
+  uint64_t* empty = bars + kW8A8MaxStages;
+  uint64_t* acc_full = bars + 2 * kW8A8MaxStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kW8A8MaxStages + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* sa_s = reinterpret_cast<float*>(tmem_slot + 4);      // [256] token scales of this chunk
   float* sw_s = sa_s + 256;                                   // [128] channel scales of this tile
@@ -92,6 +94,11 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
   const uint32_t n_pad = static_cast<uint32_t>((m_cnt + 15) & ~15);   // MMA N
   const int a_rows = (m_cnt + 15) & ~15;                               // TMA boxes of 16 rows
   const uint32_t a_bytes = static_cast<uint32_t>(a_rows) * 128u;
+  // The ring is cut for the ACTIVE chunk: under a plan-buffer graph the launch is sized for
+  // the largest M, and a smaller active M then gets more, smaller stages (more weight bytes
+  // in flight) from the same shared memory.
+  const uint32_t stage_bytes = kW8A8WTile + a_bytes;   // a multiple of 2048: TMA-aligned stages
+  const int stages = min(kW8A8MaxStages, static_cast<int>(p.ring_bytes / stage_bytes));
 
   const int kb0 = split * p.kb_per_split;
   const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
@@ -100,7 +107,7 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
 
   // ---- setup ---------------------------------------------------------------------------
   if (threadIdx.x == 0) {
-    for (int s = 0; s < p.stages; ++s) {
+    for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], VEC == 0 ? 1u : 128u);
       mbar_init(&empty[s], 1u);
     }
@@ -134,11 +141,11 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
       const uint64_t pol_a = policy_evict_last();
       int issued = 0;
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % p.stages;
-        const uint32_t ph = static_cast<uint32_t>(i / p.stages) & 1u;
+        const int s = i % stages;
+        const uint32_t ph = static_cast<uint32_t>(i / stages) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
         SPECQ_TRACE_POINT(2, i);
-        uint8_t* wt = ring + s * p.stage_bytes;
+        uint8_t* wt = ring + s * stage_bytes;
         uint8_t* at = wt + kW8A8WTile;
         mbar_arrive_expect_tx(&full[s], kW8A8WTile + a_bytes);
         const int kx = (kb0 + i) * 128;
@@ -147,8 +154,8 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
         ++issued;
       }
       if (*abort_flag) {   // let copies in flight land before the CTA can exit
-        for (int i = max(0, issued - p.stages); i < issued; ++i)
-          mbar_wait(&full[i % p.stages], static_cast<uint32_t>(i / p.stages) & 1u, p.status,
+        for (int i = max(0, issued - stages); i < issued; ++i)
+          mbar_wait(&full[i % stages], static_cast<uint32_t>(i / stages) & 1u, p.status,
                     SPECQ_STATUS_TIMEOUT_PIPELINE);
       }
     }
@@ -156,12 +163,12 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
     if (elect_one()) {
       const uint32_t idesc = idesc_i8(128, n_pad);
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % p.stages;
-        const uint32_t ph = static_cast<uint32_t>(i / p.stages) & 1u;
+        const int s = i % stages;
+        const uint32_t ph = static_cast<uint32_t>(i / stages) & 1u;
         if (!mbar_wait(&full[s], ph, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
         tc_fence_after();
         SPECQ_TRACE_POINT(3, i);
-        const uint32_t wt = smem_u32(ring + s * p.stage_bytes);
+        const uint32_t wt = smem_u32(ring + s * stage_bytes);
         const uint32_t at = wt + kW8A8WTile;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -181,10 +188,10 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
       const uint8_t* wbase = reinterpret_cast<const uint8_t*>(p.w);
       const uint8_t* abase = reinterpret_cast<const uint8_t*>(p.a);
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % p.stages;
-        const uint32_t ph = static_cast<uint32_t>(i / p.stages) & 1u;
+        const int s = i % stages;
+        const uint32_t ph = static_cast<uint32_t>(i / stages) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
-        uint8_t* wt = ring + s * p.stage_bytes;
+        uint8_t* wt = ring + s * stage_bytes;
         uint8_t* at = wt + kW8A8WTile;
         const int kx = (kb0 + i) * 128;
         ldg_tile_sw128<VEC>(wt, wbase, p.ldw, n0, 128, p.N, kx, p.K, te, 128);
