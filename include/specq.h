@@ -137,6 +137,20 @@ int specq_kv_append(const void* x, int64_t ldx, int k_col, int v_col, int8_t* kc
                     const int32_t* plan, int B, int n_seqs, int q_len, int ql_max, int H_KV, int D, int page,
                     void* stream);
 
+/* Group-wise INT4 weight quantisation and packing on the device.
+ * Replaces the reference's quantize_weight_int4 (kernels.py:138-147, a torch function), bit-exact
+ * with it on a CUDA tensor:
+ *   s[n, g] = max(amax |w[n, g*group ..]|, 1e-8) * fp32(1/7)   (torch's `/ 7.0` on a CUDA tensor)
+ *   q[n, k] = clamp(rint(w[n, k] / s[n, k/group]), -8, 7)
+ *   wp[n, j] = (q[n, j] + 8) | (q[n, j + K/2] + 8) << 4      uint8 [N, K/2], row stride ldwp
+ *   sc[n, g] = fp16(s[n, g])                                 fp16 [N, K/group], row stride ldsc
+ *   deq[n, k] = fp16(q[n, k] * s[n, k/group])                fp16 [N, K] (optional: null skips it)
+ * w: [N, K] with row stride ldw elements, w_dtype 0 = fp16, 1 = fp32, 2 = bf16.
+ * Requires K % 2 == 0 and (K/2) % group == 0 (kernels.py:140); group in {32, 64, 128, 256}.
+ */
+int specq_pack_int4(const void* w, int w_dtype, int64_t ldw, int N, int K, int group, uint8_t* wp, int64_t ldwp,
+                    void* sc, int64_t ldsc, void* deq, int64_t lddeq, void* stream);
+
 /*
  * Compiled-kernel metadata for the kernel variant a call with these arguments would launch
  * (the reference returns Triton's compiled kernel `ck`; regs.py:29-32 reads n_regs,

@@ -29,31 +29,42 @@ def _amax_rows(x: np.ndarray) -> np.ndarray:
     return np.abs(x).max(axis=-1).astype(np.float32)
 
 
-def quantize_act_int8(x: np.ndarray):
-    """Per-token symmetric INT8 (kernels.py:58-62). Returns (q int8 [M,K], s fp32 [M])."""
-    s = np.maximum(_amax_rows(x), np.float32(1e-8)) / np.float32(127.0)
+def _div_scalar(x: np.ndarray, d: float, on_cuda: bool) -> np.ndarray:
+    """`tensor / d` for a Python scalar d, as torch evaluates it: an IEEE fp32 division on a CPU
+    tensor, a multiplication by the fp32 reciprocal fp32(1/d) on a CUDA tensor."""
+    if on_cuda:
+        return (x * np.float32(1.0 / d)).astype(np.float32)
+    return (x / np.float32(d)).astype(np.float32)
+
+
+def quantize_act_int8(x: np.ndarray, on_cuda: bool = False):
+    """Per-token symmetric INT8 (kernels.py:58-62). Returns (q int8 [M,K], s fp32 [M]).
+
+    on_cuda: the scale's division by 127 as torch evaluates it on a GPU tensor."""
+    s = _div_scalar(np.maximum(_amax_rows(x), np.float32(1e-8)), 127.0, on_cuda)
     q = np.rint(x.astype(np.float32) / s[:, None])          # torch.round: half to even
     q = np.clip(q, -127, 127).astype(np.int8)
     return q, s.astype(np.float32)
 
 
-def quantize_weight_int8(w: np.ndarray):
+def quantize_weight_int8(w: np.ndarray, on_cuda: bool = False):
     """Per-output-channel symmetric INT8 (kernels.py:65-68)."""
-    return quantize_act_int8(w)
+    return quantize_act_int8(w, on_cuda)
 
 
-def quantize_weight_int4(w: np.ndarray, group: int = 128):
+def quantize_weight_int4(w: np.ndarray, group: int = 128, on_cuda: bool = False):
     """Group-wise INT4 with split-half packing (kernels.py:138-147).
 
     Returns (packed uint8 [N, K/2], sc fp16 [N, K/group], deq fp16 [N, K]).
     Byte j of row n holds q[n, j] + 8 in its low nibble and q[n, j + K/2] + 8 in its high
     nibble (kernels.py:143-145).  `deq` uses the fp32 scale before the fp16 cast
-    (kernels.py:146), exactly as the reference does.
+    (kernels.py:146), exactly as the reference does.  on_cuda: the division of the group
+    maximum by 7 as torch evaluates it on a GPU tensor.
     """
     n, k = w.shape
     assert k % 2 == 0 and (k // 2) % group == 0
     wg = w.astype(np.float32).reshape(n, k // group, group)
-    sc = np.maximum(np.abs(wg).max(axis=-1), np.float32(1e-8)) / np.float32(7.0)
+    sc = _div_scalar(np.maximum(np.abs(wg).max(axis=-1), np.float32(1e-8)), 7.0, on_cuda)
     q = np.clip(np.rint(wg / sc[..., None]), -8, 7).reshape(n, k).astype(np.int16) + 8
     lo, hi = q[:, : k // 2], q[:, k // 2:]
     packed = (lo | (hi << 4)).astype(np.uint8)

@@ -18,7 +18,19 @@
 // values, fp16 stored scale) and
 // written to slot (ctx_len[b] - q_len + t) of the sequence's pages.  One warp per
 // (token, KV head, K or V).
+//
+// pack_int4: the reference's group-wise INT4 weight quantiser (kernels.py:138-147) on the
+// device: per group of `group` weights s = max(amax|w|, 1e-8) / 7 (fp32, torch's `/ 7.0` on a
+// CUDA tensor: a multiplication by fp32(1/7)), q = clamp(rint(w / s), -8, 7), byte j of row n
+// = (q[n, j] + 8) | (q[n, j + K/2] + 8) << 4, fp16 scales, and optionally the dequantised
+// fp16 copy fp16(q * s).  One warp per (row, low group g, its high partner g + K/(2 group)):
+// lane l takes elements l, l + 32, ... of both groups, so every load and store of the warp is
+// a run of consecutive addresses.
 #pragma once
+
+#include <cuda_bf16.h>
+
+#include <type_traits>
 
 #include "sm100.cuh"
 #include "specq_host.cuh"
@@ -40,7 +52,10 @@ struct QuantRowsParams {
   int M, N, mode;
 };
 
-__device__ __forceinline__ float silu_f32(float g) { return g / (1.f + expf(-g)); }
+// silu(g) = g * sigmoid(g) with the fast exponential and division intrinsics: the fused
+// SiLU-mul mode has no bit-exact counterpart (the reference has no such kernel); its int8
+// output matches torch's silu * mul followed by the quantiser to within one unit.
+__device__ __forceinline__ float silu_f32(float g) { return __fdividef(g, 1.f + __expf(-g)); }
 
 template <int PER>
 __global__ void __launch_bounds__(kRowThreads) quant_rows_kernel(const __grid_constant__ QuantRowsParams p) {
@@ -178,6 +193,139 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_vec_kernel(const __gri
     }
   }
   if (threadIdx.x == 0) p.s[row] = s;
+}
+
+constexpr float kInv7 = 1.0f / 7.0f;   // fp32 reciprocal, as torch forms it for `/ 7.0`
+
+struct PackInt4Params {
+  const void* w;       // [N, K] fp16 / fp32 / bf16 (w_dtype 0 / 1 / 2), row stride ldw elements
+  uint8_t* wp;         // [N, K/2], row stride ldwp bytes
+  __half* sc;          // [N, K/group], row stride ldsc elements
+  __half* deq;         // optional [N, K], row stride lddeq elements
+  int64_t ldw, ldwp, ldsc, lddeq;
+  int N, K, group, w_dtype;
+};
+
+template <typename T>
+__device__ __forceinline__ float weight_to_f32(T v);
+template <>
+__device__ __forceinline__ float weight_to_f32<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float weight_to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float weight_to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// E consecutive elements from src into v: one vector load when VEC (E * sizeof(T) bytes,
+// aligned by the host's check), else E scalar loads.
+template <typename T, int E, bool VEC>
+__device__ __forceinline__ void load_run(const T* src, float (&v)[E]) {
+  if constexpr (VEC && E * sizeof(T) == 16) {
+    const uint4 u = *reinterpret_cast<const uint4*>(src);
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int i = 0; i < E; ++i) v[i] = weight_to_f32<T>(e[i]);
+  } else if constexpr (VEC && E * sizeof(T) == 8) {
+    const uint2 u = *reinterpret_cast<const uint2*>(src);
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int i = 0; i < E; ++i) v[i] = weight_to_f32<T>(e[i]);
+  } else if constexpr (VEC && E * sizeof(T) == 4) {
+    const uint32_t u = *reinterpret_cast<const uint32_t*>(src);
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int i = 0; i < E; ++i) v[i] = weight_to_f32<T>(e[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < E; ++i) v[i] = weight_to_f32<T>(src[i]);
+  }
+}
+
+// Lane l takes the E consecutive elements l*E .. l*E + E-1 of the low group and of the high
+// group, so each warp-wide load / store is one contiguous run.  A warp takes kPackUnits
+// consecutive (row, group pair) units and issues all their loads before any arithmetic:
+// enough bytes in flight per SM to cover the HBM latency.
+constexpr int kPackUnits = 4;
+
+template <typename T, int E, bool VEC>   // E = group / 32
+__global__ void __launch_bounds__(256) pack_int4_kernel(const __grid_constant__ PackInt4Params p) {
+  const int pairs = p.K / (2 * p.group);
+  const int64_t total = static_cast<int64_t>(p.N) * pairs;
+  const int64_t unit0 = (static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * kPackUnits;
+  if (unit0 >= total) return;
+  const int lane = static_cast<int>(threadIdx.x & 31);
+  const int half = p.K / 2;
+  float lo[kPackUnits][E], hi[kPackUnits][E];
+#pragma unroll
+  for (int u = 0; u < kPackUnits; ++u) {
+    const int64_t unit = unit0 + u;
+    if (unit < total) {
+      const int n = static_cast<int>(unit / pairs);
+      const int g = static_cast<int>(unit % pairs);
+      const T* row = static_cast<const T*>(p.w) + static_cast<int64_t>(n) * p.ldw + g * p.group + lane * E;
+      load_run<T, E, VEC>(row, lo[u]);
+      load_run<T, E, VEC>(row + half, hi[u]);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < kPackUnits; ++u) {
+    const int64_t unit = unit0 + u;
+    if (unit >= total) break;
+    const int n = static_cast<int>(unit / pairs);
+    const int g = static_cast<int>(unit % pairs);
+    const int k0 = g * p.group + lane * E;
+    float alo = 0.f, ahi = 0.f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      alo = fmaxf(alo, fabsf(lo[u][i]));
+      ahi = fmaxf(ahi, fabsf(hi[u][i]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      alo = fmaxf(alo, __shfl_xor_sync(0xffffffffu, alo, o));
+      ahi = fmaxf(ahi, __shfl_xor_sync(0xffffffffu, ahi, o));
+    }
+    const float slo = __fmul_rn(fmaxf(alo, 1e-8f), kInv7);
+    const float shi = __fmul_rn(fmaxf(ahi, 1e-8f), kInv7);
+    uint8_t bytes[E];
+    __half dlo[E], dhi[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      const float ql = fminf(fmaxf(rintf(__fdiv_rn(lo[u][i], slo)), -8.f), 7.f);
+      const float qh = fminf(fmaxf(rintf(__fdiv_rn(hi[u][i], shi)), -8.f), 7.f);
+      bytes[i] = static_cast<uint8_t>((static_cast<int>(ql) + 8) | ((static_cast<int>(qh) + 8) << 4));
+      dlo[i] = __float2half_rn(__fmul_rn(ql, slo));
+      dhi[i] = __float2half_rn(__fmul_rn(qh, shi));
+    }
+    uint8_t* wp = p.wp + static_cast<int64_t>(n) * p.ldwp + k0;
+    if constexpr (VEC && E == 4) {
+      *reinterpret_cast<uint32_t*>(wp) = *reinterpret_cast<const uint32_t*>(bytes);
+    } else if constexpr (VEC && E == 8) {
+      *reinterpret_cast<uint2*>(wp) = *reinterpret_cast<const uint2*>(bytes);
+    } else {
+#pragma unroll
+      for (int i = 0; i < E; ++i) wp[i] = bytes[i];
+    }
+    if (p.deq != nullptr) {
+      __half* d = p.deq + static_cast<int64_t>(n) * p.lddeq + k0;
+      if constexpr (VEC && E == 4) {
+        *reinterpret_cast<uint2*>(d) = *reinterpret_cast<const uint2*>(dlo);
+        *reinterpret_cast<uint2*>(d + half) = *reinterpret_cast<const uint2*>(dhi);
+      } else if constexpr (VEC && E == 8) {
+        *reinterpret_cast<uint4*>(d) = *reinterpret_cast<const uint4*>(dlo);
+        *reinterpret_cast<uint4*>(d + half) = *reinterpret_cast<const uint4*>(dhi);
+      } else {
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+          d[i] = dlo[i];
+          d[half + i] = dhi[i];
+        }
+      }
+    }
+    if (lane == 0) {
+      p.sc[static_cast<int64_t>(n) * p.ldsc + g] = __float2half_rn(slo);
+      p.sc[static_cast<int64_t>(n) * p.ldsc + g + pairs] = __float2half_rn(shi);
+    }
+  }
 }
 
 struct KvAppendParams {
@@ -322,6 +470,55 @@ inline int run_kv_append(const void* x, int64_t ldx, int k_col, int v_col, int8_
   p.ql_max = ql_grid; p.h_kv = H_KV; p.page = page; p.n_pages = n_pages; p.bt_cols = bt_cols;
   const dim3 grid(static_cast<unsigned>(b_grid * ql_grid), static_cast<unsigned>(ceil_div(2 * H_KV, 4)));
   kv_append_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  SPECQ_CUDA_TRY(cudaGetLastError());
+  return SPECQ_OK;
+}
+
+inline int run_pack_int4(const void* w, int w_dtype, int64_t ldw, int N, int K, int group, uint8_t* wp, int64_t ldwp,
+                         void* sc, int64_t ldsc, void* deq, int64_t lddeq, void* stream) {
+  if (N < 0 || K < 0 || group <= 0) return fail(SPECQ_ERR_INVALID_ARG, "pack_int4: negative size");
+  if (K % 2 || (K / 2) % group)
+    return fail(SPECQ_ERR_INVALID_ARG, "pack_int4: K=%d needs K %% 2 == 0 and (K/2) %% group == 0 (group %d)", K, group);
+  if (group != 32 && group != 64 && group != 128 && group != 256)
+    return fail(SPECQ_ERR_UNSUPPORTED, "pack_int4: group %d (this build supports 32, 64, 128, 256)", group);
+  if (w_dtype < 0 || w_dtype > 2) return fail(SPECQ_ERR_INVALID_ARG, "pack_int4: weight dtype code %d", w_dtype);
+  if (N == 0 || K == 0) return SPECQ_OK;
+  if (w == nullptr || wp == nullptr || sc == nullptr) return fail(SPECQ_ERR_INVALID_ARG, "pack_int4: null pointer");
+  if (ldw < K || ldwp < K / 2 || ldsc < K / group || (deq != nullptr && lddeq < K))
+    return fail(SPECQ_ERR_INVALID_ARG, "pack_int4: a row stride is shorter than the row");
+  PackInt4Params p = {};
+  p.w = w; p.wp = wp; p.sc = static_cast<__half*>(sc); p.deq = static_cast<__half*>(deq);
+  p.ldw = ldw; p.ldwp = ldwp; p.ldsc = ldsc; p.lddeq = lddeq;
+  p.N = N; p.K = K; p.group = group; p.w_dtype = w_dtype;
+  const int64_t units = static_cast<int64_t>(N) * (K / (2 * group));
+  const int64_t blocks = (units + 8 * kPackUnits - 1) / (8 * kPackUnits);
+  if (blocks > 0x7FFFFFFF) return fail(SPECQ_ERR_INVALID_ARG, "pack_int4: too many groups");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned gx = static_cast<unsigned>(blocks);
+  const int E = group / 32;
+  const int esz = w_dtype == 1 ? 4 : 2;
+  // vector accesses: every run of E elements (weights), E bytes (packed) and E fp16 (deq) aligned
+  const bool vec = E >= 4 && aligned(w, E * esz) && (ldw * esz) % (E * esz) == 0 && aligned(wp, E) && ldwp % E == 0 &&
+                   (deq == nullptr || (aligned(deq, 2 * E) && lddeq % E == 0 && (K / 2) % E == 0));
+  auto launch = [&](auto tag, auto e_tag, auto vec_tag) {
+    using T = decltype(tag);
+    pack_int4_kernel<T, decltype(e_tag)::value, decltype(vec_tag)::value><<<gx, 256, 0, st>>>(p);
+  };
+  auto by_e = [&](auto tag) {
+    using I1 = std::integral_constant<int, 1>;
+    using I2 = std::integral_constant<int, 2>;
+    using I4 = std::integral_constant<int, 4>;
+    using I8 = std::integral_constant<int, 8>;
+    using VT = std::integral_constant<bool, true>;
+    using VF = std::integral_constant<bool, false>;
+    if (E == 1) launch(tag, I1{}, VF{});
+    else if (E == 2) launch(tag, I2{}, VF{});
+    else if (E == 4) vec ? launch(tag, I4{}, VT{}) : launch(tag, I4{}, VF{});
+    else vec ? launch(tag, I8{}, VT{}) : launch(tag, I8{}, VF{});
+  };
+  if (w_dtype == 0) by_e(__half{});
+  else if (w_dtype == 1) by_e(float{});
+  else by_e(__nv_bfloat16{});
   SPECQ_CUDA_TRY(cudaGetLastError());
   return SPECQ_OK;
 }

@@ -382,6 +382,12 @@ int specq_kv_append(const void* x, int64_t ldx, int k_col, int v_col, int8_t* kc
                        block_tbl, bt_sb, bt_cols, ctx_len, plan, B, n_seqs, q_len, ql_max, H_KV, D, page, stream);
 }
 
+int specq_pack_int4(const void* w, int w_dtype, int64_t ldw, int N, int K, int group, uint8_t* wp, int64_t ldwp,
+                    void* sc, int64_t ldsc, void* deq, int64_t lddeq, void* stream) {
+  last_launch_ref() = LaunchRecord();
+  return run_pack_int4(w, w_dtype, ldw, N, K, group, wp, ldwp, sc, ldsc, deq, lddeq, stream);
+}
+
 int specq_kernel_info(int which, int variant, int* num_regs, int* local_bytes, int* static_smem, int* dynamic_smem,
                       int* max_threads) {
   const void* fn = nullptr;

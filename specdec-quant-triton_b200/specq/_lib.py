@@ -43,6 +43,7 @@ SIGNATURES = {
     "specq_paged_attention": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _i64, _i64,
                                      _i64, _i32, _vp, _i64, _i32, _vp, _vp, _i64, _i64, _i64, _vp, _i32, _i32, _i32,
                                      _i32, _i32, _i32, _i32, _i32, _i32, _vp]),
+    "specq_pack_int4": (_i32, [_vp, _i32, _i64, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _i64, _vp]),
     "specq_kernel_info": (_i32, [_i32, _i32, _pi32, _pi32, _pi32, _pi32, _pi32]),
     "specq_last_launch": (_i32, [_pi32, _pi32, _pi32, _pi32, _pi32, _pi32, _pi32]),
     "specq_get_status": (_i32, [_pi32, _i32]),

@@ -335,3 +335,29 @@ def paged_attention_packed(x, q_col, out, kc, vc, ks, vs, block_tbl, ctx_len, q_
         out.data_ptr(), 0, out.stride(0), D,
         _plan_ptr(plan), B, n_seqs, q_len, ql_max, H, H_KV, D, PAGE, QPP, _stream()))
     return out
+
+
+_W_DTYPES = {torch.float16: 0, torch.float32: 1, torch.bfloat16: 2}
+
+
+def pack_int4(w, group=128, deq=True):
+    """Group-wise INT4 quantisation and split-half packing of w [N, K] on the device
+    (kernels.py:138-147, bit-exact with the reference's torch function on a CUDA tensor).
+
+    Returns (packed uint8 [N, K/2], scales fp16 [N, K/group], dequantised fp16 [N, K] or None
+    when deq=False)."""
+    if w.dim() != 2 or w.dtype not in _W_DTYPES:
+        raise TypeError("pack_int4: w must be a 2-D float16 / float32 / bfloat16 tensor")
+    _require_cuda(w)
+    w = _unit_inner(w)
+    N, K = w.shape
+    if K % 2 or (K // 2) % group:
+        raise ValueError(f"pack_int4: K={K} needs K % 2 == 0 and (K/2) % group == 0 (group {group})")
+    wp = torch.empty((N, K // 2), dtype=torch.uint8, device=w.device)
+    sc = torch.empty((N, K // group), dtype=torch.float16, device=w.device)
+    dq = torch.empty((N, K), dtype=torch.float16, device=w.device) if deq else None
+    lib = _lib.load()
+    _lib.check(lib.specq_pack_int4(w.data_ptr(), _W_DTYPES[w.dtype], w.stride(0), N, K, group, wp.data_ptr(),
+                                   wp.stride(0), sc.data_ptr(), sc.stride(0), _ptr(dq),
+                                   dq.stride(0) if dq is not None else 0, _stream()))
+    return wp, sc, dq

@@ -26,6 +26,7 @@ difference between the plan graph and eager execution (0: bit-exact).
 from __future__ import annotations
 
 import argparse
+import os
 import json
 import random
 import time
@@ -225,6 +226,70 @@ def run(layers=4, steps=200, b_max=32, ks=(0, 2, 4, 8), ctx=1024, seed=0, allsha
     return res
 
 
+def _event_us(fn, reps=50):
+    """Mean device time of fn() in µs: `reps` calls captured in one CUDA graph (so the host's
+    launch cost is not what is timed), CUDA events around a replay."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(st):
+        with torch.cuda.graph(graph, stream=st):
+            for _ in range(reps):
+                fn()
+    torch.cuda.current_stream().wait_stream(st)
+    graph.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / reps
+
+
+def measure_rowops(hbm_gbs=None):
+    """Device time and algorithmic bandwidth of the row kernels at the stack's largest shapes:
+    the quantiser (M=288 rows of 4096 / 14336), the KV append (32 sequences x 9 tokens) and
+    the INT4 packer (the W4A16 config's 14336 x 4096 weight).  The quantiser's and the
+    append's inputs fit in L2, so theirs are L2-warm figures; the packer's 117 MB input
+    streams from HBM."""
+    import specq
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    res = {}
+
+    def rec(name, us, nbytes):
+        res[name] = {"us": round(us, 3), "bytes": int(nbytes), "gbs": round(nbytes / us / 1e3, 1)}
+        if hbm_gbs:
+            res[name]["hbm_frac"] = round(nbytes / us / 1e3 / hbm_gbs, 4)
+
+    M = 288
+    for N, mode, name in ((4096, specq.QUANT_PLAIN, "quant_rows_plain_4096"),
+                          (4096, specq.QUANT_RESIDUAL, "quant_rows_residual_4096"),
+                          (14336, specq.QUANT_SILU_MUL, "quant_rows_silu_14336")):
+        x = torch.randn(M, 2 * N if mode == specq.QUANT_SILU_MUL else N, device=dev, generator=g).half()
+        r = torch.randn(M, N, device=dev, generator=g).half() if mode == specq.QUANT_RESIDUAL else None
+        q = torch.empty(M, N, dtype=torch.int8, device=dev)
+        sc = torch.empty(M, device=dev)
+        us = _event_us(lambda: specq.quant_rows(x, mode=mode, residual=r, q=q, s=sc))
+        nbytes = x.numel() * 2 + M * N + 4 * M + (2 * 2 * M * N if r is not None else 0)
+        rec(name, us, nbytes)
+    B, ql, H_KV, D = 32, 9, 8, 128
+    kc, vc, ks, vs, bt, cl = specq.make_paged_kv(B, [1024] * B, H_KV, D, device=dev, seed=1)
+    x = torch.randn(B * ql, (32 + 2 * H_KV) * D, device=dev, generator=g).half()
+    us = _event_us(lambda: specq.kv_append(x, 32 * D, (32 + H_KV) * D, kc, vc, ks, vs, bt, cl, ql))
+    rec("kv_append_b32_q9", us, B * ql * 2 * H_KV * (2 * D + D + 2))
+    w = (torch.randn(14336, 4096, device=dev, generator=g) * 0.02).half()
+    us = _event_us(lambda: specq.pack_int4(w, 128, deq=False), reps=20)
+    rec("pack_int4_14336x4096", us, w.numel() * 2 + w.numel() // 2 + 2 * w.numel() // 128)
+    us = _event_us(lambda: specq.pack_int4(w, 128, deq=True), reps=20)
+    rec("pack_int4_14336x4096_with_deq", us, w.numel() * 4 + w.numel() // 2 + 2 * w.numel() // 128)
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--layers", type=int, default=4)
@@ -234,7 +299,14 @@ def main():
     ap.add_argument("--ctx", type=int, default=1024)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-allshapes", action="store_true")
+    ap.add_argument("--rowops", action="store_true", help="time the row kernels instead of the stack")
     args = ap.parse_args()
+    if args.rowops:
+        peaks = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                             "MEASURED_PEAKS.json")
+        hbm = json.load(open(peaks)).get("hbm_gbs") if os.path.exists(peaks) else None
+        print(json.dumps({"rowops": measure_rowops(hbm), "hbm_gbs_peak": hbm}), flush=True)
+        return
     res = run(layers=args.layers, steps=args.steps, b_max=args.b_max, ks=tuple(int(k) for k in args.ks.split(",")),
               ctx=args.ctx, seed=args.seed, allshapes=not args.no_allshapes)
     print(json.dumps(res), flush=True)

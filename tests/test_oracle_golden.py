@@ -24,6 +24,22 @@ def test_oracle_quantizers_bit_exact(golden):
     assert np.array_equal(q, g["e_q"]) and np.array_equal(s, g["e_s"])
 
 
+def test_oracle_gpu_division_semantics():
+    """on_cuda=True restates torch's GPU evaluation of `tensor / scalar` (a multiplication by
+    the fp32 reciprocal); on_cuda=False its CPU evaluation (an IEEE division)."""
+    rng = np.random.default_rng(0)
+    w = (rng.standard_normal((16, 512)) * 0.05).astype(np.float16)
+    amax = np.abs(w.astype(np.float32).reshape(16, 4, 128)).max(-1)
+    _, sc_gpu, _ = O.quantize_weight_int4(w, 128, on_cuda=True)
+    _, sc_cpu, _ = O.quantize_weight_int4(w, 128)
+    t = torch.from_numpy(amax)
+    assert np.array_equal(sc_gpu, (t * torch.tensor(1.0 / 7.0, dtype=torch.float32)).half().numpy())
+    assert np.array_equal(sc_cpu, (t / 7.0).half().numpy())
+    _, s_gpu = O.quantize_act_int8(w, on_cuda=True)
+    assert np.array_equal(s_gpu, (torch.from_numpy(np.abs(w.astype(np.float32)).max(-1)) *
+                                  torch.tensor(1.0 / 127.0, dtype=torch.float32)).numpy())
+
+
 def test_package_quantizers_bit_exact(golden):
     import specq
     g = golden("quant")

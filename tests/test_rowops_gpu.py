@@ -26,9 +26,12 @@ def test_quant_plain_bit_exact(cuda, M, N):
     rq, rs = _ref_quant(x.float())
     assert torch.equal(s, rs)
     assert torch.equal(q, rq)
-    # the reference's own function on the same fp16 rows
-    fq, fs = specq.quantize_act_int8(x)
+    # the reference's torch function evaluated on the same fp16 rows on the GPU
+    fq, fs = specq.fixtures.quantize_act_int8(x)
     assert torch.equal(q, fq.to(q.device)) and torch.equal(s, fs.to(s.device))
+    # the public drop-in name routes a CUDA fp16 tensor to the kernel
+    pq, ps = specq.quantize_act_int8(x)
+    assert torch.equal(pq, q) and torch.equal(ps, s)
 
 
 def test_quant_zero_row_and_plan(cuda):
