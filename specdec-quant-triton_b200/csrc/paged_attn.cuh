@@ -19,7 +19,7 @@
 //     rows, so one kind::i8 MMA with N = 2*NQ gives both integer partial products exactly in
 //     int32.  Four warps (one thread per token row) dequantise V to fp16 with the token's
 //     scale folded in; the V tile is read MN-major by the PV product.  Per-token scales are
-//     loaded two blocks ahead by the threads that use them.
+//     fetched two blocks ahead by cp.async into shared memory by the threads that use them.
 //   * Softmax runs one thread per token row of S^T (TMEM lane = token): the per-token K scale
 //     and the query scale fold into one per-thread scalar, the running max of each query column
 //     lives in registers; the arithmetic runs on packed fp32 pairs.  The running max is "lazy": a block is exponentiated against the
@@ -27,7 +27,9 @@
 //     the block max, rescale O^T and the normaliser, and recompute.  Blocks that lie wholly
 //     inside every query row's causal window take a mask-free path.  P is written MN-major
 //     (one 16-byte store per 8 query rows).  The normaliser l = sum_t p is produced by the
-//     tensor core itself (a ones operand in TMEM times P).
+//     tensor core itself (a ones operand in TMEM times P).  The score buffers are reset to
+//     their bias by the MMA issuer (tcgen05.cp from shared memory, in order with the MMAs),
+//     so the softmax threads never write tensor memory in the steady state.
 //   * Long contexts are split across a thread-block cluster (a power of two, from the
 //     block-table width only, so plan mode and eager mode give the same bits).  Each CTA
 //     pushes its partial (m, l, O) for the head dims a peer owns into that peer's shared
@@ -143,11 +145,6 @@ __device__ __forceinline__ void store_f16_chunk_pair(uint8_t* tile, int row, int
   }
 }
 
-__device__ __forceinline__ float load_scale(const void* base, int scale_f32, int64_t idx) {
-  return scale_f32 ? __ldg(static_cast<const float*>(base) + idx)
-                   : __half2float(__ldg(static_cast<const __half*>(base) + idx));
-}
-
 // Packed fp32 pairs (sm_100 f32x2 arithmetic: two lanes of work per instruction).
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
   float2 d;
@@ -221,7 +218,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   float* l_s = alpha_s + 64;                                       // [64]
   float* qamax = l_s + 64;                                         // [64] |q| max per query row
   float* wmax = qamax + 64;                                        // [4][64]
-  int* pages_s = reinterpret_cast<int*>(wmax + 256);                // [kAttnMaxPages] this CTA's page ids
+  float* ks_ring = wmax + 256;                                     // [3][256] softmax threads' K scales
+  float* vs_ring = ks_ring + 3 * 256;                              // [3][128] V threads' V scales
+  uint32_t* bias_s = reinterpret_cast<uint32_t*>(vs_ring + 3 * 128); // [256] the score bias, copied into TMEM
+  int* pages_s = reinterpret_cast<int*>(bias_s + 256);             // [kAttnMaxPages] this CTA's page ids
   uint64_t* bars = reinterpret_cast<uint64_t*>(pages_s + kAttnMaxPages);
   uint64_t* stage_full = bars;
   uint64_t* stage_empty = stage_full + kAttnStages;
@@ -305,10 +305,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
            static_cast<int64_t>(kvh) * p.s_sh;
   };
   auto page_ok = [&](int page) { return page >= 0 && page < p.n_pages; };
-  // per-token scale of token row `row` of block j (0 past the split end or on a bad page)
-  auto token_scale = [&](const void* base, int j, int row) -> float {
+  // The per-token scale of token row `row` of block j, fetched by cp.async into *dst two
+  // blocks before it is used (0 past the split end or on a bad page): the consumer reads it
+  // from shared memory, so no register waits on a global load.  fp16 scales: the aligned
+  // 4-byte word holding the value is copied (it never crosses a page, so it is mapped memory)
+  // and bit `slot` of `sel` records which half the value is.
+  auto fetch_scale = [&](const void* base, int j, int row, float* dst, uint32_t& sel, int slot) {
     const int pg = token_page(j, row);
-    return page_ok(pg) ? load_scale(base, p.scale_f32, scale_offset(j, row, pg)) : 0.f;
+    if (page_ok(pg)) {
+      const int64_t off = scale_offset(j, row, pg);
+      if (p.scale_f32) {
+        cp_async4(dst, static_cast<const float*>(base) + off);
+      } else {
+        const uintptr_t a = reinterpret_cast<uintptr_t>(static_cast<const __half*>(base) + off);
+        cp_async4(dst, reinterpret_cast<const void*>(a & ~uintptr_t(3)));
+        sel = (sel & ~(1u << slot)) | (static_cast<uint32_t>((a >> 1) & 1u) << slot);
+      }
+    } else {
+      *dst = 0.f;
+    }
+    cp_async_commit();
+  };
+  auto read_scale = [&](const float* src, uint32_t sel, int slot) -> float {
+    if (p.scale_f32) return *src;
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(src);
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(((sel >> slot) & 1u) ? (w >> 16) : w)));
   };
 
   // ---- setup ---------------------------------------------------------------------------------
@@ -416,19 +437,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       alpha_s[t] = 1.f;
       l_s[t] = 0.f;
     }
-    uint32_t bias8[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) bias8[i] = kScoreBias;
-    // this thread's hi and lo columns of score buffer sb back to the bias
-    auto rebias = [&](uint32_t sb) {
-#pragma unroll
-      for (int c0 = 0; c0 < NQH; c0 += 8) {
-        tmem_st8(lane_base + sb * cs2 + col0 + c0, bias8);
-        tmem_st8(lane_base + sb * cs2 + NQ + col0 + c0, bias8);
-      }
-    };
-    rebias(0u);
-    rebias(1u);
+    // the constant the MMA issuer copies into a score buffer before each QK (tcgen05.cp)
+    bias_s[t] = kScoreBias;
     {   // ones operand of the normaliser MMA: fp16 1.0 pairs, 8 columns per 16-token K-step
       uint32_t ones[16];
 #pragma unroll
@@ -450,20 +460,27 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
     // Multi-thread roles never leave a loop early: after a wait runs out (ok = false) they skip
     // the remaining waits but still reach every named barrier, so no warp is stranded.
-    // Block j; `ksr` holds this token's K scale of block j (loaded two blocks ago) and is
-    // reloaded with that of block j + 2.  The loop runs in pairs with two scale registers, so
-    // a loaded value is used where it lies (a register copy would wait for the load).
-    auto soft_block = [&](int j, float& ksr) {
+    // One copy of the block body (a plain loop, not unrolled): the softmax, V and MMA roles
+    // share each scheduler's instruction cache, so the hot code is kept small.
+    float* ksd = ks_ring + t;     // this thread's K-scale slots (stride 256)
+    uint32_t ksel = 0u;
+    fetch_scale(p.ks, 0, tl, ksd, ksel, 0);
+    fetch_scale(p.ks, 1, tl, ksd + 256, ksel, 1);
+    int slot = 0;                 // j % 3
+#pragma unroll 1
+    for (int j = 0; j < nblk; ++j) {
+      const int slot2 = slot == 0 ? 2 : slot - 1;   // (j + 2) % 3
+      fetch_scale(p.ks, j + 2, tl, ksd + 256 * slot2, ksel, slot2);
       const int t_abs = t_begin + j * 128 + tl;
       const uint32_t sb = static_cast<uint32_t>(j & 1);
       const uint32_t par2 = static_cast<uint32_t>(j >> 1) & 1u;
       // query rows q >= q_first may see this token (causal window), rows >= q_stop never do
       const int q_stop = (t_abs < t_end) ? rows_valid : 0;
       const int q_first = min(max(0, (t_abs - qpos0) * p.g), q_stop);
-      // this token's score scale: K scale x log2(e) / sqrt(D) x the query scale
-      const float a_t = ksr * p.sm_scale_log2 * q_scale;
-      ksr = token_scale(p.ks, j + 2, tl);
       if (t == 0) SPECQ_TRACE_POINT(20, j);
+      cp_async_wait<2>();   // block j's scale (fetched two blocks ago) has landed
+      // this token's score scale: K scale x log2(e) / sqrt(D) x the query scale
+      const float a_t = read_scale(ksd + 256 * slot, ksel, slot) * p.sm_scale_log2 * q_scale;
       ok = ok && mbar_wait(&s_full[sb], par2, status, SPECQ_STATUS_TIMEOUT_MMA);
       // P buffer sb is free once PV(j-2) has read it
       if (j >= 2) ok = ok && mbar_wait(&pv_done[sb], par2 ^ 1u, status, SPECQ_STATUS_TIMEOUT_MMA);
@@ -480,8 +497,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       auto score = [&](uint32_t hb, uint32_t lb) {
         return (fmaf(__uint_as_float(hb), 256.f, __uint_as_float(lb)) - kScoreBias257) * a_t;
       };
-      // one optimistic pass: P against the current max, noting whether any score exceeds it
-      // by more than 2^8 (then the block is redone below with a raised max)
+      // One pass: P against the current max, noting the largest exponent.
       auto write_p = [&](float& xmax) {
 #pragma unroll
         for (int c0 = 0; c0 < NQH; c0 += 16) {   // 16 columns per TMEM round trip (hi and lo)
@@ -522,11 +538,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
       };
-      float xmax = -INFINITY;
-      write_p(xmax);
-      const bool need = named_barrier_or(2, 256, xmax > kLazyMaxLog2);
-      if (t == 0) SPECQ_TRACE_POINT(22, j);
-      if (need) {
+#pragma unroll
+      for (int pass = 0; pass < 2; ++pass) {   // two straight-line copies: faster than a loop
+        float xmax = -INFINITY;
+        write_p(xmax);
+        if (pass == 1) break;
+        const bool need = named_barrier_or(2, 256, xmax > kLazyMaxLog2);
+        if (t == 0) SPECQ_TRACE_POINT(22, j);
+        if (!need) break;
+        // ---- rescale: some score exceeds the running max by more than 2^8 ----
         if (t == 0) SPECQ_TRACE_POINT(26, j);
         // the running O^T / normaliser must be final before they are rescaled
         if (j >= 1)
@@ -580,25 +600,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
           tmem_wait_st();
         }
-        float unused = -INFINITY;
-        write_p(unused);
       }
-      rebias(sb);            // the next QK into this buffer accumulates onto the bias
-      tmem_wait_st();
+      // P(j) is complete and score buffer sb has been read for the last time
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&s_empty[sb]);
         mbar_arrive(&p_full[sb]);
+        mbar_arrive(&s_empty[sb]);
       }
       if (t == 0) SPECQ_TRACE_POINT(24, j);
-    };
-    float ks_even = token_scale(p.ks, 0, tl), ks_odd = token_scale(p.ks, 1, tl);
-    for (int j = 0; j < nblk; j += 2) {
-      soft_block(j, ks_even);
-      if (j + 1 < nblk) soft_block(j + 1, ks_odd);
+      slot = slot == 2 ? 0 : slot + 1;
     }
+    cp_async_wait<0>();
     // ---- final normaliser and accumulator ----
     if (nblk > 0) {
       // bounded even after a failure: the tensor core must be idle before TMEM is freed
@@ -676,17 +690,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const uint32_t id_pv = idesc_f16(128, static_cast<uint32_t>(NQ), 1u, 1u);
       const uint32_t id_l = idesc_f16(128, static_cast<uint32_t>(NQ), 0u, 1u);
       const uint32_t ring_a = smem_u32(ring), vop_a = smem_u32(vop), qop_a = smem_u32(qop), pop_a = smem_u32(pop);
+      // 32 rows x 16 B of the constant bias, core matrices 128 B apart: 512 B of bias_s
+      const uint64_t bias_desc = sdesc_plain(smem_u32(bias_s), 128u, 128u);
       auto issue_qk = [&](int j, int s) {
         const uint32_t sb = static_cast<uint32_t>(j & 1);
         fence_proxy_async_smem();   // the K bytes were written by cp.async (generic proxy)
         tc_fence_after();
         SPECQ_TRACE_POINT(30, j);
         const uint32_t ka = ring_a + static_cast<uint32_t>(s) * kAttnStage;
+        // score buffer sb <- the bias (all 2*NQ hi / lo columns, 4 per copy); the MMAs below
+        // run after the copies (same issuing thread) and accumulate onto it
+#pragma unroll
+        for (int c = 0; c < 2 * NQ; c += 4) tmem_cp_32x128b_x4(tmem + sb * cs2 + static_cast<uint32_t>(c), bias_desc);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {   // 32 of the 128 head dims per step
           const uint64_t ak = sdesc_sw128(ka + k * 32u, 16u, 1024u);
           const uint64_t bq = sdesc_sw128(qop_a + k * 32u, 16u, 1024u);
-          umma_i8_ss(tmem + sb * cs2, ak, bq, id_qk, 1u);   // onto the bias the softmax left
+          umma_i8_ss(tmem + sb * cs2, ak, bq, id_qk, 1u);   // onto the copied bias
         }
         umma_commit(&s_full[sb]);
         umma_commit(&stage_empty[s]);   // the K tile is consumed
@@ -709,9 +729,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         umma_commit(&pv_done[bi]);
         SPECQ_TRACE_POINT(33, i);
       };
-      // Fixed issue order QK(0), QK(1), then per block i: QK(i+2), PV(i).  Both wait for the
-      // softmax to finish block i (its S buffer, its P tile), so neither delays the other; the
-      // blocking waits keep this thread off the issue slots the softmax warps need.
+      // Fixed issue order QK(0), QK(1), then per block i: PV(i) and QK(i+2), both as soon as the
+      // softmax has finished block i (its P tile, its score buffer).  The blocking waits keep
+      // this thread off the issue slots the softmax warps need.
       int qk_stage = 0;
       uint32_t qk_phase = 0;
       auto qk = [&](int j) {
@@ -728,12 +748,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (nblk > 0) ok = mbar_wait(q_full, 0u, status, SPECQ_STATUS_TIMEOUT_PIPELINE);
       for (int j = 0; ok && j < min(2, nblk); ++j) ok = qk(j);
       for (int i = 0; ok && i < nblk; ++i) {
-        if (i + 2 < nblk) ok = qk(i + 2);
         const uint32_t bi = static_cast<uint32_t>(i & 1);
         const uint32_t par = static_cast<uint32_t>(i >> 1) & 1u;
-        ok = ok && mbar_wait(&p_full[bi], par, status, SPECQ_STATUS_TIMEOUT_MMA) &&
+        ok = mbar_wait(&p_full[bi], par, status, SPECQ_STATUS_TIMEOUT_MMA) &&
              mbar_wait(&v_full[bi], par, status, SPECQ_STATUS_TIMEOUT_PIPELINE);
         if (ok) issue_pv(i);
+        if (ok && i + 2 < nblk) ok = qk(i + 2);
       }
     }
   } else {
@@ -742,24 +762,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // (128B-swizzled, so eight consecutive rows hit eight distinct bank groups), converts them
     // to fp16 with the token's V scale folded in and stores the row into the V operand tile.
     const int c = static_cast<int>(threadIdx.x) - 32 * (kAttnMmaWarp + 1);   // 0..127
-    // block j; `vsr` holds this token's V scale of block j (loaded two blocks ago) and is
-    // reloaded with that of block j + 2 (pairs of blocks with two registers: no copies)
-    auto step = [&](int j, float& vsr) {
+    float* vsd = vs_ring + c;     // this thread's V-scale slots (stride 128)
+    uint32_t vsel = 0u;
+    fetch_scale(p.vs, 0, c, vsd, vsel, 0);
+    fetch_scale(p.vs, 1, c, vsd + 128, vsel, 1);
+    int slot = 0;                 // j % 3
+#pragma unroll 1
+    for (int j = 0; j < nblk; ++j) {
+      const int slot2 = slot == 0 ? 2 : slot - 1;   // (j + 2) % 3
+      fetch_scale(p.vs, j + 2, c, vsd + 128 * slot2, vsel, slot2);
       const int s = j % kAttnStages;
       const uint32_t sb = static_cast<uint32_t>(j & 1);
       const uint32_t par2 = static_cast<uint32_t>(j >> 1) & 1u;
       ok = ok && mbar_wait(&stage_full[s], static_cast<uint32_t>(j / kAttnStages) & 1u, status,
                            SPECQ_STATUS_TIMEOUT_PIPELINE);
       if (c == 0) SPECQ_TRACE_POINT(40, j);
-      // the token's V scale in fp16 (exact for fp16 scales; one rounding for fp32 scales), so
-      // the per-element multiply stays on the fp16 pipe
-      const __half2 s2 = __half2half2(__float2half_rn(vsr));
-      vsr = token_scale(p.vs, j + 2, c);
       const uint8_t* vrow = ring + s * kAttnStage + kAttnKV8 + c * 128;
       uint4 raw[8];
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch)
         raw[ch] = *reinterpret_cast<const uint4*>(vrow + ((static_cast<uint32_t>(ch) ^ (static_cast<uint32_t>(c) & 7u)) << 4));
+      cp_async_wait<2>();   // block j's scale (fetched two blocks ago) has landed
+      // the token's V scale in fp16 (exact for fp16 scales; one rounding for fp32 scales), so
+      // the per-element multiply stays on the fp16 pipe
+      const __half2 s2 = __half2half2(__float2half_rn(read_scale(vsd + 128 * slot, vsel, slot)));
       // V buffer sb is free once PV(j-2) has completed
       if (j >= 2) ok = ok && mbar_wait(&pv_done[sb], par2 ^ 1u, status, SPECQ_STATUS_TIMEOUT_MMA);
       uint8_t* vdst = vop + sb * kAttnOp;
@@ -781,12 +807,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         mbar_arrive(&stage_empty[s]);   // the V half of the stage is consumed
       }
       if (c == 0) SPECQ_TRACE_POINT(45, j);
-    };
-    float vs_even = token_scale(p.vs, 0, c), vs_odd = token_scale(p.vs, 1, c);
-    for (int j = 0; j < nblk; j += 2) {
-      step(j, vs_even);
-      if (j + 1 < nblk) step(j + 1, vs_odd);
+      slot = slot == 2 ? 0 : slot + 1;
     }
+    cp_async_wait<0>();
   }
   __syncwarp();
 
@@ -1037,7 +1060,8 @@ inline int run_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_
 
   // K ring + two fp16 V tiles + int8 Q (hi, lo) + two P tiles + softmax state + barriers
   const int smem = 1024 + p.stages * static_cast<int>(kAttnStage) + 2 * static_cast<int>(kAttnOp) +
-                   p.nq * 256 + 2 * static_cast<int>(kAttnPTile) + 4096 + kAttnMaxPages * 4 +
+                   p.nq * 256 + 2 * static_cast<int>(kAttnPTile) + 4096 + (3 * 256 + 3 * 128 + 256) * 4 +
+                   kAttnMaxPages * 4 +
                    (2 * p.stages + 17) * 8 + 16;
   if (smem > 232448) return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: shared memory %d too large", smem);
   if ((p.nq * 128 + 3 * p.splits * p.nq) * 4 > p.stages * static_cast<int>(kAttnStage))

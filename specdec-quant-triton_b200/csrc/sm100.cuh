@@ -173,6 +173,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   }
 }
 
+// 4-byte cp.async global -> shared (4- and 8-byte copies take the L1-allocating .ca form).
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// wait until at most N of this thread's committed cp.async groups are still in flight
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Arrive on an mbarrier when all of this thread's earlier cp.async copies have landed.
 __device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -316,6 +327,24 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, ui
   d |= static_cast<uint64_t>(1) << 46;  // descriptor version for sm_100
   d |= static_cast<uint64_t>(2) << 61;  // SWIZZLE_128B
   return d;
+}
+
+// Shared-memory matrix descriptor, no swizzle (8-row x 16-byte core matrices; `lbo` / `sbo`
+// the byte distances between core matrices along K / along M-N).
+__device__ __forceinline__ uint64_t sdesc_plain(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;  // descriptor version for sm_100; layout 0 = no swizzle
+  return d;
+}
+
+// Shared memory -> TMEM copy, asynchronous like tcgen05.mma and executed in issue order with
+// the MMAs of the same thread: a 32-row x 128-bit matrix written to 4 columns of all four
+// 32-lane quadrants.
+__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
 
 // Byte offset of the 16-byte chunk `chunk` (0..7) of row `row` inside a 128-byte-swizzled
