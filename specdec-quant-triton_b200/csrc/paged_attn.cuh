@@ -692,22 +692,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const uint32_t ring_a = smem_u32(ring), vop_a = smem_u32(vop), qop_a = smem_u32(qop), pop_a = smem_u32(pop);
       // 32 rows x 16 B of the constant bias, core matrices 128 B apart: 512 B of bias_s
       const uint64_t bias_desc = sdesc_plain(smem_u32(bias_s), 128u, 128u);
+      // Operand descriptors: one precomputed descriptor per tile, advanced by adding address
+      // offsets in 16-byte units (this thread shares a scheduler with busy softmax and V warps,
+      // so its per-block instruction count is kept small).
+      const uint64_t kdesc0 = sdesc_sw128(ring_a, 16u, 1024u);
+      const uint64_t qdesc0 = sdesc_sw128(qop_a, 16u, 1024u);
+      const uint64_t vdesc0 = sdesc_sw128(vop_a, 16384u, 1024u);
+      const uint64_t pdesc0 = sdesc_sw128(pop_a, 16384u, 1024u);
       auto issue_qk = [&](int j, int s) {
         const uint32_t sb = static_cast<uint32_t>(j & 1);
-        fence_proxy_async_smem();   // the K bytes were written by cp.async (generic proxy)
         tc_fence_after();
         SPECQ_TRACE_POINT(30, j);
-        const uint32_t ka = ring_a + static_cast<uint32_t>(s) * kAttnStage;
+        const uint64_t kd = kdesc0 + ((static_cast<uint32_t>(s) * kAttnStage) >> 4);
         // score buffer sb <- the bias (all 2*NQ hi / lo columns, 4 per copy); the MMAs below
         // run after the copies (same issuing thread) and accumulate onto it
 #pragma unroll
         for (int c = 0; c < 2 * NQ; c += 4) tmem_cp_32x128b_x4(tmem + sb * cs2 + static_cast<uint32_t>(c), bias_desc);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {   // 32 of the 128 head dims per step
-          const uint64_t ak = sdesc_sw128(ka + k * 32u, 16u, 1024u);
-          const uint64_t bq = sdesc_sw128(qop_a + k * 32u, 16u, 1024u);
-          umma_i8_ss(tmem + sb * cs2, ak, bq, id_qk, 1u);   // onto the copied bias
-        }
+        for (int k = 0; k < 4; ++k)   // 32 of the 128 head dims (32 bytes) per step
+          umma_i8_ss(tmem + sb * cs2, kd + 2u * k, qdesc0 + 2u * k, id_qk, 1u);   // onto the copied bias
         umma_commit(&s_full[sb]);
         umma_commit(&stage_empty[s]);   // the K tile is consumed
         SPECQ_TRACE_POINT(31, j);
@@ -716,12 +719,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t bi = static_cast<uint32_t>(i & 1);
         tc_fence_after();
         SPECQ_TRACE_POINT(32, i);
-        const uint32_t vb = vop_a + bi * kAttnOp;
-        const uint32_t pb = pop_a + bi * kAttnPTile;
+        const uint64_t vd = vdesc0 + ((bi * kAttnOp) >> 4);
+        const uint64_t pd = pdesc0 + ((bi * kAttnPTile) >> 4);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {   // 16 tokens per step
-          const uint64_t av = sdesc_sw128(vb + k * 2048u, 16384u, 1024u);
-          const uint64_t bp = sdesc_sw128(pb + k * 2048u, 16384u, 1024u);
+        for (int k = 0; k < 8; ++k) {   // 16 tokens (two 1024-byte atoms) per step
+          const uint64_t av = vd + 128u * k;
+          const uint64_t bp = pd + 128u * k;
           const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
           umma_f16_ss(tmem + O_col, av, bp, id_pv, acc);
           umma_f16_ts(tmem + L_col, tmem + ONES_col + 8u * k, bp, id_l, acc);

@@ -247,6 +247,8 @@ int run_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const
   // one A slot per dequant group measured fastest (more slots let the groups run ahead and
   // compete with each other for issue slots without feeding the MMA any sooner)
   p.aslots = std::min(kW4A16Groups, (512 - round_up(p.chunk, 32)) / 64);
+  if (p.aslots != kW4A16Groups)   // the dequant group g always fills A slot g
+    return fail(SPECQ_ERR_UNSUPPORTED, "w4a16: token chunk %d leaves %d TMEM A slots", p.chunk, p.aslots);
   p.a_col = static_cast<uint32_t>(512 - 64 * p.aslots);
 
   CUtensorMap tw, ta, tac, tsc;

@@ -196,14 +196,18 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
         tma_load_2d(sc_cache, &tmap_sc, sc_full, 0, n0, policy_evict_last());
       }
       int issued = 0;
+      int s = 0;
+      uint32_t ph = 0;
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % p.stages;
-        const uint32_t ph = static_cast<uint32_t>(i / p.stages) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
         SPECQ_TRACE_POINT(2, i);
         mbar_arrive_expect_tx(&full[s], kW4A16PackTile);
         tma_load_2d(ring + s * kW4A16PackTile, &tmap_wp, &full[s], kblock(i) * 64, n0, pol_w);   // 64B-swizzled rows
         ++issued;
+        if (++s == p.stages) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
       if (*abort_flag) {   // let copies in flight land before the CTA can exit
         for (int i = max(0, issued - p.stages); i < issued; ++i)
@@ -216,9 +220,9 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
     if (elect_one()) {
       const uint64_t pol_a = policy_evict_last();
       int issued = 0;
+      int s = 0;
+      uint32_t ph = 0;
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % p.xstages;
-        const uint32_t ph = static_cast<uint32_t>(i / p.xstages) & 1u;
         if (!mbar_wait(&xempty[s], ph ^ 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
         uint8_t* alo = xring + s * p.stage_bytes;
         uint8_t* ahi = alo + a_bytes;
@@ -234,6 +238,10 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
           }
         }
         ++issued;
+        if (++s == p.xstages) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
       if (*abort_flag) {
         for (int i = max(0, issued - p.xstages); i < issued; ++i)
@@ -245,29 +253,41 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
     // ---------------- MMA issuer ----------------
     // A (the dequantised weights) from tensor memory, B (the activations) from shared memory.
     if (elect_one()) {
+      // This thread shares its scheduler with four busy dequant warps, so its loop is kept
+      // short: ring indices and phases by counters (no divisions), operand descriptors by
+      // adding address offsets (in 16-byte units) to one precomputed descriptor.
       const uint32_t idesc = idesc_f16(128, n_pad);
+      const uint64_t xdesc0 = sdesc_sw128(smem_u32(xring), 16u, 1024u);
+      int s = 0, d = 0;
+      uint32_t xph = 0, aph = 0;
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % p.xstages;
-        const int d = i % p.aslots;
-        if (!mbar_wait(&xfull[s], static_cast<uint32_t>(i / p.xstages) & 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE) ||
-            !mbar_wait(&afull[d], static_cast<uint32_t>(i / p.aslots) & 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) {
+        if (!mbar_wait(&xfull[s], xph, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE) ||
+            !mbar_wait(&afull[d], aph, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) {
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
         SPECQ_TRACE_POINT(3, i);
-        const uint32_t alo = smem_u32(xring + s * p.stage_bytes);
-        const uint32_t ahi = alo + a_bytes;
+        const uint64_t dlo = xdesc0 + ((static_cast<uint32_t>(s) * p.stage_bytes) >> 4);
+        const uint64_t dhi = dlo + (a_bytes >> 4);
         const uint32_t wa = tmem_a + 64u * static_cast<uint32_t>(d);
 #pragma unroll
-        for (int k = 0; k < 4; ++k)   // 16 low-half K values per step
-          umma_f16_ts(tmem_acc, wa + 8u * k, sdesc_sw128(alo + 32u * k, 16u, 1024u), idesc, (i > 0 || k > 0) ? 1u : 0u);
+        for (int k = 0; k < 4; ++k)   // 16 low-half K values per step (32 bytes)
+          umma_f16_ts(tmem_acc, wa + 8u * k, dlo + 2u * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
 #pragma unroll
         for (int k = 0; k < 4; ++k)   // 16 high-half K values per step
-          umma_f16_ts(tmem_acc, wa + 32u + 8u * k, sdesc_sw128(ahi + 32u * k, 16u, 1024u), idesc, 1u);
+          umma_f16_ts(tmem_acc, wa + 32u + 8u * k, dhi + 2u * k, idesc, 1u);
         umma_commit(&xempty[s]);
         umma_commit(&aempty[d]);
         SPECQ_TRACE_POINT(4, i);
+        if (++s == p.xstages) {
+          s = 0;
+          xph ^= 1u;
+        }
+        if (++d == p.aslots) {
+          d = 0;
+          aph ^= 1u;
+        }
       }
       umma_commit(acc_full);
     }
@@ -295,12 +315,15 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
       }
       named_barrier_sync(1, kW4A16DequantThreads);
     }
+    // K-block i = grp + 4 it: weight stage i % stages and its phase by a counter; A slot
+    // i % aslots = grp (the host sizes aslots == kW4A16Groups), its phase flips every turn.
+    int s = grp % p.stages;
+    uint32_t wph = static_cast<uint32_t>(grp / p.stages) & 1u;
+    const int d = grp;
+    uint32_t aph = 0;
     for (int i = grp; i < nkb; i += kW4A16Groups) {
-      const int s = i % p.stages;
-      const int d = i % p.aslots;   // more slots than groups when the accumulator is narrow
-      if (!mbar_wait(&full[s], static_cast<uint32_t>(i / p.stages) & 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE) ||
-          !mbar_wait(&aempty[d], (static_cast<uint32_t>(i / p.aslots) & 1u) ^ 1u, p.status,
-                     SPECQ_STATUS_TIMEOUT_PIPELINE)) {
+      if (!mbar_wait(&full[s], wph, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE) ||
+          !mbar_wait(&aempty[d], aph ^ 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) {
         *abort_flag = 1;
         break;
       }
@@ -338,6 +361,8 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&afull[d]);
       if (td == 0) SPECQ_TRACE_POINT(11, i);
+      aph ^= 1u;
+      for (s += kW4A16Groups; s >= p.stages; s -= p.stages) wph ^= 1u;
     }
   }
   __syncwarp();

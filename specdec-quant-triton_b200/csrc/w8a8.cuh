@@ -140,9 +140,9 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_a = policy_evict_last();
       int issued = 0;
+      int s = 0;
+      uint32_t ph = 0;
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % stages;
-        const uint32_t ph = static_cast<uint32_t>(i / stages) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
         SPECQ_TRACE_POINT(2, i);
         uint8_t* wt = ring + s * stage_bytes;
@@ -152,6 +152,10 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
         tma_load_2d(wt, &tmap_w, &full[s], kx, n0, pol_w);
         for (int r = 0; r < a_rows; r += 16) tma_load_2d(at + r * 128, &tmap_a, &full[s], kx, m0 + r, pol_a);
         ++issued;
+        if (++s == stages) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
       if (*abort_flag) {   // let copies in flight land before the CTA can exit
         for (int i = max(0, issued - stages); i < issued; ++i)
@@ -162,22 +166,25 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
   } else if (warp == 1) {
     if (elect_one()) {
       const uint32_t idesc = idesc_i8(128, n_pad);
+      // descriptors advanced by address offsets in 16-byte units; ring index by a counter
+      const uint64_t wdesc0 = sdesc_sw128(smem_u32(ring), 16u, 1024u);
+      int s = 0;
+      uint32_t ph = 0;
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % stages;
-        const uint32_t ph = static_cast<uint32_t>(i / stages) & 1u;
         if (!mbar_wait(&full[s], ph, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
         tc_fence_after();
         SPECQ_TRACE_POINT(3, i);
-        const uint32_t wt = smem_u32(ring + s * stage_bytes);
-        const uint32_t at = wt + kW8A8WTile;
+        const uint64_t wd = wdesc0 + ((static_cast<uint32_t>(s) * stage_bytes) >> 4);
+        const uint64_t ad = wd + (kW8A8WTile >> 4);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t ad = sdesc_sw128(wt + 32u * k, 16u, 1024u);
-          const uint64_t bd = sdesc_sw128(at + 32u * k, 16u, 1024u);
-          umma_i8_ss(tmem_acc, ad, bd, idesc, (i > 0 || k > 0) ? 1u : 0u);
-        }
+        for (int k = 0; k < 4; ++k)   // 32 K bytes per step
+          umma_i8_ss(tmem_acc, wd + 2u * k, ad + 2u * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
         umma_commit(&empty[s]);   // stage is free once these MMAs have read it
         SPECQ_TRACE_POINT(4, i);
+        if (++s == stages) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
       umma_commit(acc_full);      // accumulator complete
     }
