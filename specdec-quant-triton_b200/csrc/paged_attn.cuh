@@ -227,8 +227,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* stage_empty = stage_full + kAttnStages;
   uint64_t* v_full = stage_empty + kAttnStages;   // [2]
   uint64_t* s_full = v_full + 2;                  // [2]
-  uint64_t* s_empty = s_full + 2;                 // [2]
-  uint64_t* p_full = s_empty + 2;                 // [2]
+  uint64_t* p_full = s_full + 2;                  // [2]  P(j) written, score buffer j % 2 read
   uint64_t* pv_done = p_full + 2;                 // [2]  PV(j) done: frees P and V buffer j % 2
   uint64_t* q_full = pv_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_full + 1);
@@ -341,7 +340,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&v_full[i], kAttnConvWarps);
       mbar_init(&s_full[i], 1u);
-      mbar_init(&s_empty[i], 8u);
       mbar_init(&p_full[i], 8u);
       mbar_init(&pv_done[i], 1u);
     }
@@ -605,10 +603,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&p_full[sb]);
-        mbar_arrive(&s_empty[sb]);
-      }
+      if (lane == 0) mbar_arrive(&p_full[sb]);
       if (t == 0) SPECQ_TRACE_POINT(24, j);
       slot = slot == 2 ? 0 : slot + 1;
     }
@@ -699,64 +694,71 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const uint64_t qdesc0 = sdesc_sw128(qop_a, 16u, 1024u);
       const uint64_t vdesc0 = sdesc_sw128(vop_a, 16384u, 1024u);
       const uint64_t pdesc0 = sdesc_sw128(pop_a, 16384u, 1024u);
-      auto issue_qk = [&](int j, int s) {
-        const uint32_t sb = static_cast<uint32_t>(j & 1);
-        tc_fence_after();
-        SPECQ_TRACE_POINT(30, j);
-        const uint64_t kd = kdesc0 + ((static_cast<uint32_t>(s) * kAttnStage) >> 4);
-        // score buffer sb <- the bias (all 2*NQ hi / lo columns, 4 per copy); the MMAs below
-        // run after the copies (same issuing thread) and accumulate onto it
+      // score buffer sb <- the bias (all 2*NQ hi / lo columns, 4 per copy); the MMAs issued
+      // after the copies by this thread run after them and accumulate onto the bias
+      auto reset_scores = [&](uint32_t sb) {
 #pragma unroll
         for (int c = 0; c < 2 * NQ; c += 4) tmem_cp_32x128b_x4(tmem + sb * cs2 + static_cast<uint32_t>(c), bias_desc);
-#pragma unroll
-        for (int k = 0; k < 4; ++k)   // 32 of the 128 head dims (32 bytes) per step
-          umma_i8_ss(tmem + sb * cs2, kd + 2u * k, qdesc0 + 2u * k, id_qk, 1u);   // onto the copied bias
-        umma_commit(&s_full[sb]);
-        umma_commit(&stage_empty[s]);   // the K tile is consumed
-        SPECQ_TRACE_POINT(31, j);
       };
-      auto issue_pv = [&](int i) {
-        const uint32_t bi = static_cast<uint32_t>(i & 1);
-        tc_fence_after();
-        SPECQ_TRACE_POINT(32, i);
-        const uint64_t vd = vdesc0 + ((bi * kAttnOp) >> 4);
-        const uint64_t pd = pdesc0 + ((bi * kAttnPTile) >> 4);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {   // 16 tokens (two 1024-byte atoms) per step
-          const uint64_t av = vd + 128u * k;
-          const uint64_t bp = pd + 128u * k;
-          const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
-          umma_f16_ss(tmem + O_col, av, bp, id_pv, acc);
-          umma_f16_ts(tmem + L_col, tmem + ONES_col + 8u * k, bp, id_l, acc);
-        }
-        umma_commit(&pv_done[bi]);
-        SPECQ_TRACE_POINT(33, i);
-      };
-      // Fixed issue order QK(0), QK(1), then per block i: PV(i) and QK(i+2), both as soon as the
-      // softmax has finished block i (its P tile, its score buffer).  The blocking waits keep
-      // this thread off the issue slots the softmax warps need.
       int qk_stage = 0;
       uint32_t qk_phase = 0;
-      auto qk = [&](int j) {
-        if (!mbar_wait(&stage_full[qk_stage], qk_phase, status, SPECQ_STATUS_TIMEOUT_PIPELINE)) return false;
-        if (!mbar_wait(&s_empty[j & 1], (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u, status, SPECQ_STATUS_TIMEOUT_MMA))
-          return false;
-        issue_qk(j, qk_stage);
+      auto next_stage = [&]() {
         if (++qk_stage == kAttnStages) {
           qk_stage = 0;
           qk_phase ^= 1u;
         }
-        return true;
       };
+      // QK(0) and QK(1) alone; then, per block i, once the softmax has finished block i (P(i)
+      // written and score buffer i read for the last time, both signalled by p_full(i)) and V(i)
+      // is converted: PV(i) interleaved with QK(i+2).  Three independent accumulation chains
+      // (O, the normaliser, the next scores) are then in flight in the tensor pipe instead of
+      // one at a time.  The blocking waits keep this thread off the issue slots the softmax
+      // warps need.
       if (nblk > 0) ok = mbar_wait(q_full, 0u, status, SPECQ_STATUS_TIMEOUT_PIPELINE);
-      for (int j = 0; ok && j < min(2, nblk); ++j) ok = qk(j);
+      for (int j = 0; ok && j < min(2, nblk); ++j) {
+        ok = mbar_wait(&stage_full[qk_stage], qk_phase, status, SPECQ_STATUS_TIMEOUT_PIPELINE);
+        if (!ok) break;
+        tc_fence_after();
+        SPECQ_TRACE_POINT(30, j);
+        const uint32_t sb = static_cast<uint32_t>(j);
+        const uint64_t kd = kdesc0 + ((static_cast<uint32_t>(qk_stage) * kAttnStage) >> 4);
+        reset_scores(sb);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)   // 32 of the 128 head dims (32 bytes) per step
+          umma_i8_ss(tmem + sb * cs2, kd + 2u * k, qdesc0 + 2u * k, id_qk, 1u);
+        umma_commit(&s_full[sb]);
+        umma_commit(&stage_empty[qk_stage]);   // the K tile is consumed
+        next_stage();
+      }
       for (int i = 0; ok && i < nblk; ++i) {
-        const uint32_t bi = static_cast<uint32_t>(i & 1);
+        const uint32_t bi = static_cast<uint32_t>(i & 1);   // P / V buffer of block i = score buffer of i + 2
         const uint32_t par = static_cast<uint32_t>(i >> 1) & 1u;
+        const bool more = i + 2 < nblk;
         ok = mbar_wait(&p_full[bi], par, status, SPECQ_STATUS_TIMEOUT_MMA) &&
-             mbar_wait(&v_full[bi], par, status, SPECQ_STATUS_TIMEOUT_PIPELINE);
-        if (ok) issue_pv(i);
-        if (ok && i + 2 < nblk) ok = qk(i + 2);
+             mbar_wait(&v_full[bi], par, status, SPECQ_STATUS_TIMEOUT_PIPELINE) &&
+             (!more || mbar_wait(&stage_full[qk_stage], qk_phase, status, SPECQ_STATUS_TIMEOUT_PIPELINE));
+        if (!ok) break;
+        tc_fence_after();
+        SPECQ_TRACE_POINT(32, i);
+        const uint64_t vd = vdesc0 + ((bi * kAttnOp) >> 4);
+        const uint64_t pd = pdesc0 + ((bi * kAttnPTile) >> 4);
+        const uint64_t kd = kdesc0 + ((static_cast<uint32_t>(qk_stage) * kAttnStage) >> 4);
+        if (more) reset_scores(bi);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {   // 16 tokens (two 1024-byte atoms) per PV step
+          const uint64_t bp = pd + 128u * k;
+          const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
+          umma_f16_ss(tmem + O_col, vd + 128u * k, bp, id_pv, acc);
+          if (more && k < 4) umma_i8_ss(tmem + bi * cs2, kd + 2u * k, qdesc0 + 2u * k, id_qk, 1u);
+          umma_f16_ts(tmem + L_col, tmem + ONES_col + 8u * k, bp, id_l, acc);
+        }
+        if (more) {
+          umma_commit(&s_full[bi]);
+          umma_commit(&stage_empty[qk_stage]);
+          next_stage();
+        }
+        umma_commit(&pv_done[bi]);
+        SPECQ_TRACE_POINT(33, i);
       }
     }
   } else {

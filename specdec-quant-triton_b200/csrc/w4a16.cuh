@@ -256,13 +256,14 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
       // This thread shares its scheduler with four busy dequant warps, so its loop is kept
       // short: ring indices and phases by counters (no divisions), operand descriptors by
       // adding address offsets (in 16-byte units) to one precomputed descriptor.
+      // One wait per K-block: the dequant group's afull arrival comes after one of its warps
+      // has seen the activation tile land (xfull), so afull covers both operands.
       const uint32_t idesc = idesc_f16(128, n_pad);
       const uint64_t xdesc0 = sdesc_sw128(smem_u32(xring), 16u, 1024u);
       int s = 0, d = 0;
       uint32_t xph = 0, aph = 0;
       for (int i = 0; i < nkb; ++i) {
-        if (!mbar_wait(&xfull[s], xph, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE) ||
-            !mbar_wait(&afull[d], aph, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) {
+        if (!mbar_wait(&afull[d], aph, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) {
           *abort_flag = 1;
           break;
         }
@@ -319,6 +320,8 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
     // i % aslots = grp (the host sizes aslots == kW4A16Groups), its phase flips every turn.
     int s = grp % p.stages;
     uint32_t wph = static_cast<uint32_t>(grp / p.stages) & 1u;
+    int xs = grp % p.xstages;                                       // activation stage of block i
+    uint32_t xph = static_cast<uint32_t>(grp / p.xstages) & 1u;
     const int d = grp;
     uint32_t aph = 0;
     for (int i = grp; i < nkb; i += kW4A16Groups) {
@@ -358,11 +361,15 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
       }
       tmem_wait_st();
       tc_fence_before();
+      // the group's quadrant-0 warp also waits for block i's activation tile (loaded far ahead,
+      // so this rarely waits): the MMA thread then needs the afull wait alone
+      if (quad == 0 && !mbar_wait(&xfull[xs], xph, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) *abort_flag = 1;
       __syncwarp();
       if (lane == 0) mbar_arrive(&afull[d]);
       if (td == 0) SPECQ_TRACE_POINT(11, i);
       aph ^= 1u;
       for (s += kW4A16Groups; s >= p.stages; s -= p.stages) wph ^= 1u;
+      for (xs += kW4A16Groups; xs >= p.xstages; xs -= p.xstages) xph ^= 1u;
     }
   }
   __syncwarp();
