@@ -28,8 +28,8 @@
 //     inside every query row's causal window take a mask-free path.  P is written MN-major
 //     (one 16-byte store per 8 query rows).  The normaliser l = sum_t p is produced by the
 //     tensor core itself (a ones operand in TMEM times P).  The score buffers are reset to
-//     their bias by the MMA issuer (tcgen05.cp from shared memory, in order with the MMAs),
-//     so the softmax threads never write tensor memory in the steady state.
+//     their bias by the MMA issuer with one fp16 MMA (see kScoreBias), in order with the QK
+//     MMAs, so the softmax threads never write tensor memory in the steady state.
 //   * Long contexts are split across a thread-block cluster (a power of two, from the
 //     block-table width only, so plan mode and eager mode give the same bits).  Each CTA
 //     pushes its partial (m, l, O) for the head dims a peer owns into that peer's shared
@@ -89,6 +89,8 @@ constexpr int kAttnStages = 3;
 constexpr int kAttnMaxPages = 2048;            // block-table entries of one CTA's context range
 constexpr uint32_t kAttnPTile = 128 * 128;     // fp16 P tile: 128 tokens x 64 query rows
 constexpr float kLazyMaxLog2 = 8.0f;           // rescale once a score exceeds the max by 2^8
+// 32-bit words of the bias MMA's constant B operand in shared memory (256 bytes used)
+__host__ __device__ constexpr int attn_bias_words(int) { return 64; }
 
 
 
@@ -187,6 +189,12 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 // below the query's own quantisation error).
 constexpr uint32_t kScoreBias = 0x4B400000u;
 constexpr float kScoreBias257 = 3233808384.f;   // 257 * 1.5 * 2^23, exact in fp32
+// The bias is written by one kind::f16 MMA with accumulate off: sixteen products
+// 1024.0 x 768.0 (fp16 operands, exact) sum to 12582912.0 = 1.5 * 2^23 exactly, whose fp32 bit
+// pattern is kScoreBias; the INT8 MMAs of the QK product then accumulate onto those bits as
+// int32 (tensor memory is untyped).
+constexpr uint32_t kBias1024x2 = 0x64006400u;   // fp16 1024.0, twice
+constexpr uint32_t kBias768x2 = 0x62006200u;    // fp16 768.0, twice
 
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,
                                             int w, uint64_t cache_hint) {
@@ -220,15 +228,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   float* wmax = qamax + 64;                                        // [4][64]
   float* ks_ring = wmax + 256;                                     // [3][256] softmax threads' K scales
   float* vs_ring = ks_ring + 3 * 256;                              // [3][128] V threads' V scales
-  uint32_t* bias_s = reinterpret_cast<uint32_t*>(vs_ring + 3 * 128); // [256] the score bias, copied into TMEM
-  int* pages_s = reinterpret_cast<int*>(bias_s + 256);             // [kAttnMaxPages] this CTA's page ids
+  uint32_t* bias_s = reinterpret_cast<uint32_t*>(vs_ring + 3 * 128); // the score bias, copied into TMEM
+  int* pages_s = reinterpret_cast<int*>(bias_s + attn_bias_words(NQ)); // [kAttnMaxPages] this CTA's page ids
   uint64_t* bars = reinterpret_cast<uint64_t*>(pages_s + kAttnMaxPages);
   uint64_t* stage_full = bars;
   uint64_t* stage_empty = stage_full + kAttnStages;
   uint64_t* v_full = stage_empty + kAttnStages;   // [2]
   uint64_t* s_full = v_full + 2;                  // [2]
   uint64_t* p_full = s_full + 2;                  // [2]  P(j) written, score buffer j % 2 read
-  uint64_t* pv_done = p_full + 2;                 // [2]  PV(j) done: frees P and V buffer j % 2
+  uint64_t* pv_done = p_full + 2;                 // [2]  PV of the last two blocks done (see wait_pv)
   uint64_t* q_full = pv_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_full + 1);
 
@@ -329,6 +337,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (p.scale_f32) return *src;
     const uint32_t w = *reinterpret_cast<const uint32_t*>(src);
     return __half2float(__ushort_as_half(static_cast<unsigned short>(((sel >> slot) & 1u) ? (w >> 16) : w)));
+  };
+
+  // PV(i) has completed once this returns.  PV(i) and QK(i+2) are issued together and QK(i+2)'s
+  // commit (s_full) comes after PV(i) from the same thread, so it also covers PV(i); only the
+  // last two blocks, which have no QK(i+2), commit to pv_done (each buffer once: phase 0).
+  // A parity wait is only meaningful when the barrier can be neither behind nor two phases
+  // ahead of the awaited phase: the softmax has seen every earlier S complete, and the V warps
+  // see QK(0) / QK(1) complete before they release V(0) / V(1).
+  auto wait_pv = [&](int i, int code) -> bool {
+    if (i + 2 < nblk) return mbar_wait(&s_full[i & 1], static_cast<uint32_t>((i + 2) >> 1) & 1u, p.status, code);
+    return mbar_wait(&pv_done[i & 1], 0u, p.status, code);
   };
 
   // ---- setup ---------------------------------------------------------------------------------
@@ -436,13 +455,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       l_s[t] = 0.f;
     }
     // the constant the MMA issuer copies into a score buffer before each QK (tcgen05.cp)
-    bias_s[t] = kScoreBias;
-    {   // ones operand of the normaliser MMA: fp16 1.0 pairs, 8 columns per 16-token K-step
+    // B operand of the bias MMA: fp16 768.0 pairs (see kScoreBias)
+    for (int w = t; w < attn_bias_words(NQ); w += 256) bias_s[w] = kBias768x2;
+    if (grp == 0) {   // A operands in TMEM: 8 columns of fp16 1.0 (normaliser), 8 of 1024.0 (bias)
       uint32_t ones[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) ones[i] = 0x3C003C00u;
-#pragma unroll
-      for (int c = 0; c < 32; c += 16) tmem_st16(lane_base + ONES_col + grp * 32 + c, ones);
+      for (int i = 0; i < 8; ++i) {
+        ones[i] = 0x3C003C00u;
+        ones[8 + i] = kBias1024x2;
+      }
+      tmem_st16(lane_base + ONES_col, ones);
     }
     tmem_wait_st();
     fence_proxy_async_smem();
@@ -479,9 +501,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       cp_async_wait<2>();   // block j's scale (fetched two blocks ago) has landed
       // this token's score scale: K scale x log2(e) / sqrt(D) x the query scale
       const float a_t = read_scale(ksd + 256 * slot, ksel, slot) * p.sm_scale_log2 * q_scale;
+      // S(j) is ready; its commit also covers PV(j-2), so P buffer sb is free as well
       ok = ok && mbar_wait(&s_full[sb], par2, status, SPECQ_STATUS_TIMEOUT_MMA);
-      // P buffer sb is free once PV(j-2) has read it
-      if (j >= 2) ok = ok && mbar_wait(&pv_done[sb], par2 ^ 1u, status, SPECQ_STATUS_TIMEOUT_MMA);
       tc_fence_after();
       if (t == 0) SPECQ_TRACE_POINT(21, j);
       const uint32_t s_addr = lane_base + sb * cs2 + col0;
@@ -547,9 +568,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         // ---- rescale: some score exceeds the running max by more than 2^8 ----
         if (t == 0) SPECQ_TRACE_POINT(26, j);
         // the running O^T / normaliser must be final before they are rescaled
-        if (j >= 1)
-          ok = ok && mbar_wait(&pv_done[sb ^ 1u], static_cast<uint32_t>((j - 1) >> 1) & 1u, status,
-                               SPECQ_STATUS_TIMEOUT_MMA);
+        if (j >= 1) ok = ok && wait_pv(j - 1, SPECQ_STATUS_TIMEOUT_MMA);
         tc_fence_after();
         // block max per query column: warp shuffles, then across the four lane quadrants
 #pragma unroll
@@ -612,7 +631,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (nblk > 0) {
       // bounded even after a failure: the tensor core must be idle before TMEM is freed
       const int jl = nblk - 1;
-      ok = mbar_wait(&pv_done[jl & 1], static_cast<uint32_t>(jl >> 1) & 1u, status, SPECQ_STATUS_TIMEOUT_MMA) && ok;
+      ok = wait_pv(jl, SPECQ_STATUS_TIMEOUT_MMA) && ok;
       tc_fence_after();
       if (t == 0) SPECQ_TRACE_POINT(60, 0);
       if (quad == 0) {
@@ -685,8 +704,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const uint32_t id_pv = idesc_f16(128, static_cast<uint32_t>(NQ), 1u, 1u);
       const uint32_t id_l = idesc_f16(128, static_cast<uint32_t>(NQ), 0u, 1u);
       const uint32_t ring_a = smem_u32(ring), vop_a = smem_u32(vop), qop_a = smem_u32(qop), pop_a = smem_u32(pop);
-      // 32 rows x 16 B of the constant bias, core matrices 128 B apart: 512 B of bias_s
-      const uint64_t bias_desc = sdesc_plain(smem_u32(bias_s), 128u, 128u);
+      // B of the bias MMA: K-major, no swizzle, both K core matrices (128 B apart) in bias_s and
+      // every 8-row group at the same address (stride 0): 256 bytes serve any N
+      const uint64_t bias_desc = sdesc_plain(smem_u32(bias_s), 128u, 0u);
+      const uint32_t id_bias = idesc_f16(128, static_cast<uint32_t>(2 * NQ));
       // Operand descriptors: one precomputed descriptor per tile, advanced by adding address
       // offsets in 16-byte units (this thread shares a scheduler with busy softmax and V warps,
       // so its per-block instruction count is kept small).
@@ -694,11 +715,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const uint64_t qdesc0 = sdesc_sw128(qop_a, 16u, 1024u);
       const uint64_t vdesc0 = sdesc_sw128(vop_a, 16384u, 1024u);
       const uint64_t pdesc0 = sdesc_sw128(pop_a, 16384u, 1024u);
-      // score buffer sb <- the bias (all 2*NQ hi / lo columns, 4 per copy); the MMAs issued
-      // after the copies by this thread run after them and accumulate onto the bias
+      // score buffer sb <- the bias in all 2*NQ hi / lo columns (one MMA, accumulate off); the
+      // QK MMAs issued after it by this thread accumulate onto it
       auto reset_scores = [&](uint32_t sb) {
-#pragma unroll
-        for (int c = 0; c < 2 * NQ; c += 4) tmem_cp_32x128b_x4(tmem + sb * cs2 + static_cast<uint32_t>(c), bias_desc);
+        umma_f16_ts(tmem + sb * cs2, tmem + ONES_col + 8u, bias_desc, id_bias, 0u);
       };
       int qk_stage = 0;
       uint32_t qk_phase = 0;
@@ -750,14 +770,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
           umma_f16_ss(tmem + O_col, vd + 128u * k, bp, id_pv, acc);
           if (more && k < 4) umma_i8_ss(tmem + bi * cs2, kd + 2u * k, qdesc0 + 2u * k, id_qk, 1u);
-          umma_f16_ts(tmem + L_col, tmem + ONES_col + 8u * k, bp, id_l, acc);
+          umma_f16_ts(tmem + L_col, tmem + ONES_col, bp, id_l, acc);
         }
         if (more) {
-          umma_commit(&s_full[bi]);
+          umma_commit(&s_full[bi]);   // QK(i+2) and, before it, PV(i)
           umma_commit(&stage_empty[qk_stage]);
           next_stage();
+        } else {
+          umma_commit(&pv_done[bi]);
         }
-        umma_commit(&pv_done[bi]);
         SPECQ_TRACE_POINT(33, i);
       }
     }
@@ -778,7 +799,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       fetch_scale(p.vs, j + 2, c, vsd + 128 * slot2, vsel, slot2);
       const int s = j % kAttnStages;
       const uint32_t sb = static_cast<uint32_t>(j & 1);
-      const uint32_t par2 = static_cast<uint32_t>(j >> 1) & 1u;
       ok = ok && mbar_wait(&stage_full[s], static_cast<uint32_t>(j / kAttnStages) & 1u, status,
                            SPECQ_STATUS_TIMEOUT_PIPELINE);
       if (c == 0) SPECQ_TRACE_POINT(40, j);
@@ -792,7 +812,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // the per-element multiply stays on the fp16 pipe
       const __half2 s2 = __half2half2(__float2half_rn(read_scale(vsd + 128 * slot, vsel, slot)));
       // V buffer sb is free once PV(j-2) has completed
-      if (j >= 2) ok = ok && mbar_wait(&pv_done[sb], par2 ^ 1u, status, SPECQ_STATUS_TIMEOUT_MMA);
+      if (j >= 2) ok = ok && wait_pv(j - 2, SPECQ_STATUS_TIMEOUT_MMA);
       uint8_t* vdst = vop + sb * kAttnOp;
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {
@@ -806,6 +826,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         store_f16_chunk_pair(vdst, c, ch, h);
       }
       fence_proxy_async_smem();
+      // Blocks 0 and 1: see QK(j) complete before releasing V(j).  QK(j + 2) cannot complete
+      // before V(j) is released, so the parity waits in wait_pv(j) two blocks later find
+      // s_full[j & 1] one phase ahead at most (costs nothing: PV(j) follows QK(j) anyway).
+      if (j < 2) ok = ok && mbar_wait(&s_full[j], 0u, status, SPECQ_STATUS_TIMEOUT_MMA);
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&v_full[sb]);
@@ -1050,10 +1074,11 @@ inline int run_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_
   p.splits = std::min(8, next_pow2(std::max(1, ceil_div(max_ctx, 2048))));
   p.stages = kAttnStages;
   p.sm_scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
-  // TMEM: two score buffers (hi and lo int32 columns), O^T, normaliser, 64 columns of ones
+  // TMEM: two score buffers (hi and lo int32 columns), O^T, normaliser, 16 columns of constant
+  // A operands (fp16 ones for the normaliser, fp16 1024.0 for the bias MMA)
   p.col_stride = static_cast<uint32_t>(round_up(2 * p.nq, 32));
   p.o_cols = static_cast<uint32_t>(round_up(p.nq, 32));
-  p.tmem_cols = static_cast<uint32_t>(next_pow2(static_cast<int>(2 * p.col_stride + 2 * p.o_cols + 64)));
+  p.tmem_cols = static_cast<uint32_t>(next_pow2(static_cast<int>(2 * p.col_stride + 2 * p.o_cols + 16)));
   if (p.tmem_cols > 512) return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: too many query rows per CTA");
   if (static_cast<int64_t>(b_grid) * p.n_qc > 65535)
     return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: grid too large");
@@ -1065,7 +1090,7 @@ inline int run_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_
 
   // K ring + two fp16 V tiles + int8 Q (hi, lo) + two P tiles + softmax state + barriers
   const int smem = 1024 + p.stages * static_cast<int>(kAttnStage) + 2 * static_cast<int>(kAttnOp) +
-                   p.nq * 256 + 2 * static_cast<int>(kAttnPTile) + 4096 + (3 * 256 + 3 * 128 + 256) * 4 +
+                   p.nq * 256 + 2 * static_cast<int>(kAttnPTile) + 4096 + (3 * 256 + 3 * 128 + attn_bias_words(p.nq)) * 4 +
                    kAttnMaxPages * 4 +
                    (2 * p.stages + 17) * 8 + 16;
   if (smem > 232448) return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: shared memory %d too large", smem);

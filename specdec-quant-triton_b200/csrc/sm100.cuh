@@ -281,7 +281,6 @@ __device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t adesc, uin
       : "memory");
 }
 
-// Arrive (once) on `bar` when every tcgen05.mma issued so far by this thread has completed.
 // D[tmem] (+)= A[tmem] * B[smem]^T, FP16 -> FP32 (A read from tensor memory).
 __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
                                             uint32_t accumulate) {
@@ -293,6 +292,7 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// Arrive (once) on `bar` when every tcgen05 operation issued so far by this thread has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    smem_u32(bar))
@@ -340,12 +340,6 @@ __device__ __forceinline__ uint64_t sdesc_plain(uint32_t saddr, uint32_t lbo, ui
   return d;
 }
 
-// Shared memory -> TMEM copy, asynchronous like tcgen05.mma and executed in issue order with
-// the MMAs of the same thread: a 32-row x 128-bit matrix written to 4 columns of all four
-// 32-lane quadrants.
-__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
-}
 
 // Byte offset of the 16-byte chunk `chunk` (0..7) of row `row` inside a 128-byte-swizzled
 // tile whose 8-row atoms are stored contiguously (1024 B per atom).
