@@ -317,10 +317,35 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   // from shared memory, so no register waits on a global load.  fp16 scales: the aligned
   // 4-byte word holding the value is copied (it never crosses a page, so it is mapped memory)
   // and bit `slot` of `sel` records which half the value is.
-  auto fetch_scale = [&](const void* base, int j, int row, float* dst, uint32_t& sel, int slot) {
-    const int pg = token_page(j, row);
+  // With a power-of-two page of at most one block, token row `row` keeps its slot in every
+  // block and its place in the CTA's page list advances by 128 / page per block: the scale
+  // address of block j is then one shared-memory read and one multiply-add (this runs on the
+  // softmax warps' per-block critical path).
+  const bool steady_pages = p.page_shift >= 0 && p.page <= 128;
+  struct ScaleRow {
+    int row, tok0, pidx0, pstep;
+    int64_t soff;
+  };
+  auto scale_row = [&](int row) {
+    ScaleRow r;
+    r.row = row;
+    r.tok0 = t_begin + row;
+    r.pidx0 = steady_pages ? (r.tok0 >> p.page_shift) - pg_first : 0;
+    r.pstep = steady_pages ? (128 >> p.page_shift) : 0;
+    r.soff = steady_pages ? static_cast<int64_t>(r.tok0 & (p.page - 1)) * p.s_so + static_cast<int64_t>(kvh) * p.s_sh : 0;
+    return r;
+  };
+  auto fetch_scale = [&](const void* base, int j, const ScaleRow& r, float* dst, uint32_t& sel, int slot) {
+    int pg = -1;
+    int64_t off = 0;
+    if (steady_pages) {
+      if (j < nblk && r.tok0 + j * 128 < t_end) pg = pages_s[r.pidx0 + j * r.pstep];
+      off = static_cast<int64_t>(pg) * p.s_sp + r.soff;
+    } else {
+      pg = token_page(j, r.row);
+      if (pg >= 0) off = scale_offset(j, r.row, pg);
+    }
     if (page_ok(pg)) {
-      const int64_t off = scale_offset(j, row, pg);
       if (p.scale_f32) {
         cp_async4(dst, static_cast<const float*>(base) + off);
       } else {
@@ -484,13 +509,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // share each scheduler's instruction cache, so the hot code is kept small.
     float* ksd = ks_ring + t;     // this thread's K-scale slots (stride 256)
     uint32_t ksel = 0u;
-    fetch_scale(p.ks, 0, tl, ksd, ksel, 0);
-    fetch_scale(p.ks, 1, tl, ksd + 256, ksel, 1);
+    const ScaleRow krow = scale_row(tl);
+    fetch_scale(p.ks, 0, krow, ksd, ksel, 0);
+    fetch_scale(p.ks, 1, krow, ksd + 256, ksel, 1);
     int slot = 0;                 // j % 3
 #pragma unroll 1
     for (int j = 0; j < nblk; ++j) {
       const int slot2 = slot == 0 ? 2 : slot - 1;   // (j + 2) % 3
-      fetch_scale(p.ks, j + 2, tl, ksd + 256 * slot2, ksel, slot2);
+      fetch_scale(p.ks, j + 2, krow, ksd + 256 * slot2, ksel, slot2);
       const int t_abs = t_begin + j * 128 + tl;
       const uint32_t sb = static_cast<uint32_t>(j & 1);
       const uint32_t par2 = static_cast<uint32_t>(j >> 1) & 1u;
@@ -790,13 +816,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int c = static_cast<int>(threadIdx.x) - 32 * (kAttnMmaWarp + 1);   // 0..127
     float* vsd = vs_ring + c;     // this thread's V-scale slots (stride 128)
     uint32_t vsel = 0u;
-    fetch_scale(p.vs, 0, c, vsd, vsel, 0);
-    fetch_scale(p.vs, 1, c, vsd + 128, vsel, 1);
+    const ScaleRow vrow_s = scale_row(c);
+    fetch_scale(p.vs, 0, vrow_s, vsd, vsel, 0);
+    fetch_scale(p.vs, 1, vrow_s, vsd + 128, vsel, 1);
     int slot = 0;                 // j % 3
 #pragma unroll 1
     for (int j = 0; j < nblk; ++j) {
       const int slot2 = slot == 0 ? 2 : slot - 1;   // (j + 2) % 3
-      fetch_scale(p.vs, j + 2, c, vsd + 128 * slot2, vsel, slot2);
+      fetch_scale(p.vs, j + 2, vrow_s, vsd + 128 * slot2, vsel, slot2);
       const int s = j % kAttnStages;
       const uint32_t sb = static_cast<uint32_t>(j & 1);
       ok = ok && mbar_wait(&stage_full[s], static_cast<uint32_t>(j / kAttnStages) & 1u, status,

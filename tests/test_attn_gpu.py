@@ -119,7 +119,7 @@ def test_context_lengths_and_splits(cuda, ctx, cluster):
 
 
 @pytest.mark.parametrize("H,H_KV,page,qpp", [(64, 8, 16, 9), (8, 8, 16, 5), (32, 8, 8, 4), (32, 8, 32, 2),
-                                             (16, 2, 64, 9)])
+                                             (16, 2, 64, 9), (32, 8, 24, 9), (16, 4, 256, 9)])
 def test_gqa_page_and_qpp_variants(cuda, H, H_KV, page, qpp):
     import specq
     B, D, ql = 3, 128, 9
