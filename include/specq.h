@@ -117,9 +117,14 @@ int specq_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_t q_s
  *   2  y = silu(x[:, :N]) * x[:, N:2N]    x fp16 [M, 2N] (an MLP's gate and up halves)
  * q int8 [M, N] (row stride ldq), s fp32 [M].  plan (optional) = device int32, plan[0] = the
  * active M; rows past it are not touched.
+ * Rows split across GPUs (tensor parallelism): amax_out (modes 0 and 2) makes this call only
+ * write each row's amax |y| to amax_out[m] (q and s untouched); amax_in (any mode) makes it
+ * quantise with amax_in[m] -- the maximum over all shards -- in place of the local amax, so
+ * every shard gets the scale and the int8 values of the unsplit row.  Both may be null.
  */
 int specq_quant_rows(const void* x, int64_t ldx, void* r, int64_t ldr, int8_t* q, int64_t ldq, float* s,
-                     const int32_t* plan, int M, int N, int mode, void* stream);
+                     const int32_t* plan, const float* amax_in, float* amax_out, int M, int N, int mode,
+                     void* stream);
 
 /* Append the K and V of the q_len newest tokens of each sequence to an INT8 paged KV cache.
  * No reference counterpart as a kernel: the reference builds its cache with the fixture

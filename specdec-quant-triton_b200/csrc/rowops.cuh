@@ -47,6 +47,8 @@ struct QuantRowsParams {
   int8_t* q;           // [M, N]
   float* s;            // [M]
   const int32_t* plan; // plan[0] = active M
+  const float* amax_in;  // optional: the row's amax over a wider row (tensor-parallel shards)
+  float* amax_out;       // optional: write the row amax of y and stop (no quantisation)
   int* status;
   int64_t ldx, ldr, ldq;
   int M, N, mode;
@@ -99,6 +101,11 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_kernel(const __grid_co
   float m = 0.f;
 #pragma unroll
   for (int w = 0; w < kRowThreads / 32; ++w) m = fmaxf(m, red[w]);
+  if (p.amax_out != nullptr) {   // first pass of a sharded row: its amax only
+    if (threadIdx.x == 0) p.amax_out[row] = m;
+    return;
+  }
+  if (p.amax_in != nullptr) m = __ldg(p.amax_in + row);   // the whole row's amax
   const float s = __fmul_rn(fmaxf(m, 1e-8f), kInv127);
   int8_t* q = p.q + static_cast<int64_t>(row) * p.ldq;
 #pragma unroll
@@ -177,6 +184,11 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_vec_kernel(const __gri
   float m = 0.f;
 #pragma unroll
   for (int w = 0; w < kRowThreads / 32; ++w) m = fmaxf(m, red[w]);
+  if (p.amax_out != nullptr) {   // first pass of a sharded row: its amax only
+    if (threadIdx.x == 0) p.amax_out[row] = m;
+    return;
+  }
+  if (p.amax_in != nullptr) m = __ldg(p.amax_in + row);   // the whole row's amax
   const float s = __fmul_rn(fmaxf(m, 1e-8f), kInv127);
   int8_t* q = p.q + static_cast<int64_t>(row) * p.ldq;
 #pragma unroll
@@ -396,13 +408,16 @@ __global__ void __launch_bounds__(128) kv_append_kernel(const __grid_constant__ 
 }
 
 inline int run_quant_rows(const void* x, int64_t ldx, void* r, int64_t ldr, int8_t* q, int64_t ldq, float* s,
-                          const int32_t* plan, int M, int N, int mode, void* stream) {
+                          const int32_t* plan, const float* amax_in, float* amax_out, int M, int N, int mode,
+                          void* stream) {
   if (M < 0 || N <= 0) return fail(SPECQ_ERR_INVALID_ARG, "quant_rows: bad shape M=%d N=%d", M, N);
   if (mode < 0 || mode > 2) return fail(SPECQ_ERR_INVALID_ARG, "quant_rows: mode %d", mode);
   if (M == 0) return SPECQ_OK;
-  if (x == nullptr || q == nullptr || s == nullptr || (mode == 1 && r == nullptr))
+  if (amax_out != nullptr && (mode == 1 || amax_in != nullptr))
+    return fail(SPECQ_ERR_INVALID_ARG, "quant_rows: amax_out is for modes 0 and 2 without amax_in");
+  if (x == nullptr || (amax_out == nullptr && (q == nullptr || s == nullptr)) || (mode == 1 && r == nullptr))
     return fail(SPECQ_ERR_INVALID_ARG, "quant_rows: null pointer");
-  if (ldx < (mode == 2 ? 2 * static_cast<int64_t>(N) : N) || ldq < N || (mode == 1 && ldr < N))
+  if (ldx < (mode == 2 ? 2 * static_cast<int64_t>(N) : N) || (amax_out == nullptr && ldq < N) || (mode == 1 && ldr < N))
     return fail(SPECQ_ERR_INVALID_ARG, "quant_rows: row strides too small");
   if (N > kRowThreads * kRowMaxPerThread)
     return fail(SPECQ_ERR_UNSUPPORTED, "quant_rows: N=%d > %d", N, kRowThreads * kRowMaxPerThread);
@@ -414,6 +429,8 @@ inline int run_quant_rows(const void* x, int64_t ldx, void* r, int64_t ldr, int8
   p.q = q;
   p.s = s;
   p.plan = plan;
+  p.amax_in = amax_in;
+  p.amax_out = amax_out;
   p.status = dev->status;
   p.ldx = ldx; p.ldr = ldr; p.ldq = ldq;
   p.M = M; p.N = N; p.mode = mode;

@@ -369,9 +369,10 @@ int specq_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_t q_s
 }
 
 int specq_quant_rows(const void* x, int64_t ldx, void* r, int64_t ldr, int8_t* q, int64_t ldq, float* s,
-                     const int32_t* plan, int M, int N, int mode, void* stream) {
+                     const int32_t* plan, const float* amax_in, float* amax_out, int M, int N, int mode,
+                     void* stream) {
   last_launch_ref() = LaunchRecord();
-  return run_quant_rows(x, ldx, r, ldr, q, ldq, s, plan, M, N, mode, stream);
+  return run_quant_rows(x, ldx, r, ldr, q, ldq, s, plan, amax_in, amax_out, M, N, mode, stream);
 }
 
 int specq_kv_append(const void* x, int64_t ldx, int k_col, int v_col, int8_t* kc, int8_t* vc, int64_t kv_sp,

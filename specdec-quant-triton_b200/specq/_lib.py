@@ -37,7 +37,7 @@ SIGNATURES = {
     "specq_w8a8": (_i32, [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _vp, _i32, _i32, _i32, _vp]),
     "specq_w8a8_acc": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _i32, _i32, _i32, _vp]),
     "specq_w4a16": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _vp, _i64, _i64, _vp, _i32, _i32, _i32, _vp]),
-    "specq_quant_rows": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i32, _i32, _i32, _vp]),
+    "specq_quant_rows": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     "specq_kv_append": (_i32, [_vp, _i64, _i32, _i32, _vp, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _i64, _i64, _i64,
                                _vp, _i64, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp]),
     "specq_paged_attention": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _i64, _i64,

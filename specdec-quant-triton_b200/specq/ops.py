@@ -264,13 +264,16 @@ def paged_attention(q, kc, vc, ks, vs, block_tbl, ctx_len, q_len, QPP=None, BLOC
 QUANT_PLAIN, QUANT_RESIDUAL, QUANT_SILU_MUL = 0, 1, 2
 
 
-def quant_rows(x, mode=QUANT_PLAIN, residual=None, q=None, s=None, plan=None, grid_m_max=None):
+def quant_rows(x, mode=QUANT_PLAIN, residual=None, q=None, s=None, plan=None, grid_m_max=None, amax_in=None,
+               amax_out=None):
     """Per-token symmetric INT8 of fp16 rows on the device -> (q int8 [M, N], s fp32 [M]).
 
     mode QUANT_PLAIN: quantise x [M, N] (kernels.py:58-62 bit for bit).
     mode QUANT_RESIDUAL: residual <- fp16(x + residual), then quantise that sum.
     mode QUANT_SILU_MUL: quantise silu(x[:, :N]) * x[:, N:] for x [M, 2N].
-    With `plan`, only the first plan[0] rows are computed (a plan-buffer graph)."""
+    With `plan`, only the first plan[0] rows are computed (a plan-buffer graph).
+    Rows split across GPUs: `amax_out` (fp32 [M]) receives each row's amax and nothing is
+    quantised (returns None); `amax_in` quantises with the given whole-row amax."""
     if x.dtype != torch.float16 or x.dim() != 2:
         raise TypeError("quant_rows: x must be a 2-D float16 tensor")
     _require_cuda(x, residual, q, s)
@@ -280,13 +283,22 @@ def quant_rows(x, mode=QUANT_PLAIN, residual=None, q=None, s=None, plan=None, gr
     if mode == QUANT_RESIDUAL:
         if residual is None or residual.shape != (M, N) or residual.dtype != torch.float16 or residual.stride(-1) != 1:
             raise ValueError("quant_rows: QUANT_RESIDUAL needs a float16 residual [M, N] with unit inner stride")
+    for t, name in ((amax_in, "amax_in"), (amax_out, "amax_out")):
+        if t is not None and (t.dtype != torch.float32 or t.dim() != 1 or t.shape[0] < M or not t.is_cuda):
+            raise ValueError(f"quant_rows: {name} must be a CUDA float32 vector of >= {M} rows")
+    lib = _lib.load()
+    if amax_out is not None:
+        m_rows = _row_extent(M, plan, grid_m_max, amax_out.shape[0])
+        _lib.check(lib.specq_quant_rows(x.data_ptr(), x.stride(0), None, 0, None, 0, None, _plan_ptr(plan), None,
+                                        amax_out.data_ptr(), m_rows, N, mode, _stream()))
+        return None
     q = torch.empty((M, N), dtype=torch.int8, device=x.device) if q is None else q
     s = torch.empty((M,), dtype=torch.float32, device=x.device) if s is None else s
     m_rows = _row_extent(M, plan, grid_m_max, q.shape[0], s.shape[0])
-    lib = _lib.load()
     _lib.check(lib.specq_quant_rows(x.data_ptr(), x.stride(0), _ptr(residual),
                                     residual.stride(0) if residual is not None else 0, q.data_ptr(), q.stride(0),
-                                    s.data_ptr(), _plan_ptr(plan), m_rows, N, mode, _stream()))
+                                    s.data_ptr(), _plan_ptr(plan), _ptr(amax_in), None, m_rows, N, mode,
+                                    _stream()))
     return q, s
 
 

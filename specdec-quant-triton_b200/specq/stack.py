@@ -37,6 +37,24 @@ from . import ops
 from .fixtures import make_paged_kv
 
 
+def make_model(layers, hid, ff, heads, kv_heads, head_dim, m_max, seed, device):
+    """Random INT8 weights of every layer ({"qkv", "o", "gu", "down"}: (int8 [N, K], fp32 scales
+    [N])) and the initial residual stream [m_max, hid], drawn in a fixed order from one seed:
+    the single-GPU and the tensor-parallel stacks build the same model."""
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def w8(n, k):   # int8 weights uniform in [-127, 127], per-channel scales ~ 1/sqrt(k)
+        q = torch.randint(-127, 128, (n, k), generator=g, device=device, dtype=torch.int16).to(torch.int8)
+        s = (torch.rand(n, generator=g, device=device) * 0.5 + 0.5) / (127.0 * k ** 0.5)
+        return q, s
+
+    n_qkv = (heads + 2 * kv_heads) * head_dim
+    w = [{"qkv": w8(n_qkv, hid), "o": w8(hid, hid), "gu": w8(2 * ff, hid), "down": w8(hid, ff)}
+         for _ in range(layers)]
+    h0 = (torch.randn(m_max, hid, generator=g, device=device) * 0.5).half()
+    return w, h0
+
+
 class Stack:
     def __init__(self, layers=4, hid=4096, ff=14336, heads=32, kv_heads=8, head_dim=128, ctx=1024, b_max=32,
                  ks=(0, 2, 4, 8), page=16, seed=0, device="cuda"):
@@ -45,18 +63,9 @@ class Stack:
         self.ql_max = max(ks) + 1
         self.m_max = b_max * self.ql_max
         self.n_qkv = (heads + 2 * kv_heads) * head_dim
-        g = torch.Generator(device=device).manual_seed(seed)
-
-        def w8(n, k):   # int8 weights uniform in [-127, 127], per-channel scales ~ 1/sqrt(k)
-            q = torch.randint(-127, 128, (n, k), generator=g, device=device, dtype=torch.int16).to(torch.int8)
-            s = (torch.rand(n, generator=g, device=device) * 0.5 + 0.5) / (127.0 * k ** 0.5)
-            return q, s
-
-        self.w = [{"qkv": w8(self.n_qkv, hid), "o": w8(hid, hid), "gu": w8(2 * ff, hid), "down": w8(hid, ff)}
-                  for _ in range(layers)]
+        self.w, self.h0 = make_model(layers, hid, ff, heads, kv_heads, head_dim, self.m_max, seed, device)
         self.kv = [make_paged_kv(b_max, [ctx] * b_max, kv_heads, head_dim, PAGE=page, device=device, seed=seed + i)
                    for i in range(layers)]
-        self.h0 = (torch.randn(self.m_max, hid, generator=g, device=device) * 0.5).half()
         mk = lambda *shape, dtype=torch.float16: torch.zeros(shape, dtype=dtype, device=device)  # noqa: E731
         self.h = self.h0.clone()
         self.x8, self.sx = mk(self.m_max, hid, dtype=torch.int8), mk(self.m_max, dtype=torch.float32)

@@ -123,3 +123,26 @@ def test_packed_attention_equals_strided(cuda):
     specq.paged_attention_packed(qkv, 0, out2, kc, vc, ks, vs, bt, cl, ql, H, B=B, ql_max=9, plan=plan)
     assert torch.equal(out2[: B * ql].view(B, ql, H, 128), ref)
     assert bool((out2[B * ql:] == 0).all())
+
+
+@pytest.mark.parametrize("mode", [0, 2])
+def test_quant_sharded_rows_match_whole_rows(cuda, mode):
+    """A row split across two shards: amax_out per shard, the maximum as amax_in -- each shard's
+    int8 values and scale equal those of the whole row (the tensor-parallel stack relies on it)."""
+    import specq
+    M, N = 24, 4096
+    g = torch.Generator(device="cuda").manual_seed(mode + 11)
+    if mode == 0:
+        x = (torch.randn(M, N, device="cuda", generator=g) * 2).half()
+        halves = [x[:, : N // 2], x[:, N // 2:]]
+    else:   # gate | up; shard r holds [gate_r | up_r]
+        x = torch.randn(M, 2 * N, device="cuda", generator=g).half()
+        halves = [torch.cat([x[:, :N // 2], x[:, N:N + N // 2]], 1), torch.cat([x[:, N // 2:N], x[:, N + N // 2:]], 1)]
+    q, s = specq.quant_rows(x, mode=mode)
+    amax = [torch.empty(M, device="cuda") for _ in halves]
+    for h, a in zip(halves, amax):
+        assert specq.quant_rows(h, mode=mode, amax_out=a) is None
+    whole = torch.maximum(amax[0], amax[1])
+    parts = [specq.quant_rows(h, mode=mode, amax_in=whole) for h in halves]
+    assert torch.equal(parts[0][1], s) and torch.equal(parts[1][1], s)
+    assert torch.equal(torch.cat([parts[0][0], parts[1][0]], 1), q)
