@@ -209,6 +209,7 @@ template <int NQ>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     paged_attn_kernel(const __grid_constant__ AttnParams p, const __grid_constant__ CUtensorMap tmap_k,
                       const __grid_constant__ CUtensorMap tmap_v) {
+  pdl_wait();                // the previous kernel's writes are visible from here on
   static_assert(NQ % 16 == 0 && NQ >= 16 && NQ <= 64, "query rows per CTA");
   constexpr int NQH = NQ / 2;   // query columns per softmax thread
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -869,6 +870,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   }
   __syncwarp();
 
+  // The next kernel on the stream may begin launching once every CTA is here (its CTAs wait in
+  // griddepcontrol.wait until this grid has completed): launching it at the start instead
+  // measured slower, its early CTAs holding SMs this kernel's clusters could use.
+  pdl_launch_dependents();
   // ======================= epilogue: normalise, combine splits, store =======================
   // softmax warps: thread tl owns head dim d = tl (TMEM lane) for its group's query columns
   const bool soft = warp < 8;
@@ -1144,13 +1149,8 @@ inline int run_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_
   cfg.blockDim = dim3(kAttnThreads, 1, 1);
   cfg.dynamicSmemBytes = static_cast<size_t>(smem);
   cfg.stream = static_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(p.splits);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = p.splits > 1 ? 1 : 0;
+  LaunchAttrs attrs(p.splits);
+  attrs.apply(cfg);
   void* args[] = {&p, &tk, &tv};
   SPECQ_CUDA_TRY(cudaLaunchKernelExC(&cfg, fn, args));
   LaunchRecord& r = last_launch_ref();

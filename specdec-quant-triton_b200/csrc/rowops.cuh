@@ -61,6 +61,8 @@ __device__ __forceinline__ float silu_f32(float g) { return __fdividef(g, 1.f + 
 
 template <int PER>
 __global__ void __launch_bounds__(kRowThreads) quant_rows_kernel(const __grid_constant__ QuantRowsParams p) {
+  pdl_launch_dependents();   // the next kernel on the stream may begin launching
+  pdl_wait();                // the previous kernel's writes are visible from here on
   __shared__ float red[kRowThreads / 32];
   const int row = blockIdx.x;
   int M = p.M;
@@ -123,6 +125,8 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_kernel(const __grid_co
 // (CH of them) -- rows 16-byte aligned, N a multiple of 8.
 template <int CH>
 __global__ void __launch_bounds__(kRowThreads) quant_rows_vec_kernel(const __grid_constant__ QuantRowsParams p) {
+  pdl_launch_dependents();   // the next kernel on the stream may begin launching
+  pdl_wait();                // the previous kernel's writes are visible from here on
   __shared__ float red[kRowThreads / 32];
   const int row = blockIdx.x;
   int M = p.M;
@@ -260,6 +264,8 @@ constexpr int kPackUnits = 4;
 
 template <typename T, int E, bool VEC>   // E = group / 32
 __global__ void __launch_bounds__(256) pack_int4_kernel(const __grid_constant__ PackInt4Params p) {
+  pdl_launch_dependents();   // the next kernel on the stream may begin launching
+  pdl_wait();                // the previous kernel's writes are visible from here on
   const int pairs = p.K / (2 * p.group);
   const int64_t total = static_cast<int64_t>(p.N) * pairs;
   const int64_t unit0 = (static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * kPackUnits;
@@ -355,6 +361,8 @@ struct KvAppendParams {
 };
 
 __global__ void __launch_bounds__(128) kv_append_kernel(const __grid_constant__ KvAppendParams p) {
+  pdl_launch_dependents();   // the next kernel on the stream may begin launching
+  pdl_wait();                // the previous kernel's writes are visible from here on
   // blockIdx.x = token slot (b * ql_max + t), warp = (KV head, K|V) pair index
   const int warp = static_cast<int>(threadIdx.x >> 5);
   const int lane = static_cast<int>(threadIdx.x & 31);
@@ -439,18 +447,18 @@ inline int run_quant_rows(const void* x, int64_t ldx, void* r, int64_t ldr, int8
                    (mode != 1 || (aligned(r, 16) && ldr % 8 == 0));
   if (vec) {
     const int ch = ceil_div(N, 8 * kRowThreads);
-    if (ch <= 1) quant_rows_vec_kernel<1><<<M, kRowThreads, 0, st>>>(p);
-    else if (ch <= 2) quant_rows_vec_kernel<2><<<M, kRowThreads, 0, st>>>(p);
-    else if (ch <= 4) quant_rows_vec_kernel<4><<<M, kRowThreads, 0, st>>>(p);
-    else quant_rows_vec_kernel<8><<<M, kRowThreads, 0, st>>>(p);
+    if (ch <= 1) SPECQ_CUDA_TRY(launch_plain(quant_rows_vec_kernel<1>, dim3(M), dim3(kRowThreads), st, p));
+    else if (ch <= 2) SPECQ_CUDA_TRY(launch_plain(quant_rows_vec_kernel<2>, dim3(M), dim3(kRowThreads), st, p));
+    else if (ch <= 4) SPECQ_CUDA_TRY(launch_plain(quant_rows_vec_kernel<4>, dim3(M), dim3(kRowThreads), st, p));
+    else SPECQ_CUDA_TRY(launch_plain(quant_rows_vec_kernel<8>, dim3(M), dim3(kRowThreads), st, p));
     SPECQ_CUDA_TRY(cudaGetLastError());
     return SPECQ_OK;
   }
   const int per = ceil_div(N, kRowThreads);
-  if (per <= 8) quant_rows_kernel<8><<<M, kRowThreads, 0, st>>>(p);
-  else if (per <= 16) quant_rows_kernel<16><<<M, kRowThreads, 0, st>>>(p);
-  else if (per <= 32) quant_rows_kernel<32><<<M, kRowThreads, 0, st>>>(p);
-  else quant_rows_kernel<64><<<M, kRowThreads, 0, st>>>(p);
+  if (per <= 8) SPECQ_CUDA_TRY(launch_plain(quant_rows_kernel<8>, dim3(M), dim3(kRowThreads), st, p));
+  else if (per <= 16) SPECQ_CUDA_TRY(launch_plain(quant_rows_kernel<16>, dim3(M), dim3(kRowThreads), st, p));
+  else if (per <= 32) SPECQ_CUDA_TRY(launch_plain(quant_rows_kernel<32>, dim3(M), dim3(kRowThreads), st, p));
+  else SPECQ_CUDA_TRY(launch_plain(quant_rows_kernel<64>, dim3(M), dim3(kRowThreads), st, p));
   SPECQ_CUDA_TRY(cudaGetLastError());
   return SPECQ_OK;
 }
@@ -486,7 +494,7 @@ inline int run_kv_append(const void* x, int64_t ldx, int k_col, int v_col, int8_
   p.k_col = k_col; p.v_col = v_col; p.n_seqs = n_seqs; p.q_len = q_len; p.b_grid = b_grid;
   p.ql_max = ql_grid; p.h_kv = H_KV; p.page = page; p.n_pages = n_pages; p.bt_cols = bt_cols;
   const dim3 grid(static_cast<unsigned>(b_grid * ql_grid), static_cast<unsigned>(ceil_div(2 * H_KV, 4)));
-  kv_append_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  SPECQ_CUDA_TRY(launch_plain(kv_append_kernel, grid, dim3(128), static_cast<cudaStream_t>(stream), p));
   SPECQ_CUDA_TRY(cudaGetLastError());
   return SPECQ_OK;
 }
@@ -519,7 +527,7 @@ inline int run_pack_int4(const void* w, int w_dtype, int64_t ldw, int N, int K, 
                    (deq == nullptr || (aligned(deq, 2 * E) && lddeq % E == 0 && (K / 2) % E == 0));
   auto launch = [&](auto tag, auto e_tag, auto vec_tag) {
     using T = decltype(tag);
-    pack_int4_kernel<T, decltype(e_tag)::value, decltype(vec_tag)::value><<<gx, 256, 0, st>>>(p);
+    return launch_plain(pack_int4_kernel<T, decltype(e_tag)::value, decltype(vec_tag)::value>, dim3(gx), dim3(256), st, p);
   };
   auto by_e = [&](auto tag) {
     using I1 = std::integral_constant<int, 1>;

@@ -25,6 +25,14 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// Programmatic dependent launch (see LaunchAttrs): let the next kernel on the stream begin
+// launching, and wait until the previous one has completed and its writes are visible.  Every
+// kernel waits before its first global-memory access and triggers its dependents at its start
+// (short kernels) or when its main loop is done (the GEMMs and attention); without the launch
+// attribute both return at once.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31; }
 

@@ -39,13 +39,8 @@ int launch_w8a8_variant(const W8A8Params& p, const CUtensorMap& tw, const CUtens
   cfg.blockDim = dim3(kW8A8Threads, 1, 1);
   cfg.dynamicSmemBytes = static_cast<size_t>(smem);
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(p.splits);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = p.splits > 1 ? 1 : 0;
+  LaunchAttrs attrs(p.splits);
+  attrs.apply(cfg);
   SPECQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p, tw, ta));
   return SPECQ_OK;
 }
@@ -283,13 +278,8 @@ int run_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const
   cfg.blockDim = dim3(kW4A16Threads, 1, 1);
   cfg.dynamicSmemBytes = static_cast<size_t>(smem);
   cfg.stream = static_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(S);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = S > 1 ? 1 : 0;
+  LaunchAttrs attrs(S);
+  attrs.apply(cfg);
   SPECQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, w4a16_kernel, p, tw, ta, tsc, tac));
   LaunchRecord& r = last_launch_ref();
   r.variant = 0;

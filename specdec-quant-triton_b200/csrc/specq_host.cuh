@@ -7,9 +7,11 @@
 #include <cuda_runtime.h>
 
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <utility>
 #include <string>
 
 #include "specq.h"
@@ -140,6 +142,55 @@ inline int next_pow2(int x) {
   return p;
 }
 inline bool aligned(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
+
+// Programmatic dependent launch: every kernel of this library may be scheduled while the
+// previous kernel on its stream is still finishing (its CTAs then wait in griddepcontrol.wait
+// before touching global memory), which hides the launch latency between back-to-back kernels.
+// SPECQ_PDL=0 in the environment turns it off.
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("SPECQ_PDL");
+    return v == nullptr || v[0] != '0';
+  }();
+  return on;
+}
+
+// Launch attributes: the cluster shape (when > 1) and programmatic dependent launch.
+struct LaunchAttrs {
+  cudaLaunchAttribute a[2];
+  unsigned n = 0;
+  explicit LaunchAttrs(int cluster_x) {
+    if (cluster_x > 1) {
+      a[n].id = cudaLaunchAttributeClusterDimension;
+      a[n].val.clusterDim.x = static_cast<unsigned>(cluster_x);
+      a[n].val.clusterDim.y = 1;
+      a[n].val.clusterDim.z = 1;
+      ++n;
+    }
+    if (pdl_enabled()) {
+      a[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      a[n].val.programmaticStreamSerializationAllowed = 1;
+      ++n;
+    }
+  }
+  void apply(cudaLaunchConfig_t& cfg) {
+    cfg.attrs = a;
+    cfg.numAttrs = n;
+  }
+};
+
+// cudaLaunchKernelEx with the library's launch attributes and no cluster.
+template <typename... Params, typename... Args>
+inline cudaError_t launch_plain(void (*kern)(Params...), dim3 grid, dim3 block, cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  LaunchAttrs at(1);
+  at.apply(cfg);
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // Widest access width (16, 8, 4, 2, 1 bytes) that every pointer and byte count in the list
 // is a multiple of.

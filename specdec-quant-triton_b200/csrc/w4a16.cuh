@@ -98,6 +98,7 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
     w4a16_kernel(const __grid_constant__ W4A16Params p, const __grid_constant__ CUtensorMap tmap_wp,
                  const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_sc,
                  const __grid_constant__ CUtensorMap tmap_a_chunk) {
+  pdl_wait();                // the previous kernel's writes are visible from here on
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   SPECQ_TRACE_INIT();
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -374,6 +375,10 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
   }
   __syncwarp();
 
+  // The next kernel on the stream may begin launching once every CTA is here (its CTAs wait in
+  // griddepcontrol.wait until this grid has completed): launching it at the start instead
+  // measured slower, its early CTAs holding SMs this kernel's clusters could use.
+  pdl_launch_dependents();
   // ---------------- epilogue (warps 2..5) ----------------
   const bool epi = (warp >= 2 && warp < 6);
   const uint32_t quad = warp & 3u;

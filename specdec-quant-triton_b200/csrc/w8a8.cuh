@@ -57,6 +57,7 @@ template <int VEC>
 __global__ void __launch_bounds__(kW8A8Threads, 1)
     w8a8_kernel(const __grid_constant__ W8A8Params p, const __grid_constant__ CUtensorMap tmap_w,
                 const __grid_constant__ CUtensorMap tmap_a) {
+  pdl_wait();                // the previous kernel's writes are visible from here on
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   SPECQ_TRACE_INIT();
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -210,6 +211,10 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
   }
   __syncwarp();
 
+  // The next kernel on the stream may begin launching once every CTA is here (its CTAs wait in
+  // griddepcontrol.wait until this grid has completed): launching it at the start instead
+  // measured slower, its early CTAs holding SMs this kernel's clusters could use.
+  pdl_launch_dependents();
   // ---- epilogue --------------------------------------------------------------------------
   const bool epi = warp >= 2;
   const uint32_t quad = warp & 3u;                      // TMEM lane quadrant of this warp
