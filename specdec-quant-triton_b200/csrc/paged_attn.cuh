@@ -336,15 +336,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     r.soff = steady_pages ? static_cast<int64_t>(r.tok0 & (p.page - 1)) * p.s_so + static_cast<int64_t>(kvh) * p.s_sh : 0;
     return r;
   };
-  auto fetch_scale = [&](const void* base, int j, const ScaleRow& r, float* dst, uint32_t& sel, int slot) {
-    int pg = -1;
+  // The page of token row r.row in block j (-1 past the split end).  Split from fetch_scale so
+  // the shared-memory read can be issued early and consumed later in the block.
+  auto scale_page = [&](int j, const ScaleRow& r) -> int {
+    if (steady_pages) return (j < nblk && r.tok0 + j * 128 < t_end) ? pages_s[r.pidx0 + j * r.pstep] : -1;
+    return token_page(j, r.row);
+  };
+  auto fetch_scale = [&](const void* base, int j, const ScaleRow& r, int pg, float* dst, uint32_t& sel, int slot) {
     int64_t off = 0;
     if (steady_pages) {
-      if (j < nblk && r.tok0 + j * 128 < t_end) pg = pages_s[r.pidx0 + j * r.pstep];
       off = static_cast<int64_t>(pg) * p.s_sp + r.soff;
-    } else {
-      pg = token_page(j, r.row);
-      if (pg >= 0) off = scale_offset(j, r.row, pg);
+    } else if (pg >= 0) {
+      off = scale_offset(j, r.row, pg);
     }
     if (page_ok(pg)) {
       if (p.scale_f32) {
@@ -511,13 +514,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     float* ksd = ks_ring + t;     // this thread's K-scale slots (stride 256)
     uint32_t ksel = 0u;
     const ScaleRow krow = scale_row(tl);
-    fetch_scale(p.ks, 0, krow, ksd, ksel, 0);
-    fetch_scale(p.ks, 1, krow, ksd + 256, ksel, 1);
+    fetch_scale(p.ks, 0, krow, scale_page(0, krow), ksd, ksel, 0);
+    fetch_scale(p.ks, 1, krow, scale_page(1, krow), ksd + 256, ksel, 1);
     int slot = 0;                 // j % 3
 #pragma unroll 1
     for (int j = 0; j < nblk; ++j) {
       const int slot2 = slot == 0 ? 2 : slot - 1;   // (j + 2) % 3
-      fetch_scale(p.ks, j + 2, krow, ksd + 256 * slot2, ksel, slot2);
+      // page of this token in block j + 2: the read is issued here, its scale fetched after
+      // this block's P pass (the shared-memory latency then hides behind the block's work)
+      const int pg2 = scale_page(j + 2, krow);
       const int t_abs = t_begin + j * 128 + tl;
       const uint32_t sb = static_cast<uint32_t>(j & 1);
       const uint32_t par2 = static_cast<uint32_t>(j >> 1) & 1u;
@@ -525,7 +530,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const int q_stop = (t_abs < t_end) ? rows_valid : 0;
       const int q_first = min(max(0, (t_abs - qpos0) * p.g), q_stop);
       if (t == 0) SPECQ_TRACE_POINT(20, j);
-      cp_async_wait<2>();   // block j's scale (fetched two blocks ago) has landed
+      cp_async_wait<1>();   // block j's scale (fetched two blocks ago) has landed
       // this token's score scale: K scale x log2(e) / sqrt(D) x the query scale
       const float a_t = read_scale(ksd + 256 * slot, ksel, slot) * p.sm_scale_log2 * q_scale;
       // S(j) is ready; its commit also covers PV(j-2), so P buffer sb is free as well
@@ -651,6 +656,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[sb]);
       if (t == 0) SPECQ_TRACE_POINT(24, j);
+      fetch_scale(p.ks, j + 2, krow, pg2, ksd + 256 * slot2, ksel, slot2);
       slot = slot == 2 ? 0 : slot + 1;
     }
     cp_async_wait<0>();
@@ -818,13 +824,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     float* vsd = vs_ring + c;     // this thread's V-scale slots (stride 128)
     uint32_t vsel = 0u;
     const ScaleRow vrow_s = scale_row(c);
-    fetch_scale(p.vs, 0, vrow_s, vsd, vsel, 0);
-    fetch_scale(p.vs, 1, vrow_s, vsd + 128, vsel, 1);
+    fetch_scale(p.vs, 0, vrow_s, scale_page(0, vrow_s), vsd, vsel, 0);
+    fetch_scale(p.vs, 1, vrow_s, scale_page(1, vrow_s), vsd + 128, vsel, 1);
     int slot = 0;                 // j % 3
 #pragma unroll 1
     for (int j = 0; j < nblk; ++j) {
       const int slot2 = slot == 0 ? 2 : slot - 1;   // (j + 2) % 3
-      fetch_scale(p.vs, j + 2, vrow_s, vsd + 128 * slot2, vsel, slot2);
+      const int pg2 = scale_page(j + 2, vrow_s);      // fetched after this block's conversion
       const int s = j % kAttnStages;
       const uint32_t sb = static_cast<uint32_t>(j & 1);
       ok = ok && mbar_wait(&stage_full[s], static_cast<uint32_t>(j / kAttnStages) & 1u, status,
@@ -835,7 +841,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch)
         raw[ch] = *reinterpret_cast<const uint4*>(vrow + ((static_cast<uint32_t>(ch) ^ (static_cast<uint32_t>(c) & 7u)) << 4));
-      cp_async_wait<2>();   // block j's scale (fetched two blocks ago) has landed
+      cp_async_wait<1>();   // block j's scale (fetched two blocks ago) has landed
       // the token's V scale in fp16 (exact for fp16 scales; one rounding for fp32 scales), so
       // the per-element multiply stays on the fp16 pipe
       const __half2 s2 = __half2half2(__float2half_rn(read_scale(vsd + 128 * slot, vsel, slot)));
@@ -864,6 +870,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         mbar_arrive(&stage_empty[s]);   // the V half of the stage is consumed
       }
       if (c == 0) SPECQ_TRACE_POINT(45, j);
+      fetch_scale(p.vs, j + 2, vrow_s, pg2, vsd + 128 * slot2, vsel, slot2);
       slot = slot == 2 ? 0 : slot + 1;
     }
     cp_async_wait<0>();

@@ -411,12 +411,15 @@ __device__ __forceinline__ void cluster_wait() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// Atomically add `v` to the u32 at `remote` (a shared::cluster address in a peer CTA) and
-// count 4 bytes on that CTA's mbarrier `remote_bar` (complete_tx); fire-and-forget.
-__device__ __forceinline__ void red_async_add_u32(uint32_t remote, uint32_t v, uint32_t remote_bar) {
+// Bulk asynchronous reduction (u32 add) of `bytes` bytes of this CTA's shared memory into a
+// peer CTA's shared memory, counted on the peer's mbarrier (complete_tx).  dst_cluster and
+// bar_cluster are shared::cluster addresses (dsmem_map); 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_reduce_add_u32_cluster(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes,
+                                                            uint32_t bar_cluster) {
   asm volatile(
-      "red.async.relaxed.cluster.shared::cluster.mbarrier::complete_tx::bytes.add.u32 [%0], %1, [%2];" ::"r"(remote),
-      "r"(v), "r"(remote_bar)
+      "cp.reduce.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes.add.u32 [%0], [%1], %2, [%3];" ::"r"(
+          dst_cluster),
+      "r"(src_cta), "r"(bytes), "r"(bar_cluster)
       : "memory");
 }
 

@@ -66,7 +66,8 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
   uint64_t* full = bars;
   uint64_t* empty = bars + kW8A8MaxStages;
   uint64_t* acc_full = bars + 2 * kW8A8MaxStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kW8A8MaxStages + 1);
+  uint64_t* red_full = acc_full + 1;                          // split-K: the peers' rows landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kW8A8MaxStages + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* sa_s = reinterpret_cast<float*>(tmem_slot + 4);      // [256] token scales of this chunk
   float* sw_s = sa_s + 256;                                   // [128] channel scales of this tile
@@ -113,6 +114,7 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
       mbar_init(&empty[s], 1u);
     }
     mbar_init(acc_full, 1u);
+    mbar_init(red_full, 1u);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -123,11 +125,6 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
   if (warp == 1) {
     tmem_alloc(tmem_slot, p.tmem_cols);
     tmem_relinquish();
-  }
-  if (warp >= 2 && p.acc_out == nullptr) {   // epilogue scales staged once, read from smem
-    const int te = static_cast<int>(threadIdx.x) - 64;
-    for (int i = te; i < m_cnt; i += 128) sa_s[i] = __ldg(p.sa + m0 + i);
-    sw_s[te] = (n0 + te < p.N) ? __ldg(p.sw + n0 + te) : 0.f;
   }
   tc_fence_before();
   __syncthreads();
@@ -190,8 +187,15 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
       umma_commit(acc_full);      // accumulator complete
     }
   } else {
-    // epilogue warps; in the LDG variant they first produce every stage
+    // epilogue warps; in the LDG variant they first produce every stage.  They stage the
+    // epilogue's scales in shared memory while the main loop runs (not before it starts).
     const int te = static_cast<int>(threadIdx.x) - 64;   // 0..127
+    auto stage_scales = [&]() {
+      if (p.acc_out != nullptr) return;
+      for (int i = te; i < m_cnt; i += 128) sa_s[i] = __ldg(p.sa + m0 + i);
+      sw_s[te] = (n0 + te < p.N) ? __ldg(p.sw + n0 + te) : 0.f;
+    };
+    if constexpr (VEC == 0) stage_scales();
     if constexpr (VEC != 0) {
       const uint8_t* wbase = reinterpret_cast<const uint8_t*>(p.w);
       const uint8_t* abase = reinterpret_cast<const uint8_t*>(p.a);
@@ -207,6 +211,7 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
         fence_proxy_async_smem();
         mbar_arrive(&full[s]);
       }
+      stage_scales();
     }
   }
   __syncwarp();
@@ -223,6 +228,7 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
   if (epi) {
     ok = mbar_wait(acc_full, 0u, p.status, SPECQ_STATUS_TIMEOUT_MMA) && (*abort_flag == 0);
     tc_fence_after();
+    named_barrier_sync(1, 128);   // every epilogue thread's staged scales are visible
     if (warp == 2 && lane == 0) SPECQ_TRACE_POINT(5, 0);
   }
 
@@ -252,64 +258,108 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
       }
     }
   } else {
-    // Split-K, push model: CTA r owns tile rows [r*R, (r+1)*R).  After a cluster barrier (every
-    // ring idle), each CTA stores the INT32 partial of every row straight into the owner's
-    // shared memory (st.shared::cluster, fire-and-forget), slot [source split][row]; after a
-    // second barrier each CTA sums its own rows locally -- INT32 addition is exact, so the
-    // bits do not depend on the order.  All warps take part in both cluster barriers.
+    // Split-K: CTA r owns tile rows (channels) [r*R, (r+1)*R).  Every CTA parks its whole INT32
+    // partial in its idle ring ([128 rows][pitch]); after one cluster barrier each CTA adds the
+    // rows a peer owns into that peer's copy with one bulk asynchronous reduction per peer
+    // (cp.reduce.async.bulk .add, completing on the owner's mbarrier), so the owner's rows hold
+    // the full sums without a summation pass.  INT32 addition is exact: the bits do not depend
+    // on the order.  A second cluster barrier (arrive once the own rows are complete, wait after
+    // the output stores) keeps every CTA, and the ring its reductions read, alive until all of
+    // them have landed.
     const int S = p.splits;
     const int lgR = 7 - (31 - __clz(S));       // rows owned by one CTA: R = 128 / S
     const int R = 1 << lgR;
     const uint32_t pitch = n_pad * 4u + 16u;   // padded row pitch: conflict-free v4 access
-    cluster_sync();
-    if (warp == 2 && lane == 0) SPECQ_TRACE_POINT(6, 0);
     if (epi && ok) {
-      const uint32_t dst = dsmem_map(smem_u32(ring), static_cast<uint32_t>(row >> lgR)) +
-                           static_cast<uint32_t>(split * R + (row & (R - 1))) * pitch;
+      uint8_t* dst = ring + static_cast<uint32_t>(row) * pitch;
       for (uint32_t c0 = 0; c0 < n_pad; c0 += 16) {
         uint32_t r[16];
         tmem_ld16(tmem_acc + ((quad * 32u) << 16) + c0, r);
         tmem_wait_ld();
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4)
-          dsmem_st_v4(dst + c0 * 4u + 16u * q4, make_uint4(r[4 * q4], r[4 * q4 + 1], r[4 * q4 + 2], r[4 * q4 + 3]));
+          *reinterpret_cast<uint4*>(dst + c0 * 4u + 16u * q4) =
+              make_uint4(r[4 * q4], r[4 * q4 + 1], r[4 * q4 + 2], r[4 * q4 + 3]);
+      }
+      fence_proxy_async_smem();   // the bulk reductions read the ring through the async proxy
+    }
+    cluster_sync();   // every CTA's partial is parked; every ring is idle
+    if (warp == 2 && lane == 0) SPECQ_TRACE_POINT(6, 0);
+    const uint32_t blk = static_cast<uint32_t>(R) * pitch;   // bytes of one owner's rows
+    if (threadIdx.x == 64) {   // one epilogue thread issues this CTA's reductions
+      mbar_arrive_expect_tx(red_full, static_cast<uint32_t>(S - 1) * blk);
+      for (int q = 0; q < S; ++q) {
+        if (q == split) continue;
+        const uint32_t off = static_cast<uint32_t>(q) * blk;
+        bulk_reduce_add_u32_cluster(dsmem_map(smem_u32(ring) + off, static_cast<uint32_t>(q)), smem_u32(ring) + off, blk,
+                                    dsmem_map(smem_u32(red_full), static_cast<uint32_t>(q)));
       }
     }
-    cluster_sync();   // every partial has landed; nothing remote is touched after this
+    bool red_ok = true;
+    if (epi) red_ok = mbar_wait(red_full, 0u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE);
     if (warp == 2 && lane == 0) SPECQ_TRACE_POINT(7, 0);
-    if (epi && ok) {
-      const int nq = static_cast<int>(n_pad >> 2);
+    // this CTA's incoming reductions have landed: arrive now, wait (for the peers' to have
+    // landed too, so every ring may be released) after the output stores
+    cluster_arrive();
+    if (epi && ok && red_ok) {
       const int te = static_cast<int>(threadIdx.x) - 64;
-      for (int item = te; item < R * nq; item += 128) {
-        const int rl = item % R;          // consecutive threads: consecutive rows (pitch-padded)
-        const int cq = item / R;
-        int4 acc = make_int4(0, 0, 0, 0);
-        for (int pr = 0; pr < S; ++pr) {
-          const int4 v = *reinterpret_cast<const int4*>(ring + (pr * R + rl) * pitch + cq * 16);
-          acc.x += v.x;
-          acc.y += v.y;
-          acc.z += v.z;
-          acc.w += v.w;
-        }
-        const int n = n0 + split * R + rl;
-        if (n < p.N) {
-          const int32_t sv[4] = {acc.x, acc.y, acc.z, acc.w};
-          const float swn = sw_s[n - n0];
+      const uint8_t* own = ring + static_cast<uint32_t>(split * R) * pitch;
+      const bool vec = p.acc_out == nullptr && p.ldo_n == 1 && (p.ldo % 8) == 0 &&
+                       (reinterpret_cast<uintptr_t>(p.out) & 15u) == 0 && (n0 + split * R) % 8 == 0;
+      if (vec) {
+        // item = (token m, 8 consecutive owned channels): eight row reads, one 16-byte store
+        const int ng = R >> 3;
+        for (int item = te; item < ng * static_cast<int>(n_pad); item += 128) {
+          const int m = item % static_cast<int>(n_pad);
+          const int g = item / static_cast<int>(n_pad);
+          if (m0 + m >= M) continue;
+          const int nl = split * R + 8 * g;          // first channel of the group in the tile
+          const float sam = sa_s[m];
+          uint32_t hw[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int m = m0 + cq * 4 + j;
-            if (m < M) {
-              if (p.acc_out != nullptr) {
-                p.acc_out[static_cast<int64_t>(m) * p.ldacc + n] = sv[j];
-              } else {
-                const float val = __fmul_rn(__fmul_rn(static_cast<float>(sv[j]), sa_s[m - m0]), swn);
-                p.out[static_cast<int64_t>(m) * p.ldo + static_cast<int64_t>(n) * p.ldo_n] = __float2half_rn(val);
+          for (int k = 0; k < 8; k += 2) {
+            const int32_t v0 = *reinterpret_cast<const int32_t*>(own + (8 * g + k) * pitch + m * 4);
+            const int32_t v1 = *reinterpret_cast<const int32_t*>(own + (8 * g + k + 1) * pitch + m * 4);
+            const __half2 h = __floats2half2_rn(__fmul_rn(__fmul_rn(static_cast<float>(v0), sam), sw_s[nl + k]),
+                                                __fmul_rn(__fmul_rn(static_cast<float>(v1), sam), sw_s[nl + k + 1]));
+            hw[k >> 1] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          const int n = n0 + nl;
+          if (n + 8 <= p.N) {
+            *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(m0 + m) * p.ldo + n) =
+                make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          } else {
+            const __half* hv = reinterpret_cast<const __half*>(hw);
+            for (int k = 0; k < 8 && n + k < p.N; ++k) p.out[static_cast<int64_t>(m0 + m) * p.ldo + n + k] = hv[k];
+          }
+        }
+      } else {
+        const int nq = static_cast<int>(n_pad >> 2);
+        for (int item = te; item < R * nq; item += 128) {
+          const int rl = item % R;          // consecutive threads: consecutive rows (pitch-padded)
+          const int cq = item / R;
+          const int4 acc = *reinterpret_cast<const int4*>(own + rl * pitch + cq * 16);
+          const int n = n0 + split * R + rl;
+          if (n < p.N) {
+            const int32_t sv[4] = {acc.x, acc.y, acc.z, acc.w};
+            const float swn = sw_s[n - n0];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int m = m0 + cq * 4 + j;
+              if (m < M) {
+                if (p.acc_out != nullptr) {
+                  p.acc_out[static_cast<int64_t>(m) * p.ldacc + n] = sv[j];
+                } else {
+                  const float val = __fmul_rn(__fmul_rn(static_cast<float>(sv[j]), sa_s[m - m0]), swn);
+                  p.out[static_cast<int64_t>(m) * p.ldo + static_cast<int64_t>(n) * p.ldo_n] = __float2half_rn(val);
+                }
               }
             }
           }
         }
       }
     }
+    cluster_wait();   // every reduction into every CTA has landed: rings may be released
     if (warp == 2 && lane == 0) SPECQ_TRACE_POINT(8, 0);
   }
 
