@@ -1109,8 +1109,12 @@ inline int run_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_
   // Split count from the block-table width only (never from B or the plan), so eager and
   // plan-mode launches reduce identical partials.
   const int max_ctx = bt_cols * page;
-  // A power of two (each split owns 128 / splits head dims in the combine).
-  p.splits = std::min(8, next_pow2(std::max(1, ceil_div(max_ctx, 2048))));
+  // A power of two (each split owns 128 / splits head dims in the combine): at least one split
+  // per 2048 tokens, and more when a shard holds few KV heads (tensor-parallel shards keep the
+  // SMs busy), but clusters of 8 only with one KV head: 16 such clusters do not fit the GPU in
+  // one wave.  Splits of fewer than 512 tokens are not made.
+  const int by_heads = H_KV >= 8 ? 2 : (H_KV >= 2 ? 4 : 8);
+  p.splits = std::min(8, next_pow2(std::max({1, ceil_div(max_ctx, 2048), std::min(by_heads, ceil_div(max_ctx, 512))})));
   p.stages = kAttnStages;
   p.sm_scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
   // TMEM: two score buffers (hi and lo int32 columns), O^T, normaliser, 16 columns of constant

@@ -14,7 +14,9 @@ activation (int8) and the down-projection output (fp16), plus one all-reduce (MA
 activation's per-token amax, so every rank quantises its slice with the whole row's scale.
 Every kernel computes each output column exactly as the single-GPU stack does (W8A8 sums in
 int32 whatever the column split), so the tensor-parallel residual stream equals the single-GPU
-one bit for bit.
+one bit for bit whenever the attention splits each context the same way on both (the split
+count follows the context length and the KV heads a GPU holds; at the stack's 1024-token
+contexts it is 2 on one GPU and on a 2-way shard).
 
 Under the plan graph the collectives move the maximum grid's rows (a graph fixes their sizes);
 eager steps move the active rows.
