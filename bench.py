@@ -415,15 +415,15 @@ def run_ours(args):
     _barrier(world)
     step_ms = _max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
 
-    # per-kernel launch durations (CUDA events around captured runs of one kernel over the
-    # rotating copies), for the roofline of each kernel
+    # per-kernel launch durations (CUDA events around captured chains of chain_len launches of
+    # one kernel over the rotating copies, like the step chains), for the roofline of each kernel
     per_kernel = {}
     for name in ("w8a8", "w4a16", "paged_attention"):
-        g = _capture([_kernels(x)[name] for x in inputs])
+        g = _capture([_kernels(inputs[i % n_copies])[name] for i in range(chain_len)])
         g.replay()
         torch.cuda.synchronize()
         # long enough (~0.7 s) for the clock sampler to see the GPU under load
-        reps = max(5, min(20000, int(700.0 / max(step_ms, 1e-3) / n_copies)))
+        reps = max(5, min(20000, int(700.0 / max(step_ms, 1e-3) / chain_len)))
         if args.per_kernel_reps:
             reps = args.per_kernel_reps
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -432,7 +432,7 @@ def run_ours(args):
             g.replay()
         b.record()
         torch.cuda.synchronize()
-        per_kernel[name] = _max_over_ranks(a.elapsed_time(b) * 1e3 / (reps * n_copies), world)   # us
+        per_kernel[name] = _max_over_ranks(a.elapsed_time(b) * 1e3 / (reps * chain_len), world)   # us
         del g
     clocks = sampler.stop()
 
@@ -508,7 +508,7 @@ def run_ours(args):
         "timing": {"l2": f"{n_copies} rotating input copies of {copy_bytes / 1e6:.1f} MB (> 2x L2)",
                    "method": f"CUDA events around K steps, replayed as captured chains of {chain_len} steps "
                              "(kernels launched with programmatic dependent launch); per-kernel: events around "
-                             "captured runs of that kernel over the copies"},
+                             f"captured chains of {chain_len} launches of that kernel over the copies"},
         "kernels": kern,
         "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": traffic,

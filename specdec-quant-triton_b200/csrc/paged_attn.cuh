@@ -209,11 +209,13 @@ template <int NQ>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     paged_attn_kernel(const __grid_constant__ AttnParams p, const __grid_constant__ CUtensorMap tmap_k,
                       const __grid_constant__ CUtensorMap tmap_v) {
-  pdl_wait();                // the previous kernel's writes are visible from here on
   static_assert(NQ % 16 == 0 && NQ >= 16 && NQ <= 64, "query rows per CTA");
   constexpr int NQH = NQ / 2;   // query columns per softmax thread
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   SPECQ_TRACE_INIT();
+  if (threadIdx.x == 0) SPECQ_TRACE_POINT(0, 0);
+  pdl_wait();                // the previous kernel's writes are visible from here on
+  if (threadIdx.x == 0) SPECQ_TRACE_POINT(3, 0);
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // ring stage: [K int8, 128 tokens x 128 B, 128B-swizzled (a tcgen05 operand as it lands)]
   //             [V int8, 128 tokens x 128 B, 128B-swizzled (read row-wise by the V warps)]

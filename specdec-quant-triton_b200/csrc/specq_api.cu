@@ -30,8 +30,8 @@ namespace {
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in per block on sm_100
 
 template <int VEC>
-int launch_w8a8_variant(const W8A8Params& p, const CUtensorMap& tw, const CUtensorMap& ta, dim3 grid, int smem,
-                        cudaStream_t stream) {
+int launch_w8a8_variant(const W8A8Params& p, const CUtensorMap& tw, const CUtensorMap& ta, const CUtensorMap& tac,
+                        dim3 grid, int smem, cudaStream_t stream) {
   auto kern = w8a8_kernel<VEC>;
   SPECQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   cudaLaunchConfig_t cfg = {};
@@ -41,7 +41,7 @@ int launch_w8a8_variant(const W8A8Params& p, const CUtensorMap& tw, const CUtens
   cfg.stream = stream;
   LaunchAttrs attrs(p.splits);
   attrs.apply(cfg);
-  SPECQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p, tw, ta));
+  SPECQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p, tw, ta, tac));
   return SPECQ_OK;
 }
 
@@ -113,9 +113,10 @@ int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int
 
   // TMA needs 16-byte aligned bases and row strides; otherwise use the register-staged loader.
   const bool tma_ok = aligned(a, 16) && aligned(w, 16) && (lda % 16 == 0) && (ldw % 16 == 0);
-  CUtensorMap tw, ta;
+  CUtensorMap tw, ta, tac;
   memset(&tw, 0, sizeof(tw));
   memset(&ta, 0, sizeof(ta));
+  memset(&tac, 0, sizeof(tac));
   int vec = 0;
   if (tma_ok) {
     const uint64_t dw[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
@@ -126,21 +127,25 @@ int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int
     const uint64_t sa_[1] = {static_cast<uint64_t>(lda)};
     const uint32_t ba[2] = {128, 16};
     if (int rc = encode_tiled(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a, da, sa_, ba, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+    const uint32_t bac[2] = {128, static_cast<uint32_t>(p.chunk)};   // a whole token chunk
+    if (int rc = encode_tiled(&tac, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a, da, sa_, bac, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
   } else {
     vec = common_vec_width({reinterpret_cast<uintptr_t>(a), reinterpret_cast<uintptr_t>(w),
                             static_cast<uint64_t>(lda), static_cast<uint64_t>(ldw), static_cast<uint64_t>(K)});
   }
 
-  const dim3 grid(static_cast<unsigned>(S), static_cast<unsigned>(n_tiles), static_cast<unsigned>(n_chunks));
+  // (split, chunk, tile): a tile's chunks launch back to back and share its weights through L2
+  if (n_tiles > 65535) return fail(SPECQ_ERR_UNSUPPORTED, "w8a8: N=%d exceeds the grid", N);
+  const dim3 grid(static_cast<unsigned>(S), static_cast<unsigned>(n_chunks), static_cast<unsigned>(n_tiles));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc;
   switch (vec) {
-    case 0: rc = launch_w8a8_variant<0>(p, tw, ta, grid, smem, st); break;
-    case 16: rc = launch_w8a8_variant<16>(p, tw, ta, grid, smem, st); break;
-    case 8: rc = launch_w8a8_variant<8>(p, tw, ta, grid, smem, st); break;
-    case 4: rc = launch_w8a8_variant<4>(p, tw, ta, grid, smem, st); break;
-    case 2: rc = launch_w8a8_variant<2>(p, tw, ta, grid, smem, st); break;
-    default: rc = launch_w8a8_variant<1>(p, tw, ta, grid, smem, st); break;
+    case 0: rc = launch_w8a8_variant<0>(p, tw, ta, tac, grid, smem, st); break;
+    case 16: rc = launch_w8a8_variant<16>(p, tw, ta, tac, grid, smem, st); break;
+    case 8: rc = launch_w8a8_variant<8>(p, tw, ta, tac, grid, smem, st); break;
+    case 4: rc = launch_w8a8_variant<4>(p, tw, ta, tac, grid, smem, st); break;
+    case 2: rc = launch_w8a8_variant<2>(p, tw, ta, tac, grid, smem, st); break;
+    default: rc = launch_w8a8_variant<1>(p, tw, ta, tac, grid, smem, st); break;
   }
   if (rc == SPECQ_OK) {
     LaunchRecord& r = last_launch_ref();

@@ -98,7 +98,6 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
     w4a16_kernel(const __grid_constant__ W4A16Params p, const __grid_constant__ CUtensorMap tmap_wp,
                  const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_sc,
                  const __grid_constant__ CUtensorMap tmap_a_chunk) {
-  pdl_wait();                // the previous kernel's writes are visible from here on
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   SPECQ_TRACE_INIT();
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -125,6 +124,27 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
   const int n0 = blockIdx.y * 128;
   const int m0 = blockIdx.z * p.chunk;
   const int half_k = p.K / 2;
+  const int kb0 = split * p.kb_per_split;
+  const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
+  const int nkb = kb1 - kb0;
+  // Each N tile walks its K range from a different starting block, so the CTAs do not all
+  // read the same activation lines (one set of L2 slices) at the same time.  The order depends
+  // only on the tile, never on M: plan and non-plan launches add the same partial products in
+  // the same order.
+  const int rot = nkb > 0 ? static_cast<int>((static_cast<int64_t>(blockIdx.y) * 5) % nkb) : 0;
+  auto kblock = [&](int i) { return kb0 + (i + rot < nkb ? i + rot : i + rot - nkb); };
+
+  // While the previous kernel on the stream finishes, warm L2 with this CTA's scale tile and
+  // first packed weight tiles (the first token chunk only: later chunks find them there).
+  if (threadIdx.x == 0 && blockIdx.z == 0) {
+    tma_prefetch_desc(&tmap_wp);
+    if (p.sc_cache_cols > 0) {
+      tma_prefetch_desc(&tmap_sc);
+      tma_prefetch_l2_2d(&tmap_sc, 0, n0);
+    }
+    for (int i = 0; i < min(nkb, p.stages); ++i) tma_prefetch_l2_2d(&tmap_wp, kblock(i) * 64, n0);
+  }
+  pdl_wait();                // the previous kernel's writes are visible from here on
 
   int M = p.m_rows;
   if (p.plan != nullptr) {
@@ -142,15 +162,6 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
   const int a_rows = (m_cnt + 15) & ~15;                       // TMA boxes of 16 rows
   const uint32_t a_bytes = static_cast<uint32_t>(a_rows) * 128u;
 
-  const int kb0 = split * p.kb_per_split;
-  const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
-  const int nkb = kb1 - kb0;
-  // Each N tile walks its K range from a different starting block, so the CTAs do not all
-  // read the same activation lines (one set of L2 slices) at the same time.  The order depends
-  // only on the tile, never on M: plan and non-plan launches add the same partial products in
-  // the same order.
-  const int rot = nkb > 0 ? static_cast<int>((static_cast<int64_t>(blockIdx.y) * 5) % nkb) : 0;
-  auto kblock = [&](int i) { return kb0 + (i + rot < nkb ? i + rot : i + rot - nkb); };
   if (threadIdx.x == 0) SPECQ_TRACE_POINT(0, 0);
 
   if (threadIdx.x == 0) {

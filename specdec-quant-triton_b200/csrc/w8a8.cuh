@@ -9,9 +9,14 @@
 //     holds the INT32 accumulators of up to 256 tokens for its 128 channels in TMEM, so the
 //     weights are streamed from HBM once whatever M = B*(k+1) is -- there is no M-tile
 //     staircase (the reference re-streams the weights for every BLOCK_M rows).
-//   * TMA loads 128-byte-swizzled [128 x 128 B] weight tiles and [32-row x 128 B] activation
-//     boxes into a multi-stage mbarrier ring; one elected thread issues tcgen05.mma
-//     kind::i8 (M=128, N=tokens rounded up to 16, K=32 per instruction).
+//   * TMA loads 128-byte-swizzled [128 x 128 B] weight tiles and the token chunk's activations
+//     (one box of the whole chunk, or 16-row boxes for a ragged last chunk) into a multi-stage
+//     mbarrier ring; one elected thread issues tcgen05.mma kind::i8 (M=128, N=tokens rounded
+//     up to 16, K=32 per instruction).
+//   * Grid (split, chunk, tile): the CTAs of one weight tile are adjacent in launch order, so
+//     a tile's second token chunk reads the weights from L2 while the first streams them.
+//     Each tile walks its K range from its own starting block, so the CTAs do not all read
+//     the same activation lines (one set of L2 slices) at once.
 //   * Split-K across a thread-block cluster along grid.x fills the 148 SMs at small N; the
 //     INT32 partials are reduced through distributed shared memory, no HBM partials.
 //     Integer addition is exact, so any split gives the same bits.
@@ -56,8 +61,7 @@ constexpr int kW8A8MaxStages = 8;
 template <int VEC>
 __global__ void __launch_bounds__(kW8A8Threads, 1)
     w8a8_kernel(const __grid_constant__ W8A8Params p, const __grid_constant__ CUtensorMap tmap_w,
-                const __grid_constant__ CUtensorMap tmap_a) {
-  pdl_wait();                // the previous kernel's writes are visible from here on
+                const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_a_chunk) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   SPECQ_TRACE_INIT();
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -75,8 +79,22 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
   const int split = blockIdx.x;             // == cluster rank (cluster spans grid.x)
-  const int n0 = blockIdx.y * 128;
-  const int m0 = blockIdx.z * p.chunk;
+  const int n0 = blockIdx.z * 128;
+  const int m0 = blockIdx.y * p.chunk;
+  const int kb0 = split * p.kb_per_split;
+  const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
+  const int nkb = kb1 - kb0;                                          // >= 1 (host guarantees)
+  // K blocks in a per-tile rotated order (INT32 sums do not depend on the order)
+  const int rot = static_cast<int>((static_cast<int64_t>(blockIdx.z) * 5) % nkb);
+  auto kblock = [&](int i) { return kb0 + (i + rot < nkb ? i + rot : i + rot - nkb); };
+
+  // While the previous kernel on the stream finishes, warm L2 with this CTA's first weight
+  // tiles (the first token chunk only: later chunks of the tile find them there).
+  if (VEC == 0 && threadIdx.x == 0 && blockIdx.y == 0) {
+    tma_prefetch_desc(&tmap_w);
+    for (int i = 0; i < min(nkb, kW8A8MaxStages); ++i) tma_prefetch_l2_2d(&tmap_w, kblock(i) * 128, n0);
+  }
+  pdl_wait();                // the previous kernel's writes are visible from here on
 
   // ---- active extent (plan mode reads M on the device) --------------------------------
   int M = p.m_rows;
@@ -94,17 +112,13 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
   // together and no cluster barrier is left waiting.
   if (m_cnt <= 0) return;
   const uint32_t n_pad = static_cast<uint32_t>((m_cnt + 15) & ~15);   // MMA N
-  const int a_rows = (m_cnt + 15) & ~15;                               // TMA boxes of 16 rows
+  const int a_rows = (m_cnt + 15) & ~15;                               // activation rows staged
   const uint32_t a_bytes = static_cast<uint32_t>(a_rows) * 128u;
   // The ring is cut for the ACTIVE chunk: under a plan-buffer graph the launch is sized for
   // the largest M, and a smaller active M then gets more, smaller stages (more weight bytes
   // in flight) from the same shared memory.
   const uint32_t stage_bytes = kW8A8WTile + a_bytes;   // a multiple of 2048: TMA-aligned stages
   const int stages = min(kW8A8MaxStages, static_cast<int>(p.ring_bytes / stage_bytes));
-
-  const int kb0 = split * p.kb_per_split;
-  const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
-  const int nkb = kb1 - kb0;                                          // >= 1 (host guarantees)
   if (threadIdx.x == 0) SPECQ_TRACE_POINT(0, 0);
 
   // ---- setup ---------------------------------------------------------------------------
@@ -121,6 +135,7 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
   if (warp == 0 && VEC == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_w);
     tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_a_chunk);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, p.tmem_cols);
@@ -146,9 +161,13 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
         uint8_t* wt = ring + s * stage_bytes;
         uint8_t* at = wt + kW8A8WTile;
         mbar_arrive_expect_tx(&full[s], kW8A8WTile + a_bytes);
-        const int kx = (kb0 + i) * 128;
+        const int kx = kblock(i) * 128;
         tma_load_2d(wt, &tmap_w, &full[s], kx, n0, pol_w);
-        for (int r = 0; r < a_rows; r += 16) tma_load_2d(at + r * 128, &tmap_a, &full[s], kx, m0 + r, pol_a);
+        if (a_rows == p.chunk) {   // a whole chunk: one box (TMA issue is serial)
+          tma_load_2d(at, &tmap_a_chunk, &full[s], kx, m0, pol_a);
+        } else {
+          for (int r = 0; r < a_rows; r += 16) tma_load_2d(at + r * 128, &tmap_a, &full[s], kx, m0 + r, pol_a);
+        }
         ++issued;
         if (++s == stages) {
           s = 0;
@@ -205,7 +224,7 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
         if (!mbar_wait(&empty[s], ph ^ 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
         uint8_t* wt = ring + s * stage_bytes;
         uint8_t* at = wt + kW8A8WTile;
-        const int kx = (kb0 + i) * 128;
+        const int kx = kblock(i) * 128;
         ldg_tile_sw128<VEC>(wt, wbase, p.ldw, n0, 128, p.N, kx, p.K, te, 128);
         ldg_tile_sw128<VEC>(at, abase, p.lda, m0, a_rows, M, kx, p.K, te, 128);
         fence_proxy_async_smem();
