@@ -213,7 +213,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   constexpr int NQH = NQ / 2;   // query columns per softmax thread
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   SPECQ_TRACE_INIT();
-  if (threadIdx.x == 0) SPECQ_TRACE_POINT(0, 0);
+  if (threadIdx.x == 0) {
+    SPECQ_TRACE_POINT(0, 0);
+    tma_prefetch_desc(&tmap_k);   // kernel parameters: fetched while the previous kernel finishes
+    tma_prefetch_desc(&tmap_v);
+  }
   pdl_wait();                // the previous kernel's writes are visible from here on
   if (threadIdx.x == 0) SPECQ_TRACE_POINT(3, 0);
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -264,11 +268,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   }
   // the whole cluster (same blockIdx.y/z) leaves together
   if (b >= n_seqs || qc * p.qpp >= q_len) return;
-  int L = __ldg(p.ctx_len + b);
-  if (L < 0 || L > p.bt_cols * p.page) {
-    if (threadIdx.x == 0 && split == 0) report_status(p.status, SPECQ_STATUS_PLAN_CLAMPED);
-    L = min(max(L, 0), p.bt_cols * p.page);
-  }
   // A zero sequence stride means packed token rows (sequence b's token t at row
   // b * q_len + t): the stride follows the active q_len, e.g. a projection's output under a
   // plan-buffer graph.
@@ -277,6 +276,39 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int q_lo = qc * p.qpp;
   const int q_hi = min(q_lo + p.qpp, q_len);
   const int rows_valid = (q_hi - q_lo) * p.g;
+
+  // The sequence length, the block-table row (when it fits in shared memory) and the query
+  // rows do not depend on one another: they are all requested here, so the prologue waits for
+  // one memory round trip instead of three dependent ones.
+  int L = __ldg(p.ctx_len + b);
+  // softmax warps: the raw fp16 query pieces (row, 16 head dims) this thread quantises below
+  constexpr int kItems = (NQ * 8 + 255) / 256;
+  uint4 qraw[kItems][2];
+  if (warp < 8) {
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+      const int it = static_cast<int>(threadIdx.x) + 256 * k;
+      const int row = it >> 3;
+      const int piece = it & 7;
+      qraw[k][0] = qraw[k][1] = make_uint4(0u, 0u, 0u, 0u);
+      if (it < NQ * 8 && row < rows_valid) {
+        const int qi = q_lo + (p.g_shift >= 0 ? (row >> p.g_shift) : (row / p.g));
+        const int head = kvh * p.g + (p.g_shift >= 0 ? (row & (p.g - 1)) : (row % p.g));
+        const uint4* src = reinterpret_cast<const uint4*>(p.q + b * q_sb + static_cast<int64_t>(qi) * p.q_st +
+                                                          static_cast<int64_t>(head) * p.q_sh) + 2 * piece;
+        qraw[k][0] = __ldg(src);
+        qraw[k][1] = __ldg(src + 1);
+      }
+    }
+  }
+  const bool whole_row = p.bt_cols <= kAttnMaxPages;
+  if (whole_row)
+    for (int i = static_cast<int>(threadIdx.x); i < p.bt_cols; i += kAttnThreads)
+      pages_s[i] = __ldg(p.bt + b * p.bt_sb + i);
+  if (L < 0 || L > p.bt_cols * p.page) {
+    if (threadIdx.x == 0 && split == 0) report_status(p.status, SPECQ_STATUS_PLAN_CLAMPED);
+    L = min(max(L, 0), p.bt_cols * p.page);
+  }
   const int qpos0 = L - q_len + q_lo;                 // last visible token of query-row group 0
   const int kv_end = max(0, L - q_len + q_hi);
   const int tchunk = ((kv_end + p.splits - 1) / p.splits + 127) & ~127;
@@ -291,13 +323,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   constexpr uint32_t ONES_col = L_col + kOCols;
   auto page_of = [&](int tok) { return p.page_shift >= 0 ? (tok >> p.page_shift) : (tok / p.page); };
   auto slot_of = [&](int tok) { return p.page_shift >= 0 ? (tok & (p.page - 1)) : (tok % p.page); };
-  // The block-table entries of this CTA's token range, read once into shared memory: a page
-  // lookup is then a shared-memory read instead of a dependent global load (which takes
-  // longer than a whole block under full HBM load).
-  const int pg_first = page_of(t_begin);
-  const int pg_count = nblk > 0 ? page_of(t_end - 1) - pg_first + 1 : 0;
-  for (int i = static_cast<int>(threadIdx.x); i < pg_count; i += kAttnThreads)
-    pages_s[i] = __ldg(p.bt + b * p.bt_sb + pg_first + i);
+  // The block-table entries of this CTA's token range live in shared memory (the whole row
+  // read above, or else this range's entries, read here): a page lookup is then a
+  // shared-memory read instead of a dependent global load (which takes longer than a whole
+  // block under full HBM load).
+  const int pg_first = whole_row ? 0 : page_of(t_begin);
+  if (!whole_row) {
+    const int pg_count = nblk > 0 ? page_of(t_end - 1) - pg_first + 1 : 0;
+    for (int i = static_cast<int>(threadIdx.x); i < pg_count; i += kAttnThreads)
+      pages_s[i] = __ldg(p.bt + b * p.bt_sb + pg_first + i);
+  }
   // page id of token row `row` of block j (-1 past the split end)
   auto token_page = [&](int j, int row) -> int {
     const int tok = t_begin + j * 128 + row;
@@ -422,8 +457,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // hi, lo int8: two int8 operand rows each, so QK^T runs on the INT8 tensor core against
     // the raw K bytes.  One scale makes the score scale a per-token scalar (no per-column
     // constant); the rounding error of every row is relative to the CTA's largest |q|.
-    constexpr int kItems = (NQ * 8 + 255) / 256;   // (row, 16 head dims) pieces per thread
-    float qv[kItems][16];
+    float qv[kItems][16];   // (row, 16 head dims) pieces of this thread, loaded in the prologue
 #pragma unroll
     for (int k = 0; k < kItems; ++k) {
       const int it = t + 256 * k;
@@ -431,11 +465,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const int piece = it & 7;
       float amax = 0.f;
       if (it < NQ * 8 && row < rows_valid) {
-        const int qi = q_lo + (p.g_shift >= 0 ? (row >> p.g_shift) : (row / p.g));
-        const int head = kvh * p.g + (p.g_shift >= 0 ? (row & (p.g - 1)) : (row % p.g));
-        const uint4* src = reinterpret_cast<const uint4*>(p.q + b * q_sb + static_cast<int64_t>(qi) * p.q_st +
-                                                          static_cast<int64_t>(head) * p.q_sh) + 2 * piece;
-        const uint4 u0 = __ldg(src), u1 = __ldg(src + 1);
+        const uint4 u0 = qraw[k][0], u1 = qraw[k][1];
         const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -614,9 +644,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const int q = col0 + c0 + i;
-            float y = (q >= q_first && q < q_stop) ? score(rh[i], rl[i]) : -INFINITY;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) y = fmaxf(y, __shfl_xor_sync(0xffffffffu, y, o));
+            const float y = warp_max_f32((q >= q_first && q < q_stop) ? score(rh[i], rl[i]) : -INFINITY);
             if (lane == 0) wmax[quad * 64 + q] = y;
           }
         }
@@ -698,7 +726,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int br = p.box_rows;
     const int nbox = 128 >> p.box_shift;
     const uint64_t hint = policy_evict_first();
-    if (l == 0) tma_prefetch_desc(tmap);
     int s = 0;
     uint32_t phase = 0;
     int issued = 0;

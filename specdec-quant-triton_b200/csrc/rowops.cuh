@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_kernel(const __grid_co
     amax = fmaxf(amax, fabsf(v));
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  amax = warp_max_f32(amax);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
   __syncthreads();
   float m = 0.f;
@@ -182,7 +182,7 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_vec_kernel(const __gri
     }
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  amax = warp_max_f32(amax);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
   __syncthreads();
   float m = 0.f;
@@ -297,11 +297,8 @@ __global__ void __launch_bounds__(256) pack_int4_kernel(const __grid_constant__ 
       alo = fmaxf(alo, fabsf(lo[u][i]));
       ahi = fmaxf(ahi, fabsf(hi[u][i]));
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      alo = fmaxf(alo, __shfl_xor_sync(0xffffffffu, alo, o));
-      ahi = fmaxf(ahi, __shfl_xor_sync(0xffffffffu, ahi, o));
-    }
+    alo = warp_max_f32(alo);
+    ahi = warp_max_f32(ahi);
     const float slo = __fmul_rn(fmaxf(alo, 1e-8f), kInv7);
     const float shi = __fmul_rn(fmaxf(ahi, 1e-8f), kInv7);
     uint8_t bytes[E];
@@ -397,7 +394,7 @@ __global__ void __launch_bounds__(128) kv_append_kernel(const __grid_constant__ 
   const float v[4] = {f01.x, f01.y, f23.x, f23.y};
   float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  amax = warp_max_f32(amax);
   const float s = __fmul_rn(fmaxf(amax, 1e-8f), kInv127);
   uint32_t packed = 0;
 #pragma unroll

@@ -27,9 +27,10 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 // Programmatic dependent launch (see LaunchAttrs): let the next kernel on the stream begin
 // launching, and wait until the previous one has completed and its writes are visible.  Every
-// kernel waits before its first global-memory access and triggers its dependents at its start
-// (short kernels) or when its main loop is done (the GEMMs and attention); without the launch
-// attribute both return at once.
+// kernel waits before its first global-memory load (only L2 prefetches, which cannot observe
+// stale data, and tensor-map prefetches come before it) and triggers its dependents at its
+// start (short kernels) or when its main loop is done (the GEMMs and attention); without the
+// launch attribute both return at once.
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
@@ -84,6 +85,14 @@ __device__ int g_specq_trace_cta = 0;
   do {                        \
   } while (0)
 #endif
+
+// Maximum of v over the 32 lanes of the warp in one instruction (sm_100a redux.sync on f32).
+// A maximum is exact, so the result does not depend on the reduction order.
+__device__ __forceinline__ float warp_max_f32(float v) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
+}
 
 // Record the first error code of a launch; later codes do not overwrite it.
 __device__ __forceinline__ void report_status(int* status, int code) {
