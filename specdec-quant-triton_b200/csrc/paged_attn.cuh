@@ -594,6 +594,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             tmem_ld8(s_addr + NQ + c0 + 8, *reinterpret_cast<uint32_t(*)[8]>(rl + 8));
           }
           tmem_wait_ld();
+          if (t == 0 && c0 == 0) SPECQ_TRACE_POINT(28, j);
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             if (h == 1 && !two) break;
@@ -623,12 +624,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       };
 #pragma unroll
       for (int pass = 0; pass < 2; ++pass) {   // two straight-line copies: faster than a loop
-        float xmax = -INFINITY;
-        write_p(xmax);
-        if (pass == 1) break;
-        const bool need = named_barrier_or(2, 256, xmax > kLazyMaxLog2);
-        if (t == 0) SPECQ_TRACE_POINT(22, j);
-        if (!need) break;
+        // Block 0 always rescales (the running max starts at -inf and the split's first token is
+        // visible to its last query row), so its first pass, whose P would be overwritten, is
+        // skipped.
+        if (pass == 1 || j > 0) {
+          float xmax = -INFINITY;
+          write_p(xmax);
+          if (pass == 1) break;
+          const bool need = named_barrier_or(2, 256, xmax > kLazyMaxLog2);
+          if (t == 0) SPECQ_TRACE_POINT(22, j);
+          if (!need) break;
+        }
         // ---- rescale: some score exceeds the running max by more than 2^8 ----
         if (t == 0) SPECQ_TRACE_POINT(26, j);
         // the running O^T / normaliser must be final before they are rescaled
@@ -687,6 +693,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (lane == 0) mbar_arrive(&p_full[sb]);
       if (t == 0) SPECQ_TRACE_POINT(24, j);
       fetch_scale(p.ks, j + 2, krow, pg2, ksd + 256 * slot2, ksel, slot2);
+      if (t == 0) SPECQ_TRACE_POINT(27, j);
       slot = slot == 2 ? 0 : slot + 1;
     }
     cp_async_wait<0>();
