@@ -96,7 +96,6 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_kernel(const __grid_co
     y[k] = v;
     amax = fmaxf(amax, fabsf(v));
   }
-#pragma unroll
   amax = warp_max_f32(amax);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
   __syncthreads();
@@ -181,7 +180,6 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_vec_kernel(const __gri
       for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(y[k][i]));
     }
   }
-#pragma unroll
   amax = warp_max_f32(amax);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
   __syncthreads();
@@ -393,7 +391,6 @@ __global__ void __launch_bounds__(128) kv_append_kernel(const __grid_constant__ 
   const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
   const float v[4] = {f01.x, f01.y, f23.x, f23.y};
   float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-#pragma unroll
   amax = warp_max_f32(amax);
   const float s = __fmul_rn(fmaxf(amax, 1e-8f), kInv127);
   uint32_t packed = 0;
