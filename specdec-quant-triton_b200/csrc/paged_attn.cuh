@@ -552,9 +552,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll 1
     for (int j = 0; j < nblk; ++j) {
       const int slot2 = slot == 0 ? 2 : slot - 1;   // (j + 2) % 3
-      // page of this token in block j + 2: the read is issued here, its scale fetched after
-      // this block's P pass (the shared-memory latency then hides behind the block's work)
-      const int pg2 = scale_page(j + 2, krow);
+      const int pg2 = scale_page(j + 2, krow);   // page of this token in block j + 2
       const int t_abs = t_begin + j * 128 + tl;
       const uint32_t sb = static_cast<uint32_t>(j & 1);
       const uint32_t par2 = static_cast<uint32_t>(j >> 1) & 1u;
@@ -565,6 +563,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       cp_async_wait<1>();   // block j's scale (fetched two blocks ago) has landed
       // this token's score scale: K scale x log2(e) / sqrt(D) x the query scale
       const float a_t = read_scale(ksd + 256 * slot, ksel, slot) * p.sm_scale_log2 * q_scale;
+      // block j + 2's scale into the slot block j - 1 used (issued here, at the top of the
+      // block, it measured faster than after the P pass)
+      fetch_scale(p.ks, j + 2, krow, pg2, ksd + 256 * slot2, ksel, slot2);
       // S(j) is ready; its commit also covers PV(j-2), so P buffer sb is free as well
       ok = ok && mbar_wait(&s_full[sb], par2, status, SPECQ_STATUS_TIMEOUT_MMA);
       tc_fence_after();
@@ -692,7 +693,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[sb]);
       if (t == 0) SPECQ_TRACE_POINT(24, j);
-      fetch_scale(p.ks, j + 2, krow, pg2, ksd + 256 * slot2, ksel, slot2);
       if (t == 0) SPECQ_TRACE_POINT(27, j);
       slot = slot == 2 ? 0 : slot + 1;
     }
