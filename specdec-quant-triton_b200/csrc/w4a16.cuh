@@ -100,6 +100,7 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
                  const __grid_constant__ CUtensorMap tmap_a_chunk) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   SPECQ_TRACE_INIT();
+  if (threadIdx.x == 0) SPECQ_TRACE_POINT(12, 0);
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;                                              // packed weights [stages][128 x 64 B]
   uint8_t* xring = ring + p.stages * kW4A16PackTile;                 // activations [xstages][lo | hi]
@@ -206,6 +207,7 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
       if (p.sc_cache_cols > 0) {   // the CTA's [128 x K/group] fp16 scale tile, once
         mbar_arrive_expect_tx(sc_full, 128u * p.sc_cache_cols * 2u);
         tma_load_2d(sc_cache, &tmap_sc, sc_full, 0, n0, policy_evict_last());
+        SPECQ_TRACE_POINT(16, 0);
       }
       int issued = 0;
       int s = 0;
@@ -250,6 +252,7 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
           }
         }
         ++issued;
+        SPECQ_TRACE_POINT(15, i);
         if (++s == p.xstages) {
           s = 0;
           ph ^= 1u;
@@ -321,12 +324,21 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
     auto group_of = [&](int k) { return p.group_shift >= 0 ? (k >> p.group_shift) : (k / p.group); };
     if (scc > 0) {
       if (!mbar_wait(sc_full, 0u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) *abort_flag = 1;
-      // transpose the scale tile once: [g][row] reads are conflict-free in the loop below
-      for (int e = td; e < scc * 128; e += kW4A16DequantThreads) {
-        const int g = e >> 7, rr = e & 127;
-        sc_t[e] = sc_cache[rr * scc + g];
+      if (td == 0) SPECQ_TRACE_POINT(13, 0);
+      // transpose the scale tile once: [g][row] reads are conflict-free in the loop below.
+      // Item = (8 consecutive groups, row): one 16-byte read of the row's groups, eight 2-byte
+      // writes; the 32 lanes of a warp take 32 consecutive rows, so each write is one
+      // contiguous 64-byte row segment (reading element-wise instead, 64 bytes apart per lane,
+      // cost ~1.3 us of 16-way bank conflicts at config 1).
+      for (int e = td; e < (scc >> 3) * 128; e += kW4A16DequantThreads) {
+        const int g8 = e >> 7, rr = e & 127;
+        const uint4 v = *reinterpret_cast<const uint4*>(sc_cache + rr * scc + 8 * g8);
+        const __half* h = reinterpret_cast<const __half*>(&v);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) sc_t[(8 * g8 + k) * 128 + rr] = h[k];
       }
       named_barrier_sync(1, kW4A16DequantThreads);
+      if (td == 0) SPECQ_TRACE_POINT(14, 0);
     }
     // K-block i = grp + 4 it: weight stage i % stages and its phase by a counter; A slot
     // i % aslots = grp (the host sizes aslots == kW4A16Groups), its phase flips every turn.
