@@ -296,8 +296,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int head = kvh * p.g + (p.g_shift >= 0 ? (row & (p.g - 1)) : (row % p.g));
         const uint4* src = reinterpret_cast<const uint4*>(p.q + b * q_sb + static_cast<int64_t>(qi) * p.q_st +
                                                           static_cast<int64_t>(head) * p.q_sh) + 2 * piece;
-        qraw[k][0] = __ldg(src);
-        qraw[k][1] = __ldg(src + 1);
+        qraw[k][0] = ldg_nc_v4_now(src);
+        qraw[k][1] = ldg_nc_v4_now(src + 1);
       }
     }
   }
@@ -485,8 +485,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (it < NQ * 8 && piece == 0) qamax[row] = amax;
     }
     named_barrier_sync(3, 256);
-    float gmax = 0.f;
-    for (int r = 0; r < NQ; ++r) gmax = fmaxf(gmax, qamax[r]);
+    if (t == 0) SPECQ_TRACE_POINT(11, 0);
+    // the CTA's largest |q|: two rows per lane, one warp reduction (|q| >= 0, so 0 is neutral)
+    const float gmax = warp_max_f32(fmaxf(static_cast<int>(lane) < NQ ? qamax[lane] : 0.f,
+                                          static_cast<int>(lane) + 32 < NQ ? qamax[lane + 32] : 0.f));
     const float q_inv = gmax > 0.f ? 32639.f / gmax : 0.f;
     const float q_scale = gmax / 32639.f;
 #pragma unroll
@@ -533,6 +535,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     named_barrier_sync(3, 256);
     __syncwarp();
     if (lane == 0) mbar_arrive(q_full);
+    if (t == 0) SPECQ_TRACE_POINT(13, 0);
 
     // -max of this thread's query columns, kept in registers (changes only on a rescale)
     float nmr[NQH];

@@ -190,6 +190,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   }
 }
 
+// 16-byte read-only global load issued where it stands: volatile, so the compiler keeps it in
+// program order with the other volatile operations (ahead of a barrier, say) and its latency
+// overlaps what follows instead of being paid where the value is first used.
+__device__ __forceinline__ uint4 ldg_nc_v4_now(const void* ptr) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(ptr));
+  return v;
+}
+
 // 4-byte cp.async global -> shared (4- and 8-byte copies take the L1-allocating .ca form).
 __device__ __forceinline__ void cp_async4(void* smem_dst, const void* gsrc) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
