@@ -1193,7 +1193,7 @@ inline int run_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_
   const void* fn = paged_attn_kernel_by_variant(variant);
   const dim3 grid(static_cast<unsigned>(p.splits), static_cast<unsigned>(H_KV),
                   static_cast<unsigned>(b_grid * p.n_qc));
-  SPECQ_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  SPECQ_CUDA_TRY(ensure_dyn_smem(fn, smem));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kAttnThreads, 1, 1);

@@ -33,7 +33,7 @@ template <int VEC>
 int launch_w8a8_variant(const W8A8Params& p, const CUtensorMap& tw, const CUtensorMap& ta, const CUtensorMap& tac,
                         dim3 grid, int smem, cudaStream_t stream) {
   auto kern = w8a8_kernel<VEC>;
-  SPECQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  SPECQ_CUDA_TRY(ensure_dyn_smem(reinterpret_cast<const void*>(kern), smem));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kW8A8Threads, 1, 1);
@@ -282,7 +282,7 @@ int run_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const
     if (int rc = encode_tiled(&tac, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, d, s_, bc, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
   }
   const dim3 grid(static_cast<unsigned>(S), static_cast<unsigned>(n_tiles), static_cast<unsigned>(n_chunks));
-  SPECQ_CUDA_TRY(cudaFuncSetAttribute(w4a16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  SPECQ_CUDA_TRY(ensure_dyn_smem(reinterpret_cast<const void*>(w4a16_kernel), smem));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kW4A16Threads, 1, 1);

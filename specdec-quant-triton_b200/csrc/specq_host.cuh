@@ -10,6 +10,7 @@
 #include <cstdlib>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <utility>
 #include <string>
@@ -89,6 +90,22 @@ inline int get_device_state(DeviceState** out) {
   }
   *out = &st;
   return SPECQ_OK;
+}
+
+// Raise a kernel's dynamic shared-memory limit once per (kernel, device): the driver call
+// otherwise costs about a microsecond of host time on every launch.
+inline cudaError_t ensure_dyn_smem(const void* kern, int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> granted;
+  std::lock_guard<std::mutex> lock(mu);
+  int& cur = granted[{kern, dev}];
+  if (cur >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) cur = bytes;
+  return e;
 }
 
 // ---- tensor maps ------------------------------------------------------------------------------

@@ -96,10 +96,22 @@ def get_status(clear: bool = True) -> int:
     return v.value
 
 
+_launch_buf = threading.local()
+
+
+def last_launch_raw() -> tuple:
+    """(variant, grid x, y, z, cluster, threads, dynamic smem) of this thread's last launch, read
+    through buffers allocated once per thread (it runs after every operator call)."""
+    b = getattr(_launch_buf, "b", None)
+    if b is None:
+        arr = (C.c_int * 7)()
+        b = _launch_buf.b = (arr, [C.pointer(C.c_int.from_buffer(arr, 4 * i)) for i in range(7)])
+    load().specq_last_launch(*b[1])
+    return tuple(b[0])
+
+
 def last_launch() -> dict:
-    vals = [C.c_int(0) for _ in range(7)]
-    load().specq_last_launch(*[C.byref(v) for v in vals])
-    variant, gx, gy, gz, cx, threads, smem = (v.value for v in vals)
+    variant, gx, gy, gz, cx, threads, smem = last_launch_raw()
     return {"variant": variant, "grid": (gx, gy, gz), "cluster": cx, "threads": threads, "dynamic_smem": smem}
 
 

@@ -29,22 +29,33 @@ W8A8, W4A16, PAGED_ATTN = 0, 1, 2
 
 
 class KernelHandle:
-    """What a launch used: variant, registers, local (spill) bytes, shared memory, grid."""
+    """What a launch used: variant, registers, local (spill) bytes, shared memory, grid.
 
-    def __init__(self, which: int, launch: dict, hints: dict):
-        # variant < 0: the call launched nothing (an empty problem)
-        info = (_kernel_info_cached(which, launch["variant"]) if launch["variant"] >= 0 else
-                {"n_regs": 0, "local_bytes": 0, "static_smem": 0})
-        self.kernel = ("w8a8", "w4a16", "paged_attention")[which]
-        self.variant = launch["variant"]
-        self.n_regs = info["n_regs"]
-        self.n_spills = info["local_bytes"]
-        self.metadata = SimpleNamespace(shared=info["static_smem"] + launch["dynamic_smem"],
-                                        num_warps=launch["threads"] // 32)
-        self.grid = launch["grid"]
-        self.cluster = launch["cluster"]
-        self.num_warps = launch["threads"] // 32
+    Built after every call from the raw launch record; the compiled-kernel attributes are
+    looked up only when read, so the handle costs the caller almost nothing."""
+
+    _NO_INFO = {"n_regs": 0, "local_bytes": 0, "static_smem": 0}
+
+    def __init__(self, which: int, launch: tuple, hints: dict, device: int):
+        self._which, self._launch, self._device = which, launch, device
         self.hints = hints
+
+    def _info(self):
+        # variant < 0: the call launched nothing (an empty problem)
+        v = self._launch[0]
+        return _kernel_info_cached(self._device, self._which, v) if v >= 0 else self._NO_INFO
+
+    kernel = property(lambda self: ("w8a8", "w4a16", "paged_attention")[self._which])
+    variant = property(lambda self: self._launch[0])
+    grid = property(lambda self: tuple(self._launch[1:4]))
+    cluster = property(lambda self: self._launch[4])
+    num_warps = property(lambda self: self._launch[5] // 32)
+    n_regs = property(lambda self: self._info()["n_regs"])
+    n_spills = property(lambda self: self._info()["local_bytes"])
+
+    @property
+    def metadata(self):
+        return SimpleNamespace(shared=self._info()["static_smem"] + self._launch[6], num_warps=self._launch[5] // 32)
 
     def __repr__(self):
         return (f"KernelHandle({self.kernel} v{self.variant}, grid={self.grid}, cluster={self.cluster}, "
@@ -54,10 +65,11 @@ class KernelHandle:
 _info_cache: dict = {}
 
 
-def _kernel_info_cached(which: int, variant: int) -> dict:
-    key = (torch.cuda.current_device(), which, variant)
+def _kernel_info_cached(device: int, which: int, variant: int) -> dict:
+    key = (device, which, variant)
     if key not in _info_cache:
-        _info_cache[key] = _lib.kernel_info(which, variant)
+        with torch.cuda.device(device):
+            _info_cache[key] = _lib.kernel_info(which, variant)
     return _info_cache[key]
 
 
@@ -75,8 +87,7 @@ class CompiledKernelRegistry:
         self.device_caches: dict = {}
         self.cache: dict = {}
 
-    def record(self, variant: int):
-        dev = torch.cuda.current_device()
+    def record(self, variant: int, dev: int):
         entry = self.device_caches.setdefault(dev, ({},))
         entry[0][variant] = True
         self.cache.setdefault(dev, {})[variant] = True
@@ -147,11 +158,12 @@ def w8a8_matmul(a_q, sa, w_q, sw, out=None, BLOCK_M=16, BLOCK_N=64, BLOCK_K=128,
     _lib.check(lib.specq_w8a8(a_q.data_ptr(), a_q.stride(0), sa.data_ptr(), w_q.data_ptr(), w_q.stride(0),
                               sw.data_ptr(), out.data_ptr(), out.stride(0), out.stride(1), _plan_ptr(plan),
                               m_rows, N, K, _stream()))
-    launch = _lib.last_launch()
-    if launch["variant"] >= 0:
-        _w8a8_kernel.record(launch["variant"])
+    launch = _lib.last_launch_raw()
+    dev = a_q.device.index
+    if launch[0] >= 0:
+        _w8a8_kernel.record(launch[0], dev)
     ck = KernelHandle(W8A8, launch, dict(BLOCK_M=BLOCK_M, BLOCK_N=BLOCK_N, BLOCK_K=BLOCK_K, num_warps=num_warps,
-                                         num_stages=num_stages))
+                                         num_stages=num_stages), dev)
     return out, ck
 
 
@@ -199,11 +211,12 @@ def w4a16_matmul(a, wp, sc, group=128, out=None, BLOCK_M=16, BLOCK_N=64, BLOCK_K
     _lib.check(lib.specq_w4a16(a.data_ptr(), a.stride(0), wp.data_ptr(), wp.stride(0), sc.data_ptr(), sc.stride(0),
                                group, out.data_ptr(), out.stride(0), out.stride(1), _plan_ptr(plan), m_rows, N, K,
                                _stream()))
-    launch = _lib.last_launch()
-    if launch["variant"] >= 0:
-        _w4a16_kernel.record(launch["variant"])
+    launch = _lib.last_launch_raw()
+    dev = a.device.index
+    if launch[0] >= 0:
+        _w4a16_kernel.record(launch[0], dev)
     ck = KernelHandle(W4A16, launch, dict(BLOCK_M=BLOCK_M, BLOCK_N=BLOCK_N, BLOCK_K=BLOCK_K, num_warps=num_warps,
-                                          num_stages=num_stages))
+                                          num_stages=num_stages), dev)
     return out, ck
 
 
@@ -248,11 +261,12 @@ def paged_attention(q, kc, vc, ks, vs, block_tbl, ctx_len, q_len, QPP=None, BLOC
         block_tbl.data_ptr(), block_tbl.stride(0), block_tbl.shape[1], ctx_len.data_ptr(),
         out_k.data_ptr(), out_k.stride(0), out_k.stride(1), out_k.stride(2),
         _plan_ptr(plan), B, n_seqs, q_len, QLMAX, H, H_KV, D, PAGE, QPP, _stream()))
-    launch = _lib.last_launch()
-    if launch["variant"] >= 0:
-        _paged_attn_kernel.record(launch["variant"])
+    launch = _lib.last_launch_raw()
+    dev = q.device.index
+    if launch[0] >= 0:
+        _paged_attn_kernel.record(launch[0], dev)
     ck = KernelHandle(PAGED_ATTN, launch, dict(QPP=QPP, BLOCK_N=BLOCK_N, num_warps=num_warps,
-                                               num_stages=num_stages))
+                                               num_stages=num_stages), dev)
     return out, ck
 
 
