@@ -26,6 +26,7 @@ research repo with no package metadata) on this host's cores, rank 0 only.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import math
 import os
@@ -86,6 +87,21 @@ def _traffic_from_profiles():
 # ----------------------------------------------------------------------------------------------
 # distributed plumbing
 # ----------------------------------------------------------------------------------------------
+@contextlib.contextmanager
+def _stdout_to_stderr():
+    """Route what native libraries print on file descriptor 1 (NCCL's version banner when a
+    communicator is created) to stderr, so rank 0's stdout carries only the JSON line."""
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        yield
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
+
+
 def _dist_init(n_gpus):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -97,8 +113,10 @@ def _dist_init(n_gpus):
 
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        with _stdout_to_stderr():
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+            dist.barrier()
     else:
         torch.cuda.set_device(0)
     return rank, world
