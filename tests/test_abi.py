@@ -101,3 +101,17 @@ def test_drop_in_module_exports_reference_names():
                  "quantize_weight_int4", "make_paged_kv", "paged_attention_ref", "_w8a8_kernel", "_w4a16_kernel"):
         assert hasattr(kernels, name), name
     assert kernels._w8a8_kernel.device_caches == {} or isinstance(kernels._w8a8_kernel.device_caches, dict)
+
+
+def test_kernel_handle_reads_the_launch_record():
+    """The `ck` handle each operator returns carries what regs.py reads (n_regs, n_spills,
+    metadata.shared) and the launch geometry; a call that launched nothing (variant -1) needs
+    no kernel lookup."""
+    from specq.ops import KernelHandle, W8A8
+    ck = KernelHandle(W8A8, (-1, 4, 2, 32, 4, 192, 1024), {"BLOCK_M": 16}, 0)
+    assert ck.kernel == "w8a8" and ck.variant == -1
+    assert ck.grid == (4, 2, 32) and ck.cluster == 4 and ck.num_warps == 6
+    assert ck.n_regs == 0 and ck.n_spills == 0
+    assert ck.metadata.shared == 1024 and ck.metadata.num_warps == 6
+    assert ck.hints == {"BLOCK_M": 16}
+    assert "w8a8" in repr(ck)
