@@ -46,7 +46,7 @@ import torch  # noqa: E402
 
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-INT8_DENSE_TOPS_NOMINAL = 4500.0   # datasheet dense INT8 (no measured figure on this pool)
+INT8_DENSE_TOPS_NOMINAL = 4500.0   # datasheet dense INT8, used only when no measured figure exists
 
 # per-GPU workload at N = 1
 W8 = dict(M=40, K=4096, N=4096)
@@ -70,6 +70,25 @@ def _peaks():
         return {k: float(d[k]) for k in ("hbm_gbs", "bf16_tflops", "bf16_tflops_sustained")}, "measured"
     except Exception:
         return dict(FALLBACK_PEAKS), "fallback"
+
+
+def _int8_peak():
+    """Dense INT8 tensor peak in TOPS: the figure `bench.py --mma-peak` measured on this pool
+    (committed in profiles/int8_mma_peak.md as `int8_dense_tops_burst:` / `..._sustained:`), else
+    the datasheet value.  Returns (burst, sustained, source)."""
+    path = os.path.join(REPO, "profiles", "int8_mma_peak.md")
+    vals = {}
+    try:
+        for line in open(path):
+            for key in ("int8_dense_tops_burst", "int8_dense_tops_sustained"):
+                if line.startswith(key + ":"):
+                    vals[key] = float(line.split(":", 1)[1].strip())
+    except Exception:
+        pass
+    if "int8_dense_tops_burst" in vals:
+        return (vals["int8_dense_tops_burst"], vals.get("int8_dense_tops_sustained", vals["int8_dense_tops_burst"]),
+                "measured (bench.py --mma-peak)")
+    return INT8_DENSE_TOPS_NOMINAL, INT8_DENSE_TOPS_NOMINAL, "nominal datasheet"
 
 
 def _traffic_from_profiles():
@@ -404,31 +423,30 @@ def run_ours(args):
     copy_bytes = sum(v.numel() * v.element_size() for v in _make_inputs(sh, 0, dev).values())
     n_copies = max(2, math.ceil(2 * L2_BYTES / copy_bytes))
     inputs = [_make_inputs(sh, 1000 * rank + i, dev) for i in range(n_copies)]
-    graphs = [_capture(list(_kernels(x).values())) for x in inputs]
-    # Steps run as chains of CHAIN consecutive steps (inputs rotating over the copies) captured
-    # in one graph, so the host's graph launches do not pace the device and consecutive
-    # kernels overlap their launch as they would in a serving loop; exactly `steps` steps are
-    # timed (whole chains, then single-step graphs for the remainder).
-    chain_len = n_copies * max(1, 30 // n_copies)
-    chain = _capture([f for i in range(chain_len) for f in _kernels(inputs[i % n_copies]).values()])
-    torch.cuda.synchronize()
+    # The timed region is ONE replay of a graph that holds exactly `steps` consecutive steps
+    # (inputs rotating over the copies): the host's launches do not pace the device and
+    # consecutive kernels overlap their launch (programmatic dependent launch) as in a serving
+    # loop.  The warm-up replays a graph of exactly `warmup` steps; the timed graph is replayed
+    # once before that, untimed, so its upload to the device is not in the timed region.
+    def _steps_graph(n):
+        return _capture([f for i in range(n) for f in _kernels(inputs[i % n_copies]).values()])
 
-    def run_steps(n):
-        for _ in range(n // chain_len):
-            chain.replay()
-        for i in range(n % chain_len):
-            graphs[i % n_copies].replay()
+    warm_steps = max(3, args.warmup)
+    g_warm, g_timed = _steps_graph(warm_steps), _steps_graph(args.steps)
+    chain_len = n_copies * max(1, 30 // n_copies)   # per-kernel chains below
+    torch.cuda.synchronize()
 
     sampler = ClockSampler(dev.index)
     sampler.start()
     time.sleep(0.3)
-    run_steps(max(3, args.warmup))
+    g_timed.replay()      # upload (untimed)
+    g_warm.replay()       # warm-up steps
     torch.cuda.synchronize()
     _barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     e0.record()
-    run_steps(args.steps)
+    g_timed.replay()
     e1.record()
     torch.cuda.synchronize()
     _barrier(world)
@@ -500,7 +518,7 @@ def run_ours(args):
     if world > 1:
         import torch.distributed as dist
         _barrier(world)
-        del graphs
+        del g_warm, g_timed
         dist.destroy_process_group()
     if rank != 0:
         return 0
@@ -515,7 +533,10 @@ def run_ours(args):
         tflops = flops[name] / (us * 1e-6) / 1e12
         entry["tflops_or_tops"] = round(tflops, 1)
         if name == "w8a8":
-            entry["int8_tensor_frac_nominal"] = round(tflops / INT8_DENSE_TOPS_NOMINAL, 4)
+            i8_burst, _, i8_src = _int8_peak()
+            entry["int8_tensor_frac"] = round(tflops / i8_burst, 4)
+            entry["int8_peak_tops"] = i8_burst
+            entry["int8_peak_source"] = i8_src
         else:
             entry["fp16_tensor_frac"] = round(tflops / peaks["bf16_tflops"], 4)
         kern[name] = entry
@@ -537,9 +558,10 @@ def run_ours(args):
         "data": "synthetic (BASELINE config value distributions, seeded, generated on device)",
         "config": _config(world),
         "timing": {"l2": f"{n_copies} rotating input copies of {copy_bytes / 1e6:.1f} MB (> 2x L2)",
-                   "method": f"CUDA events around K steps, replayed as captured chains of {chain_len} steps "
-                             "(kernels launched with programmatic dependent launch); per-kernel: events around "
-                             f"captured chains of {chain_len} launches of that kernel over the copies",
+                   "method": f"CUDA events around one replay of a captured graph of exactly {args.steps} steps "
+                             f"(3 launches each, programmatic dependent launch), after {warm_steps} warm-up steps "
+                             "from a graph of their own; per-kernel: events around replays of captured chains "
+                             f"of {chain_len} launches of that kernel over the copies",
                    "e2e": "steps back to back; each call's chain (H2D of its inputs, the call, D2H of its "
                           "output) on its own stream"},
         "kernels": kern,
@@ -557,6 +579,146 @@ def run_ours(args):
     return 0
 
 
+# ----------------------------------------------------------------------------------------------
+# tensor-pipe peak (tcgen05 microbenchmark) and the GEMM sweep over the verification grid
+# ----------------------------------------------------------------------------------------------
+def run_mma_peak(args):
+    """Dense tensor-pipe throughput of this GPU: kind::i8 (the INT8 peak the W8A8 large-M
+    roofline needs) and kind::f16 (a cross-check against the measured cuBLAS bf16 figure), each
+    as a burst (one launch of ~1 ms, best of 10) and sustained (back to back for ~3 s, clocks
+    sampled).  One CTA per SM issues M=128 x N=256 MMAs from resident shared-memory tiles."""
+    import specq
+    from specq import _lib
+    torch.cuda.set_device(0)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    sink = torch.zeros(sms, dtype=torch.int32, device="cuda")
+    lib = _lib.load()
+    res = {"sms": sms}
+    for kind, name, k_per in ((0, "int8", 32), (1, "fp16", 16)):
+        iters = 4096
+        ops_per_launch = sms * iters * 4 * 2 * 128 * 256 * k_per
+
+        def launch():
+            _lib.check(lib.specq_mma_peak(kind, iters, sms, sink.data_ptr(), torch.cuda.current_stream().cuda_stream))
+
+        for _ in range(3):
+            launch()
+        torch.cuda.synchronize()
+        best = float("inf")
+        for _ in range(10):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            launch()
+            b.record()
+            torch.cuda.synchronize()
+            best = min(best, a.elapsed_time(b))
+        per = best / 1e3
+        n_sus = max(10, int(3.0 / per))
+        sampler = ClockSampler(0)
+        sampler.start()
+        time.sleep(0.3)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(n_sus):
+            launch()
+        b.record()
+        torch.cuda.synchronize()
+        clocks = sampler.stop()
+        sus = a.elapsed_time(b) / 1e3 / n_sus
+        res[name] = {"burst_t": round(ops_per_launch / per / 1e12, 1), "sustained_t": round(ops_per_launch / sus / 1e12, 1),
+                     "launch_ms_best": round(best, 4), "launches_sustained": n_sus, "clocks": clocks,
+                     "unit": "TOPS" if kind == 0 else "TFLOP/s"}
+    res["device_status"] = specq.get_status(clear=True)
+    peaks, src = _peaks()
+    res["cublas_bf16_tflops_measured"] = {"burst": peaks["bf16_tflops"], "sustained": peaks["bf16_tflops_sustained"],
+                                          "source": src}
+    print(json.dumps({"mma_peak": res}), flush=True)
+    return 0
+
+
+LINEAR_SET = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (28672, 4096), "down": (4096, 14336)}
+SWEEP_BS, SWEEP_KS = (1, 2, 4, 8, 16, 32), (0, 2, 4, 8)
+
+
+def _sweep_time(fns, reps, chain=30):
+    """Mean device time of one launch: a captured chain of at least `chain` launches rotating
+    over `fns` (input copies together larger than L2), replayed `reps` times, CUDA events."""
+    for f in fns:
+        f()
+    torch.cuda.synchronize()
+    fns = [fns[i % len(fns)] for i in range(len(fns) * max(1, -(-chain // len(fns))))]
+    g = _capture(fns)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / (reps * len(fns))
+
+
+def run_sweep(args):
+    """The GEMMs over the verification grid M = B*(k+1), B in {1,2,4,8,16,32}, k in {0,2,4,8}:
+    W8A8 on the Llama-3-8B linear set with N sharded g ways (the per-GPU shard is timed, as each
+    rank of `--gpus g` runs it; survey config 3) and W4A16 on gate_proj (config 1).  One JSON
+    line: per point us, algorithmic GB/s and fraction of the measured HBM bandwidth, and the
+    tensor throughput against the INT8 peak (measured when profiles/int8_mma_peak.md has it) or
+    the measured FP16 burst peak."""
+    import specq
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda")
+    peaks, _ = _peaks()
+    i8_peak, _, i8_src = _int8_peak()
+    gen = torch.Generator(device=dev).manual_seed(0)
+    shards = tuple(int(x) for x in args.shards.split(","))
+    reps = args.sweep_reps
+    pts = []
+    for g in shards:
+        for name, (n_full, K) in LINEAR_SET.items():
+            N = n_full // g
+            copies = max(2, math.ceil(2 * L2_BYTES / (N * K)))
+            ws = [torch.randint(-127, 128, (N, K), generator=gen, device=dev, dtype=torch.int16).to(torch.int8)
+                  for _ in range(copies)]
+            sws = [torch.rand(N, generator=gen, device=dev) * 0.019 + 0.001 for _ in range(copies)]
+            for B in SWEEP_BS:
+                for k in SWEEP_KS:
+                    M = B * (k + 1)
+                    a = torch.randint(-127, 128, (M, K), generator=gen, device=dev, dtype=torch.int16).to(torch.int8)
+                    sa = torch.rand(M, generator=gen, device=dev) * 0.019 + 0.001
+                    outs = [torch.empty(M, N, dtype=torch.float16, device=dev) for _ in range(copies)]
+                    us = _sweep_time([lambda i=i: specq.w8a8_matmul(a, sa, ws[i], sws[i], out=outs[i])
+                                      for i in range(copies)], reps)
+                    nbytes = M * K + N * K + 4 * M + 4 * N + 2 * M * N
+                    tops = 2.0 * M * N * K / us / 1e6
+                    pts.append({"kernel": "w8a8", "shape": name, "shards": g, "N": N, "K": K, "B": B, "k": k, "M": M,
+                                "us": round(us, 3), "gbs": round(nbytes / us / 1e3, 1),
+                                "hbm_frac": round(nbytes / us / 1e3 / peaks["hbm_gbs"], 4), "tops": round(tops, 1),
+                                "int8_frac": round(tops / i8_peak, 4)})
+            del ws, sws
+    N, K = 14336, 4096
+    copies = max(2, math.ceil(2 * L2_BYTES / (N * K // 2)))
+    wps = [torch.randint(0, 256, (N, K // 2), generator=gen, device=dev, dtype=torch.int32).to(torch.uint8)
+           for _ in range(copies)]
+    scs = [(torch.rand(N, K // 128, generator=gen, device=dev) * 0.015 + 0.005).half() for _ in range(copies)]
+    for B in SWEEP_BS:
+        for k in SWEEP_KS:
+            M = B * (k + 1)
+            x = torch.randn(M, K, generator=gen, device=dev).half()
+            outs = [torch.empty(M, N, dtype=torch.float16, device=dev) for _ in range(copies)]
+            us = _sweep_time([lambda i=i: specq.w4a16_matmul(x, wps[i], scs[i], out=outs[i]) for i in range(copies)],
+                             reps)
+            nbytes = N * K // 2 + 2 * N * K // 128 + 2 * M * K + 2 * M * N
+            tf = 2.0 * M * N * K / us / 1e6
+            pts.append({"kernel": "w4a16", "N": N, "K": K, "B": B, "k": k, "M": M, "us": round(us, 3),
+                        "gbs": round(nbytes / us / 1e3, 1), "hbm_frac": round(nbytes / us / 1e3 / peaks["hbm_gbs"], 4),
+                        "tflops": round(tf, 1), "fp16_frac": round(tf / peaks["bf16_tflops"], 4)})
+    print(json.dumps({"sweep": pts, "hbm_gbs": peaks["hbm_gbs"], "int8_peak_tops": i8_peak, "int8_peak_source": i8_src,
+                      "fp16_peak_tflops": peaks["bf16_tflops"], "status": specq.get_status(clear=True)}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -567,7 +729,17 @@ def main():
     ap.add_argument("--per-kernel-reps", type=int, default=0,
                     help="replays per kernel for the per-kernel durations (0: ~0.7 s each); small values "
                          "keep the launch count low for a profiler's launch list")
+    ap.add_argument("--sweep", action="store_true",
+                    help="time the GEMMs over the B x k verification grid (1 GPU) instead of the step")
+    ap.add_argument("--shards", default="1,2,4,8", help="--sweep: N-shard counts of the W8A8 linear set")
+    ap.add_argument("--sweep-reps", type=int, default=20)
+    ap.add_argument("--mma-peak", action="store_true",
+                    help="measure the dense tcgen05 INT8 / FP16 tensor-pipe peak (1 GPU) instead of the step")
     args = ap.parse_args()
+    if args.mma_peak:
+        return run_mma_peak(args)
+    if args.sweep:
+        return run_sweep(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

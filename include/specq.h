@@ -181,6 +181,16 @@ int specq_get_status(int* status, int clear);
 int specq_selftest_wait_timeout(uint64_t limit_ns, void* stream);
 
 /*
+ * Tensor-pipe throughput microbenchmark.  No reference counterpart: it measures the dense peak
+ * that the GEMMs' large-M roofline is scored against (the pool measures only HBM copy bandwidth
+ * and a cuBLAS bf16 GEMM).  Launches `ctas` CTAs (one per SM: pass the SM count), each issuing
+ * `iters` x 4 back-to-back tcgen05 MMAs of M=128, N=256 from shared-memory tiles into tensor
+ * memory: kind 0 = kind::i8 (K=32, 2*128*256*32 ops each), kind 1 = kind::f16 (K=16).  `sink`
+ * (device uint32 [ctas]) receives one checksum word per CTA.  Time it with events on `stream`.
+ */
+int specq_mma_peak(int kind, int iters, int ctas, uint32_t* sink, void* stream);
+
+/*
  * Pipeline tracing (builds compiled with -DSPECQ_TRACE only; other builds return
  * SPECQ_ERR_UNSUPPORTED): the CTA with linear index `cta` records SM-clock timestamps of its
  * pipeline events into `buffer` (device, 64 x 64 uint64: [event slot][iteration]).

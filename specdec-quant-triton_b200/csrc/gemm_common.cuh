@@ -1,9 +1,8 @@
-// gemm_common.cuh -- pieces shared by the W8A8 and W4A16 kernels:
-//   * the launch-geometry record both GEMMs fill on the host,
-//   * a register-staged global->shared tile loader that writes the 128-byte-swizzled
-//     K-major layout the tensor core reads (used when a row stride or base address is not
-//     16-byte aligned, so TMA cannot be used),
-//   * the split-K reduction over a thread-block cluster through distributed shared memory.
+// gemm_common.cuh -- the register-staged global->shared tile loader of the GEMMs: it writes
+// the 128-byte-swizzled K-major layout the tensor core reads, for operands whose row stride or
+// base address is not 16-byte aligned (so TMA cannot be used).  The split-K reductions live in
+// the kernels themselves (w8a8.cuh: bulk asynchronous DSMEM adds; w4a16.cuh: fixed-order DSMEM
+// loads).
 #pragma once
 
 #include "sm100.cuh"

@@ -142,19 +142,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Non-blocking test of phase `parity` (for loops that poll several barriers).
-__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
 // try_wait with a suspend-time hint: the thread sleeps (instead of spinning and taking issue
 // slots from the working warps) until the phase completes or ~0.5 ms pass.
 __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {

@@ -10,6 +10,7 @@
 #include "w4a16.cuh"
 #include "paged_attn.cuh"
 #include "rowops.cuh"
+#include "mma_peak.cuh"
 
 namespace specq {
 
@@ -67,7 +68,11 @@ int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int
   if (lda < K || ldw < K) return fail(SPECQ_ERR_INVALID_ARG, "w8a8: row strides (%lld, %lld) < K=%d",
                                       (long long)lda, (long long)ldw, K);
   if (K > (1 << 30) / 127) return fail(SPECQ_ERR_UNSUPPORTED, "w8a8: K=%d could overflow the INT32 accumulator", K);
-  if (M == 0) return SPECQ_OK;
+  if (acc != nullptr && ldacc < N)
+    return fail(SPECQ_ERR_INVALID_ARG, "w8a8: accumulator row stride %lld < N=%d", (long long)ldacc, N);
+  if (acc == nullptr && (ldo < 1 || ldo_n < 1))
+    return fail(SPECQ_ERR_INVALID_ARG, "w8a8: output strides (%lld, %lld) must be positive", (long long)ldo,
+                (long long)ldo_n);
   DeviceState* dev = nullptr;
   if (int rc = get_device_state(&dev)) return rc;
 
@@ -186,6 +191,9 @@ int run_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const
     return fail(SPECQ_ERR_UNSUPPORTED, "w4a16: needs (K/2) %% 64 == 0 and group %% 64 == 0 (K=%d, group=%d)", K, group);
   if (lda < K || ldwp < K / 2 || ldsc < (K + group - 1) / group)
     return fail(SPECQ_ERR_INVALID_ARG, "w4a16: row strides too small");
+  if (ldo < 1 || ldo_n < 1)
+    return fail(SPECQ_ERR_INVALID_ARG, "w4a16: output strides (%lld, %lld) must be positive", (long long)ldo,
+                (long long)ldo_n);
   if (!aligned(a, 16) || (lda * 2) % 16 != 0 || !aligned(wp, 16) || ldwp % 16 != 0)
     return fail(SPECQ_ERR_UNSUPPORTED, "w4a16: activations/packed weights need 16-byte aligned rows");
   if (M == 0) return SPECQ_OK;
@@ -214,8 +222,10 @@ int run_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const
   p.splits = S;
   p.kb_per_split = ceil_div(p.kb_total, S);
   // Scale tile by TMA when its rows allow it (16-byte aligned, <= 32 KB); otherwise each
-  // K-block's two scales per row are prefetched into registers one block ahead.
-  const int G = K / group;
+  // K-block's two scales per row are prefetched into registers one block ahead.  A row holds
+  // ceil(K / group) groups: with K % group != 0 the last group is partial, and the high-half
+  // K-blocks near the end read it (column (k + K/2) / group, as kernels.py:119-120 does).
+  const int G = (K + group - 1) / group;
   const bool sc_tma = (G % 8 == 0) && G <= 128 && aligned(sc, 16) && (ldsc * 2) % 16 == 0;
   p.sc_cache_cols = sc_tma ? static_cast<uint32_t>(G) : 0u;
   const int sc_bytes = sc_tma ? 128 * G * 2 : 0;
@@ -445,6 +455,26 @@ int specq_trace_configure(void* buffer, int cta) {
   (void)cta;
   return fail(SPECQ_ERR_UNSUPPORTED, "trace points are compiled in only with -DSPECQ_TRACE");
 #endif
+}
+
+int specq_mma_peak(int kind, int iters, int ctas, uint32_t* sink, void* stream) {
+  last_launch_ref() = LaunchRecord();
+  if (kind != 0 && kind != 1) return fail(SPECQ_ERR_INVALID_ARG, "mma_peak: kind %d (0 = i8, 1 = f16)", kind);
+  if (iters < 2 || ctas < 1 || sink == nullptr)
+    return fail(SPECQ_ERR_INVALID_ARG, "mma_peak: iters=%d ctas=%d sink=%p", iters, ctas, (void*)sink);
+  DeviceState* dev = nullptr;
+  if (int rc = get_device_state(&dev)) return rc;
+  auto kern = kind == 0 ? mma_peak_kernel<0> : mma_peak_kernel<1>;
+  SPECQ_CUDA_TRY(ensure_dyn_smem(reinterpret_cast<const void*>(kern), kPeakSmem));
+  kern<<<ctas, kPeakThreads, kPeakSmem, static_cast<cudaStream_t>(stream)>>>(iters, dev->status, sink);
+  SPECQ_CUDA_TRY(cudaGetLastError());
+  LaunchRecord& r = last_launch_ref();
+  r.variant = kind;
+  r.grid[0] = ctas; r.grid[1] = 1; r.grid[2] = 1;
+  r.cluster_x = 1;
+  r.threads = kPeakThreads;
+  r.dyn_smem = kPeakSmem;
+  return SPECQ_OK;
 }
 
 int specq_selftest_wait_timeout(uint64_t limit_ns, void* stream) {

@@ -125,6 +125,19 @@ def _plan_ptr(plan):
     return plan.data_ptr()
 
 
+def _check_out(name: str, out, dtype, n_cols: int, n_rows: int):
+    """A caller-supplied output must have the kernel's dtype, at least n_cols columns (and, without
+    a plan, n_rows rows) and positive strides: the kernel writes through the pointer and strides,
+    so a smaller buffer would be written past its end."""
+    if out.dtype != dtype:
+        raise TypeError(f"{name}: out must be {dtype}, got {out.dtype}")
+    if out.dim() != 2 or out.shape[1] < n_cols or out.shape[0] < n_rows:
+        raise ValueError(f"{name}: out must be 2-D with >= {n_rows} rows and >= {n_cols} columns, "
+                         f"got {tuple(out.shape)}")
+    if out.stride(0) < 1 or out.stride(1) < 1:
+        raise ValueError(f"{name}: out strides {tuple(out.stride())} must be positive")
+
+
 def _row_extent(n_rows: int, plan, grid_m_max, *tensors_rows) -> int:
     """Rows the kernel may touch: the tensor extent, or the plan grid's maximum."""
     if plan is None:
@@ -146,8 +159,9 @@ def w8a8_matmul(a_q, sa, w_q, sw, out=None, BLOCK_M=16, BLOCK_N=64, BLOCK_K=128,
         raise TypeError("w8a8_matmul: a_q and w_q must be int8")
     if out is None:
         out = torch.empty((M, N), device=a_q.device, dtype=torch.float16)
-    if out.dtype != torch.float16:
-        raise TypeError("w8a8_matmul: out must be float16")
+    _check_out("w8a8_matmul", out, torch.float16, N, M if plan is None else 0)
+    if sa.numel() < M or sw.numel() < N:
+        raise ValueError(f"w8a8_matmul: scales have {sa.numel()} / {sw.numel()} entries for M={M}, N={N}")
     _require_cuda(a_q, sa, w_q, sw, out)
     a_q, w_q = _unit_inner(a_q), _unit_inner(w_q)
     sa = sa if sa.dtype == torch.float32 else sa.float()
@@ -172,9 +186,16 @@ def w8a8_accumulator(a_q, w_q, plan=None, grid_m_max=None, out=None):
     kernel (the `acc` of kernels.py:44-50, before the scale epilogue)."""
     M, K = a_q.shape
     N = w_q.shape[0]
-    _require_cuda(a_q, w_q)
+    if w_q.shape[1] != K:
+        raise ValueError(f"w8a8_accumulator: a_q is [M, {K}] but w_q is {tuple(w_q.shape)}")
+    if a_q.dtype != torch.int8 or w_q.dtype != torch.int8:
+        raise TypeError("w8a8_accumulator: a_q and w_q must be int8")
     if out is None:
         out = torch.empty((M, N), device=a_q.device, dtype=torch.int32)
+    _check_out("w8a8_accumulator", out, torch.int32, N, M if plan is None else 0)
+    if out.stride(1) != 1:
+        raise ValueError("w8a8_accumulator: out must have unit column stride")
+    _require_cuda(a_q, w_q, out)
     a_q, w_q = _unit_inner(a_q), _unit_inner(w_q)
     m_rows = _row_extent(M, plan, grid_m_max, M, out.shape[0])
     lib = _lib.load()
@@ -199,8 +220,10 @@ def w4a16_matmul(a, wp, sc, group=128, out=None, BLOCK_M=16, BLOCK_N=64, BLOCK_K
         raise TypeError("w4a16_matmul: wp must be uint8")
     if out is None:
         out = torch.empty((M, N), device=a.device, dtype=torch.float16)
-    if out.dtype != torch.float16:
-        raise TypeError("w4a16_matmul: out must be float16")
+    _check_out("w4a16_matmul", out, torch.float16, N, M if plan is None else 0)
+    n_groups = -(-K // group)
+    if sc.dim() != 2 or sc.shape[0] < N or sc.shape[1] < n_groups:
+        raise ValueError(f"w4a16_matmul: sc is {tuple(sc.shape)}, needs [>= {N}, >= {n_groups}] (ceil(K/group))")
     _require_cuda(a, wp, sc, out)
     sc = sc if sc.dtype == torch.float16 else sc.half()
     a, wp, sc = _unit_inner(a), _unit_inner(wp), _unit_inner(sc)

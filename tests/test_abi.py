@@ -115,3 +115,37 @@ def test_kernel_handle_reads_the_launch_record():
     assert ck.metadata.shared == 1024 and ck.metadata.num_warps == 6
     assert ck.hints == {"BLOCK_M": 16}
     assert "w8a8" in repr(ck)
+
+
+def test_output_buffers_checked_before_launch():
+    """A caller-supplied `out` that the kernel would write past the end of is rejected on the
+    host: wrong dtype, too few columns or rows, non-positive strides (the C ABI rejects
+    non-positive output strides and an accumulator row stride below N as well)."""
+    import specq
+    from specq import _lib
+    a = torch.zeros(4, 128, dtype=torch.int8)
+    w = torch.zeros(8, 128, dtype=torch.int8)
+    s4, s8 = torch.ones(4), torch.ones(8)
+    with pytest.raises(ValueError, match="columns"):
+        specq.w8a8_matmul(a, s4, w, s8, out=torch.empty(4, 7, dtype=torch.float16))
+    with pytest.raises(ValueError, match="rows"):
+        specq.w8a8_matmul(a, s4, w, s8, out=torch.empty(3, 8, dtype=torch.float16))
+    with pytest.raises(TypeError):
+        specq.w8a8_accumulator(a, w, out=torch.empty(4, 8, dtype=torch.float32))
+    with pytest.raises(ValueError, match="columns"):
+        specq.w8a8_accumulator(a, w, out=torch.empty(4, 6, dtype=torch.int32))
+    with pytest.raises(ValueError, match="entries"):
+        specq.w8a8_matmul(a, torch.ones(3), w, s8)
+    x = torch.zeros(2, 256, dtype=torch.float16)
+    wp = torch.zeros(8, 128, dtype=torch.uint8)
+    with pytest.raises(ValueError, match="columns"):
+        specq.w4a16_matmul(x, wp, torch.ones(8, 2, dtype=torch.float16), out=torch.empty(2, 4, dtype=torch.float16))
+    with pytest.raises(ValueError, match="ceil"):          # 256 / 96 -> 3 scale columns needed
+        specq.w4a16_matmul(x, wp, torch.ones(8, 2, dtype=torch.float16), group=96, BLOCK_K=32)
+    lib = _lib.load()
+    rc = lib.specq_w8a8_acc(16, 128, 16, 128, 16, 7, None, 4, 8, 128, None)           # ldacc < N
+    assert rc == _lib.SPECQ_ERR_INVALID_ARG
+    rc = lib.specq_w8a8(16, 128, 16, 16, 128, 16, 16, 0, 1, None, 4, 8, 128, None)    # ldo = 0
+    assert rc == _lib.SPECQ_ERR_INVALID_ARG
+    rc = lib.specq_w4a16(16, 256, 16, 128, 16, 2, 128, 16, 8, -1, None, 2, 8, 256, None)  # ldo_n < 0
+    assert rc == _lib.SPECQ_ERR_INVALID_ARG

@@ -135,3 +135,28 @@ def test_cuda_graph_plan_replay(cuda):
         ref, _ = specq.w4a16_matmul(x[:M], wpd, scd)
         torch.cuda.synchronize()
         assert torch.equal(out[:M], ref) and bool((out[M:] == 0).all())
+
+
+@pytest.mark.parametrize("K,group", [(1408, 192), (1664, 192), (2176, 256), (1536, 192)])
+def test_partial_last_group(cuda, K, group):
+    """K % group != 0: each row has ceil(K/group) scale columns, the last one covering a partial
+    group that the high-half K-blocks near the end read (column (k + K/2) // group, as
+    kernels.py:119-120 indexes it).  (1408, 192) takes the TMA scale tile (8 columns),
+    (1664, 192) and (2176, 256) the per-block scale loads (9 columns); (1536, 192) divides
+    evenly and is the control."""
+    import specq
+    N, M = 200, 24
+    G = -(-K // group)
+    g = torch.Generator().manual_seed(K + group)
+    nib = torch.randint(0, 16, (N, K), generator=g, dtype=torch.int16)
+    wp = (nib[:, : K // 2] | (nib[:, K // 2:] << 4)).to(torch.uint8)
+    sc = (torch.rand(N, G, generator=g) * 0.015 + 0.005).half()
+    x = torch.randn(M, K, generator=g).half()
+    out, _ = specq.w4a16_matmul(x.cuda(), wp.cuda(), sc.cuda(), group=group)
+    torch.cuda.synchronize()
+    ref = O.w4a16_ref(x.numpy(), wp.numpy(), sc.numpy(), group)
+    assert O.rel_fro_err(out.cpu().numpy(), ref) < 1e-3
+    # a scale tile that read the wrong column of the last group would be off by far more
+    sc_bad = sc.clone()
+    sc_bad[:, G - 1] *= 2
+    assert O.rel_fro_err(O.w4a16_ref(x.numpy(), wp.numpy(), sc_bad.numpy(), group), ref) > 1e-2
