@@ -599,7 +599,8 @@ def run_mma_peak(args):
         ops_per_launch = sms * iters * 4 * 2 * 128 * 256 * k_per
 
         def launch():
-            _lib.check(lib.specq_mma_peak(kind, iters, sms, sink.data_ptr(), torch.cuda.current_stream().cuda_stream))
+            _lib.check(lib.specq_mma_peak(kind, 256, 0, 0, 0, 0, 0, iters, sms, sink.data_ptr(),
+                                          torch.cuda.current_stream().cuda_stream))
 
         for _ in range(3):
             launch()

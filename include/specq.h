@@ -183,12 +183,17 @@ int specq_selftest_wait_timeout(uint64_t limit_ns, void* stream);
 /*
  * Tensor-pipe throughput microbenchmark.  No reference counterpart: it measures the dense peak
  * that the GEMMs' large-M roofline is scored against (the pool measures only HBM copy bandwidth
- * and a cuBLAS bf16 GEMM).  Launches `ctas` CTAs (one per SM: pass the SM count), each issuing
- * `iters` x 4 back-to-back tcgen05 MMAs of M=128, N=256 from shared-memory tiles into tensor
- * memory: kind 0 = kind::i8 (K=32, 2*128*256*32 ops each), kind 1 = kind::f16 (K=16).  `sink`
- * (device uint32 [ctas]) receives one checksum word per CTA.  Time it with events on `stream`.
+ * and a cuBLAS bf16 GEMM), and prices the small MMAs the attention and GEMM kernels issue.
+ * Launches `ctas` CTAs (one per SM: pass the SM count), each issuing `iters` x 4 back-to-back
+ * tcgen05 MMAs of M=128 and N=`n` (16..256, multiple of 16) from shared-memory tiles into
+ * tensor memory: kind 0 = kind::i8 (K=32, 2*128*n*32 ops each), kind 1 = kind::f16 (K=16).
+ * a_mn_major / b_mn_major select MN-major operand layouts; a_tmem = 1 (kind 1, n <= 128) reads
+ * A from tensor memory; `busy_warps` (0..28) extra warps each run `busy_iters` 16-byte
+ * shared-memory loads and stores per thread meanwhile.  `sink` (device uint32 [ctas])
+ * receives one checksum word per CTA.  Time it with events on `stream`.
  */
-int specq_mma_peak(int kind, int iters, int ctas, uint32_t* sink, void* stream);
+int specq_mma_peak(int kind, int n, int a_mn_major, int b_mn_major, int a_tmem, int busy_warps, int busy_iters,
+                   int iters, int ctas, uint32_t* sink, void* stream);
 
 /*
  * Pipeline tracing (builds compiled with -DSPECQ_TRACE only; other builds return

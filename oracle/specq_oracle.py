@@ -172,6 +172,55 @@ def paged_attention_ref(q, kc, vc, ks, vs, block_tbl, ctx_len, q_len) -> np.ndar
 
 
 # ----------------------------------------------------------------------------------
+# Verification-layer glue (the plan-graph stack of bench_graphs.py:49-64, extended with a
+# connected data flow): KV-cache append, SiLU-mul quantisation, fp16 residual add
+# ----------------------------------------------------------------------------------
+
+
+def kv_quant_rows(x: np.ndarray, on_cuda: bool = True):
+    """INT8 of K or V rows [T, H_KV, D] with one scale per (token, head), the cache format of
+    make_paged_kv's q8 (kernels.py:276-283): s = max(amax, 1e-8) / 127 (fp32; stored fp16),
+    q = clamp(rint(x / s), -127, 127) with the fp32 s.  on_cuda: `/ 127.0` as torch evaluates
+    it on a GPU tensor (the device append runs there)."""
+    xf = x.astype(np.float32)
+    s = _div_scalar(np.maximum(np.abs(xf).max(axis=-1), np.float32(1e-8)), 127.0, on_cuda)
+    q = np.clip(np.rint(xf / s[..., None]), -127, 127).astype(np.int8)
+    return q, s.astype(np.float16)
+
+
+def kv_append(x_rows, k_col, v_col, kc, vc, ks, vs, block_tbl, ctx_len, q_len, n_seqs, h_kv, d, page):
+    """Write the K / V of the q_len newest tokens of each sequence into copies of the caches.
+    x_rows: packed token rows (sequence b's token t at row b*q_len + t), K of head h at columns
+    k_col + h*d, V at v_col + h*d; token t goes to position ctx_len[b] - q_len + t."""
+    kc, vc, ks, vs = kc.copy(), vc.copy(), ks.copy(), vs.copy()
+    for b in range(n_seqs):
+        for t in range(q_len):
+            pos = int(ctx_len[b]) - q_len + t
+            pg, slot = int(block_tbl[b, pos // page]), pos % page
+            row = x_rows[b * q_len + t]
+            for col, c, sc in ((k_col, kc, ks), (v_col, vc, vs)):
+                q, s = kv_quant_rows(row[col:col + h_kv * d].reshape(1, h_kv, d))
+                c[pg, slot] = q[0]
+                sc[pg, slot] = s[0]
+    return kc, vc, ks, vs
+
+
+def silu_mul(gu: np.ndarray) -> np.ndarray:
+    """silu(gate) * up in fp32 for fp16 rows [M, 2N] (gate = first half): the MLP activation of
+    the stack's gate_up projection, torch.nn.functional.silu(g.float()) * u.float()."""
+    n = gu.shape[1] // 2
+    g = gu[:, :n].astype(np.float32)
+    u = gu[:, n:].astype(np.float32)
+    return (g / (np.float32(1.0) + np.exp(-g))).astype(np.float32) * u
+
+
+def residual_add(x: np.ndarray, r: np.ndarray) -> np.ndarray:
+    """fp16(x + r) of two fp16 tensors (one rounding: the fp32 sum of two fp16 values rounds to
+    the same fp16 value as the exact sum, 24 >= 2 * 11 + 2 bits)."""
+    return (x.astype(np.float32) + r.astype(np.float32)).astype(np.float16)
+
+
+# ----------------------------------------------------------------------------------
 # Error metrics used by the reference's correctness script
 # ----------------------------------------------------------------------------------
 

@@ -31,8 +31,8 @@ namespace {
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in per block on sm_100
 
 template <int VEC>
-int launch_w8a8_variant(const W8A8Params& p, const CUtensorMap& tw, const CUtensorMap& ta, const CUtensorMap& tac,
-                        dim3 grid, int smem, cudaStream_t stream) {
+int launch_w8a8_variant(const W8A8Params& p, const CUtensorMap& tw, const W8A8ActMaps& ta, dim3 grid, int smem,
+                        cudaStream_t stream) {
   auto kern = w8a8_kernel<VEC>;
   SPECQ_CUDA_TRY(ensure_dyn_smem(reinterpret_cast<const void*>(kern), smem));
   cudaLaunchConfig_t cfg = {};
@@ -42,7 +42,7 @@ int launch_w8a8_variant(const W8A8Params& p, const CUtensorMap& tw, const CUtens
   cfg.stream = stream;
   LaunchAttrs attrs(p.splits);
   attrs.apply(cfg);
-  SPECQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p, tw, ta, tac));
+  SPECQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p, tw, ta));
   return SPECQ_OK;
 }
 
@@ -85,8 +85,12 @@ int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int
   p.lda = lda; p.ldw = ldw; p.ldo = ldo; p.ldo_n = ldo_n; p.ldacc = ldacc;
   p.m_rows = M; p.N = N; p.K = K;
 
-  const int n_chunks = ceil_div(M, 256);
+  // One token chunk per CTA up to kW8A8MaxChunk tokens (past 256 rows: a multiple of 32, so a
+  // whole chunk arrives in two TMA boxes of chunk / 2 rows).
+  const int n_chunks = ceil_div(M, kW8A8MaxChunk);
   p.chunk = round_up(ceil_div(M, n_chunks), 16);
+  if (p.chunk > 256) p.chunk = round_up(p.chunk, 32);
+  p.chunk_box = p.chunk > 256 ? p.chunk / 2 : p.chunk;
   p.kb_total = ceil_div(K, 128);
   const int n_tiles = ceil_div(N, 128);
   const int base = n_tiles * n_chunks;
@@ -106,7 +110,7 @@ int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int
   p.stage_bytes = kW8A8WTile + static_cast<uint32_t>(round_up(p.chunk, 16)) * 128u;
   // split-K partial tile [128][chunk] int32 (padded rows), parked in the idle ring
   const uint32_t red_bytes = (S > 1) ? 128u * (static_cast<uint32_t>(round_up(p.chunk, 16)) * 4u + 16u) : 0u;
-  const int overhead = 1024 + 256 + 384 * 4;   // alignment slack, barriers, staged scales
+  const int overhead = 1024 + 256 + (kW8A8MaxChunk + 128) * 4;   // alignment slack, barriers, staged scales
   int stages = std::min(8, (kSmemLimit - overhead) / static_cast<int>(p.stage_bytes));
   if (stages < 2) return fail(SPECQ_ERR_UNSUPPORTED, "w8a8: token chunk %d does not fit shared memory", p.chunk);
   while (static_cast<uint32_t>(stages) * p.stage_bytes < red_bytes && stages < 8) ++stages;
@@ -118,10 +122,10 @@ int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int
 
   // TMA needs 16-byte aligned bases and row strides; otherwise use the register-staged loader.
   const bool tma_ok = aligned(a, 16) && aligned(w, 16) && (lda % 16 == 0) && (ldw % 16 == 0);
-  CUtensorMap tw, ta, tac;
+  CUtensorMap tw;
+  W8A8ActMaps ta;
   memset(&tw, 0, sizeof(tw));
   memset(&ta, 0, sizeof(ta));
-  memset(&tac, 0, sizeof(tac));
   int vec = 0;
   if (tma_ok) {
     const uint64_t dw[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
@@ -130,10 +134,14 @@ int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int
     if (int rc = encode_tiled(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, dw, sw_, bw, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
     const uint64_t da[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
     const uint64_t sa_[1] = {static_cast<uint64_t>(lda)};
-    const uint32_t ba[2] = {128, 16};
-    if (int rc = encode_tiled(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a, da, sa_, ba, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
-    const uint32_t bac[2] = {128, static_cast<uint32_t>(p.chunk)};   // a whole token chunk
-    if (int rc = encode_tiled(&tac, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a, da, sa_, bac, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+    for (int b = 0; b < 4; ++b) {
+      const uint32_t ba[2] = {128, 16u << b};
+      if (int rc = encode_tiled(&ta.rows[b], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a, da, sa_, ba, CU_TENSOR_MAP_SWIZZLE_128B))
+        return rc;
+    }
+    const uint32_t bac[2] = {128, static_cast<uint32_t>(p.chunk_box)};   // a whole token chunk (or half of it)
+    if (int rc = encode_tiled(&ta.chunk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a, da, sa_, bac, CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
   } else {
     vec = common_vec_width({reinterpret_cast<uintptr_t>(a), reinterpret_cast<uintptr_t>(w),
                             static_cast<uint64_t>(lda), static_cast<uint64_t>(ldw), static_cast<uint64_t>(K)});
@@ -145,12 +153,12 @@ int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc;
   switch (vec) {
-    case 0: rc = launch_w8a8_variant<0>(p, tw, ta, tac, grid, smem, st); break;
-    case 16: rc = launch_w8a8_variant<16>(p, tw, ta, tac, grid, smem, st); break;
-    case 8: rc = launch_w8a8_variant<8>(p, tw, ta, tac, grid, smem, st); break;
-    case 4: rc = launch_w8a8_variant<4>(p, tw, ta, tac, grid, smem, st); break;
-    case 2: rc = launch_w8a8_variant<2>(p, tw, ta, tac, grid, smem, st); break;
-    default: rc = launch_w8a8_variant<1>(p, tw, ta, tac, grid, smem, st); break;
+    case 0: rc = launch_w8a8_variant<0>(p, tw, ta, grid, smem, st); break;
+    case 16: rc = launch_w8a8_variant<16>(p, tw, ta, grid, smem, st); break;
+    case 8: rc = launch_w8a8_variant<8>(p, tw, ta, grid, smem, st); break;
+    case 4: rc = launch_w8a8_variant<4>(p, tw, ta, grid, smem, st); break;
+    case 2: rc = launch_w8a8_variant<2>(p, tw, ta, grid, smem, st); break;
+    default: rc = launch_w8a8_variant<1>(p, tw, ta, grid, smem, st); break;
   }
   if (rc == SPECQ_OK) {
     LaunchRecord& r = last_launch_ref();
@@ -457,22 +465,37 @@ int specq_trace_configure(void* buffer, int cta) {
 #endif
 }
 
-int specq_mma_peak(int kind, int iters, int ctas, uint32_t* sink, void* stream) {
+int specq_mma_peak(int kind, int n, int a_mn_major, int b_mn_major, int a_tmem, int busy_warps, int busy_iters,
+                   int iters, int ctas, uint32_t* sink, void* stream) {
   last_launch_ref() = LaunchRecord();
   if (kind != 0 && kind != 1) return fail(SPECQ_ERR_INVALID_ARG, "mma_peak: kind %d (0 = i8, 1 = f16)", kind);
-  if (iters < 2 || ctas < 1 || sink == nullptr)
-    return fail(SPECQ_ERR_INVALID_ARG, "mma_peak: iters=%d ctas=%d sink=%p", iters, ctas, (void*)sink);
+  if (n < 16 || n > 256 || n % 16 != 0) return fail(SPECQ_ERR_INVALID_ARG, "mma_peak: N=%d", n);
+  if (a_tmem && (kind != 1 || n > 128 || a_mn_major))
+    return fail(SPECQ_ERR_INVALID_ARG, "mma_peak: A from tensor memory needs kind f16, K-major, N <= 128");
+  if (iters < 2 || ctas < 1 || sink == nullptr || busy_warps < 0 || busy_warps > 28 || busy_iters < 0)
+    return fail(SPECQ_ERR_INVALID_ARG, "mma_peak: iters=%d ctas=%d busy_warps=%d", iters, ctas, busy_warps);
   DeviceState* dev = nullptr;
   if (int rc = get_device_state(&dev)) return rc;
+  MmaPeakParams mp = {};
+  mp.iters = iters;
+  mp.n = static_cast<uint32_t>(n);
+  mp.a_mn = a_mn_major ? 1u : 0u;
+  mp.b_mn = b_mn_major ? 1u : 0u;
+  mp.a_tmem = a_tmem;
+  mp.busy_warps = busy_warps;
+  mp.busy_iters = busy_iters;
+  mp.status = dev->status;
+  mp.sink = sink;
   auto kern = kind == 0 ? mma_peak_kernel<0> : mma_peak_kernel<1>;
   SPECQ_CUDA_TRY(ensure_dyn_smem(reinterpret_cast<const void*>(kern), kPeakSmem));
-  kern<<<ctas, kPeakThreads, kPeakSmem, static_cast<cudaStream_t>(stream)>>>(iters, dev->status, sink);
+  const int threads = kPeakThreads + 32 * busy_warps;
+  kern<<<ctas, threads, kPeakSmem, static_cast<cudaStream_t>(stream)>>>(mp);
   SPECQ_CUDA_TRY(cudaGetLastError());
   LaunchRecord& r = last_launch_ref();
   r.variant = kind;
   r.grid[0] = ctas; r.grid[1] = 1; r.grid[2] = 1;
   r.cluster_x = 1;
-  r.threads = kPeakThreads;
+  r.threads = threads;
   r.dyn_smem = kPeakSmem;
   return SPECQ_OK;
 }

@@ -6,9 +6,12 @@
 // Design (B200-first, not the reference's tiling):
 //   * Swap-AB.  The tensor-core M=128 axis runs over 128 weight channels (A operand = the
 //     weight tile); the N axis runs over the CTA's tokens (B operand = activations).  One CTA
-//     holds the INT32 accumulators of up to 256 tokens for its 128 channels in TMEM, so the
-//     weights are streamed from HBM once whatever M = B*(k+1) is -- there is no M-tile
-//     staircase (the reference re-streams the weights for every BLOCK_M rows).
+//     holds the INT32 accumulators of up to 288 tokens (the largest verification batch,
+//     32 x 9) for its 128 channels in TMEM -- two MMAs per K step past 256 tokens, the
+//     instruction's N limit -- so the weights are streamed from HBM once whatever
+//     M = B*(k+1) is: there is no M-tile staircase (the reference re-streams the weights for
+//     every BLOCK_M rows), and a plan-buffer graph sized for M = 288 has the same grid and
+//     split-K as an eager call at any smaller M.
 //   * TMA loads 128-byte-swizzled [128 x 128 B] weight tiles and the token chunk's activations
 //     (one box of the whole chunk, or 16-row boxes for a ragged last chunk) into a multi-stage
 //     mbarrier ring; one elected thread issues tcgen05.mma kind::i8 (M=128, N=tokens rounded
@@ -43,7 +46,8 @@ struct W8A8Params {
   int64_t lda, ldw, ldo, ldo_n, ldacc;
   int m_rows;          // rows the kernel may touch (grid extent)
   int N, K;
-  int chunk;           // tokens per CTA along grid.z (multiple of 16, <= 256)
+  int chunk;           // tokens per CTA along grid.y (multiple of 16, <= kW8A8MaxChunk)
+  int chunk_box;       // rows of one activation TMA box of a whole chunk (chunk, or chunk / 2)
   int kb_total;        // ceil(K / 128)
   int kb_per_split;    // 128-byte K blocks per split-K CTA
   int splits;          // cluster size along grid.x
@@ -56,12 +60,21 @@ struct W8A8Params {
 constexpr int kW8A8Threads = 192;  // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue (+ LDG producer)
 constexpr uint32_t kW8A8WTile = 128 * 128;  // bytes of one weight tile
 constexpr int kW8A8MaxStages = 8;
+constexpr int kW8A8MaxChunk = 288;          // tokens per CTA: 256 + 32 in a second MMA
+
+// Activation tensor maps: boxes of 16, 32, 64 and 128 rows (a token chunk of any multiple of 16
+// rows arrives in at most four copies -- TMA copies issue one after another), and one box of a
+// whole chunk (or half of one past 256 rows).
+struct W8A8ActMaps {
+  CUtensorMap rows[4];   // 16, 32, 64, 128 rows x 128 bytes
+  CUtensorMap chunk;     // chunk_box rows x 128 bytes
+};
 
 // VEC = 0: TMA producer; VEC in {16, 8, 4, 2, 1}: register-staged loads of that width.
 template <int VEC>
 __global__ void __launch_bounds__(kW8A8Threads, 1)
     w8a8_kernel(const __grid_constant__ W8A8Params p, const __grid_constant__ CUtensorMap tmap_w,
-                const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_a_chunk) {
+                const __grid_constant__ W8A8ActMaps tmap_a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   SPECQ_TRACE_INIT();
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -73,8 +86,8 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
   uint64_t* red_full = acc_full + 1;                          // split-K: the peers' rows landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kW8A8MaxStages + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* sa_s = reinterpret_cast<float*>(tmem_slot + 4);      // [256] token scales of this chunk
-  float* sw_s = sa_s + 256;                                   // [128] channel scales of this tile
+  float* sa_s = reinterpret_cast<float*>(tmem_slot + 4);      // [kW8A8MaxChunk] token scales of this chunk
+  float* sw_s = sa_s + kW8A8MaxChunk;                         // [128] channel scales of this tile
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -134,8 +147,8 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
   }
   if (warp == 0 && VEC == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_w);
-    tma_prefetch_desc(&tmap_a);
-    tma_prefetch_desc(&tmap_a_chunk);
+    for (int i = 0; i < 4; ++i) tma_prefetch_desc(&tmap_a.rows[i]);
+    tma_prefetch_desc(&tmap_a.chunk);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, p.tmem_cols);
@@ -163,10 +176,13 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
         mbar_arrive_expect_tx(&full[s], kW8A8WTile + a_bytes);
         const int kx = kblock(i) * 128;
         tma_load_2d(wt, &tmap_w, &full[s], kx, n0, pol_w);
-        if (a_rows == p.chunk) {   // a whole chunk: one box (TMA issue is serial)
-          tma_load_2d(at, &tmap_a_chunk, &full[s], kx, m0, pol_a);
-        } else {
-          for (int r = 0; r < a_rows; r += 16) tma_load_2d(at + r * 128, &tmap_a, &full[s], kx, m0 + r, pol_a);
+        if (a_rows == p.chunk) {   // a whole chunk: one box, or two past 256 rows (TMA issue is serial)
+          for (int r = 0; r < a_rows; r += p.chunk_box) tma_load_2d(at + r * 128, &tmap_a.chunk, &full[s], kx, m0 + r, pol_a);
+        } else {   // a ragged chunk (the last one, or the active rows of a plan-graph launch)
+          int r = 0;
+          for (int b = 3; b >= 0; --b)
+            for (const int box = 16 << b; a_rows - r >= box; r += box)
+              tma_load_2d(at + r * 128, &tmap_a.rows[b], &full[s], kx, m0 + r, pol_a);
         }
         ++issued;
         if (++s == stages) {
@@ -182,7 +198,11 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
     }
   } else if (warp == 1) {
     if (elect_one()) {
-      const uint32_t idesc = idesc_i8(128, n_pad);
+      // tokens [0, 256) in one MMA, the rest (at most 32, at TMEM column 256) in a second
+      const uint32_t n_lo = n_pad < 256u ? n_pad : 256u;
+      const uint32_t n_hi = n_pad - n_lo;
+      const uint32_t idesc = idesc_i8(128, n_lo);
+      const uint32_t idesc_hi = idesc_i8(128, n_hi > 0u ? n_hi : 16u);
       // descriptors advanced by address offsets in 16-byte units; ring index by a counter
       const uint64_t wdesc0 = sdesc_sw128(smem_u32(ring), 16u, 1024u);
       int s = 0;
@@ -194,8 +214,11 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
         const uint64_t wd = wdesc0 + ((static_cast<uint32_t>(s) * stage_bytes) >> 4);
         const uint64_t ad = wd + (kW8A8WTile >> 4);
 #pragma unroll
-        for (int k = 0; k < 4; ++k)   // 32 K bytes per step
+        for (int k = 0; k < 4; ++k) {   // 32 K bytes per step
           umma_i8_ss(tmem_acc, wd + 2u * k, ad + 2u * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+          if (n_hi > 0u)   // token rows 256.. start 256 * 128 bytes into the activation tile
+            umma_i8_ss(tmem_acc + 256u, wd + 2u * k, ad + 2048u + 2u * k, idesc_hi, (i > 0 || k > 0) ? 1u : 0u);
+        }
         umma_commit(&empty[s]);   // stage is free once these MMAs have read it
         SPECQ_TRACE_POINT(4, i);
         if (++s == stages) {

@@ -48,7 +48,7 @@ SIGNATURES = {
     "specq_last_launch": (_i32, [_pi32, _pi32, _pi32, _pi32, _pi32, _pi32, _pi32]),
     "specq_get_status": (_i32, [_pi32, _i32]),
     "specq_selftest_wait_timeout": (_i32, [_u64, _vp]),
-    "specq_mma_peak": (_i32, [_i32, _i32, _i32, _vp, _vp]),
+    "specq_mma_peak": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
     "specq_trace_configure": (_i32, [_vp, _i32]),
 }
 

@@ -173,3 +173,26 @@ def test_checks_catch_a_planted_causal_mistake(golden):
     full = np.zeros_like(g["ref"])
     full[:, : ql - 1] = out[:, : ql - 1]
     assert O.max_abs_err(full[:, : ql - 1], g["ref"][:, 1:ql]) > 1e-2 or O.max_abs_err(full, g["ref"]) > 1e-2
+
+
+def test_oracle_kv_quant_reproduces_reference_cache(golden):
+    """kv_quant_rows (the per-token cache quantiser the stack's KV append restates) gives the
+    reference fixture's int8 cache and fp16 scales (make_paged_kv, kernels.py:265-286) from the
+    same fp16 draws (CPU division semantics, as the fixture ran)."""
+    g = golden("attn_small")
+    gen = torch.Generator().manual_seed(5)
+    total = (37 + 15) // 16 + (70 + 15) // 16
+    torch.randperm(total, generator=gen)
+    kf = torch.randn((total, 16, 2, 128), generator=gen).half().numpy()
+    vf = torch.randn((total, 16, 2, 128), generator=gen).half().numpy()
+    for x, qk, sk in ((kf, "kc", "ks"), (vf, "vc", "vs")):
+        q, s = O.kv_quant_rows(x, on_cuda=False)
+        assert np.array_equal(q, g[qk]) and np.array_equal(s.view(np.uint16), g[sk].view(np.uint16))
+
+
+def test_oracle_residual_add_is_one_fp16_rounding():
+    rng = np.random.default_rng(3)
+    x = (rng.standard_normal(4096) * rng.choice([1e-3, 1.0, 300.0], 4096)).astype(np.float16)
+    r = (rng.standard_normal(4096) * rng.choice([1e-3, 1.0, 300.0], 4096)).astype(np.float16)
+    exact = (x.astype(np.float64) + r.astype(np.float64)).astype(np.float16)
+    assert np.array_equal(O.residual_add(x, r).view(np.uint16), exact.view(np.uint16))

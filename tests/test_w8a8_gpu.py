@@ -134,13 +134,15 @@ def test_plan_value_out_of_range_is_clamped_and_flagged(cuda):
     assert specq.get_status(clear=True) & 0x100
 
 
-@pytest.mark.parametrize("M", [257, 600])
-def test_more_tokens_than_one_tmem_chunk(cuda, M):
+@pytest.mark.parametrize("M,chunks", [(257, 1), (272, 1), (288, 1), (289, 2), (600, 3)])
+def test_token_chunks_past_one_mma(cuda, M, chunks):
+    """Up to 288 tokens (32 sequences x 9) share one CTA per channel tile: past 256 the second
+    MMA of each K step covers tokens 256.. at TMEM column 256.  More tokens take more chunks."""
     import specq
     a, sa, w, sw = _inputs(M, 384, 768, M)
     out, ck = specq.w8a8_matmul(a.cuda(), sa.cuda(), w.cuda(), sw.cuda())
     torch.cuda.synchronize()
-    assert ck.grid[1] >= 2      # grid = (split, token chunk, channel tile)
+    assert ck.grid[1] == chunks      # grid = (split, token chunk, channel tile)
     assert np.array_equal(_bits(out), O.w8a8_ref(a.numpy(), sa.numpy(), w.numpy(), sw.numpy()).view(np.uint16))
 
 
