@@ -76,12 +76,15 @@ struct AttnParams {
   int out_vec;             // out rows are 16-byte aligned: 8 head dims per store
 };
 
+// warps [0, 8) softmax, 8 K gather + 9 V gather (TMA), 10 MMA issue + TMEM owner,
+// [11, 15) V conversion
+constexpr int kAttnLoadWarps = 2;
+constexpr int kAttnMmaWarp = 8 + kAttnLoadWarps;
 constexpr int kAttnConvWarps = 4;              // one thread per token row of a block
+constexpr int kAttnThreads = 32 * (kAttnMmaWarp + 1) + 32 * kAttnConvWarps;
 constexpr uint32_t kAttnKV8 = 128 * 128;       // int8 K (or V) block: 128 tokens x 128 B
-constexpr uint32_t kAttnStage = 2 * kAttnKV8;  // K + V int8 (later the fp16 V tile: 128 tokens x 128 d)
-constexpr int kAttnMaxStages = 6;
-// threads of the CTA for NQ query rows: NQ/4 softmax warps, 2 gather, 1 MMA, kAttnConvWarps V
-__host__ __device__ constexpr int attn_threads(int nq) { return 32 * (nq / 4 + 3 + kAttnConvWarps); }
+constexpr uint32_t kAttnStage = 2 * kAttnKV8;  // K + V, both 128B-swizzled
+constexpr int kAttnMaxStages = 6;              // ring stages (the host fits as many as shared memory allows)
 constexpr int kAttnMaxPages = 2048;            // block-table entries of one CTA's context range
 constexpr uint32_t kAttnPTile = 128 * 128;     // fp16 P tile: 128 tokens x 64 query rows
 constexpr float kLazyMaxLog2 = 8.0f;           // rescale once a score exceeds the max by 2^8
@@ -201,28 +204,12 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// Warp roles of the CTA for NQ query rows: softmax warps [0, NQ/4) -- four TMEM lane quadrants
-// x NQ/16 column groups of 16 query columns --, then the K gather warp, the V gather warp, the
-// MMA warp (issuer and TMEM owner) and kAttnConvWarps V conversion warps.
 template <int NQ>
-struct AttnRoles {
-  static constexpr int kSoftWarps = NQ / 4;
-  static constexpr int kSoft = 32 * kSoftWarps;   // softmax threads (one 16-byte query piece each)
-  static constexpr int kKWarp = kSoftWarps;
-  static constexpr int kVWarp = kSoftWarps + 1;
-  static constexpr int kMmaWarp = kSoftWarps + 2;
-  static constexpr int kConvWarp0 = kSoftWarps + 3;
-  static constexpr int kThreads = 32 * (kConvWarp0 + kAttnConvWarps);
-};
-
-template <int NQ>
-__global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
+__global__ void __launch_bounds__(kAttnThreads, 1)
     paged_attn_kernel(const __grid_constant__ AttnParams p, const __grid_constant__ CUtensorMap tmap_k,
                       const __grid_constant__ CUtensorMap tmap_v) {
   static_assert(NQ % 16 == 0 && NQ >= 16 && NQ <= 64, "query rows per CTA");
-  using R = AttnRoles<NQ>;
-  constexpr int kSoft = R::kSoft;
-  constexpr int kCols = 16;     // query columns per softmax thread
+  constexpr int NQH = NQ / 2;   // query columns per softmax thread
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   SPECQ_TRACE_INIT();
   if (threadIdx.x == 0) {
@@ -233,11 +220,11 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
   pdl_wait();                // the previous kernel's writes are visible from here on
   if (threadIdx.x == 0) SPECQ_TRACE_POINT(3, 0);
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  // ring stage (32 KB): [K int8, 128 tokens x 128 B, 128B-swizzled (a tcgen05 operand as it lands)]
-  //                     [V int8, 128 tokens x 128 B, 128B-swizzled (read row-wise by the V warps)]
-  // Once QK has read K, the V warps overwrite the whole stage with the fp16 V tile
-  // [2 atom columns (d 0-63, 64-127)][128 tokens][128 B] that the PV product reads; the stage
-  // is refilled after PV has completed.
+  // ring stage: [K int8, 128 tokens x 128 B, 128B-swizzled (a tcgen05 operand as it lands)]
+  //             [V int8, 128 tokens x 128 B, 128B-swizzled (read row-wise by the V warps)]
+  // Once QK has read a stage's K half, the V warps overwrite the whole stage with the fp16 V
+  // tile [2 atom columns (d 0-63, 64-127)][128 tokens][128 B] the PV product reads; the stage is
+  // refilled after PV has completed.  No separate V buffers: the shared memory goes to ring depth.
   const int n_stages = p.stages;
   uint8_t* ring = smem;
   uint8_t* qop = ring + n_stages * kAttnStage;                     // int8 Q: hi rows [0,NQ), lo rows [NQ,2NQ)
@@ -247,10 +234,10 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
   float* alpha_s = nm_s + 64;                                      // [64]
   float* l_s = alpha_s + 64;                                       // [64]
   float* qamax = l_s + 64;                                         // [64] |q| max per query row
-  float* wmax = qamax + 64;                                        // [4][64] per lane quadrant
-  float* ks_ring = wmax + 256;                                     // [3][kSoft] softmax threads' K scales
-  float* vs_ring = ks_ring + 3 * kSoft;                            // [3][128] V threads' V scales
-  uint32_t* bias_s = reinterpret_cast<uint32_t*>(vs_ring + 3 * 128); // the bias MMA's B operand
+  float* wmax = qamax + 64;                                        // [4][64]
+  float* ks_ring = wmax + 256;                                     // [3][256] softmax threads' K scales
+  float* vs_ring = ks_ring + 3 * 256;                              // [3][128] V threads' V scales
+  uint32_t* bias_s = reinterpret_cast<uint32_t*>(vs_ring + 3 * 128); // the score bias, copied into TMEM
   int* pages_s = reinterpret_cast<int*>(bias_s + attn_bias_words(NQ)); // [kAttnMaxPages] this CTA's page ids
   uint64_t* bars = reinterpret_cast<uint64_t*>(pages_s + kAttnMaxPages);
   uint64_t* stage_full = bars;
@@ -296,25 +283,29 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
   // rows do not depend on one another: they are all requested here, so the prologue waits for
   // one memory round trip instead of three dependent ones.
   int L = __ldg(p.ctx_len + b);
-  // softmax warps: the raw fp16 query piece (row, 16 head dims) this thread quantises below
-  // (NQ rows x 8 pieces = one piece per softmax thread)
-  uint4 qraw[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
-  if (warp < static_cast<uint32_t>(R::kSoftWarps)) {
-    const int it = static_cast<int>(threadIdx.x);
-    const int row = it >> 3;
-    const int piece = it & 7;
-    if (row < rows_valid) {
-      const int qi = q_lo + (p.g_shift >= 0 ? (row >> p.g_shift) : (row / p.g));
-      const int head = kvh * p.g + (p.g_shift >= 0 ? (row & (p.g - 1)) : (row % p.g));
-      const uint4* src = reinterpret_cast<const uint4*>(p.q + b * q_sb + static_cast<int64_t>(qi) * p.q_st +
-                                                        static_cast<int64_t>(head) * p.q_sh) + 2 * piece;
-      qraw[0] = ldg_nc_v4_now(src);
-      qraw[1] = ldg_nc_v4_now(src + 1);
+  // softmax warps: the raw fp16 query pieces (row, 16 head dims) this thread quantises below
+  constexpr int kItems = (NQ * 8 + 255) / 256;
+  uint4 qraw[kItems][2];
+  if (warp < 8) {
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+      const int it = static_cast<int>(threadIdx.x) + 256 * k;
+      const int row = it >> 3;
+      const int piece = it & 7;
+      qraw[k][0] = qraw[k][1] = make_uint4(0u, 0u, 0u, 0u);
+      if (it < NQ * 8 && row < rows_valid) {
+        const int qi = q_lo + (p.g_shift >= 0 ? (row >> p.g_shift) : (row / p.g));
+        const int head = kvh * p.g + (p.g_shift >= 0 ? (row & (p.g - 1)) : (row % p.g));
+        const uint4* src = reinterpret_cast<const uint4*>(p.q + b * q_sb + static_cast<int64_t>(qi) * p.q_st +
+                                                          static_cast<int64_t>(head) * p.q_sh) + 2 * piece;
+        qraw[k][0] = ldg_nc_v4_now(src);
+        qraw[k][1] = ldg_nc_v4_now(src + 1);
+      }
     }
   }
   const bool whole_row = p.bt_cols <= kAttnMaxPages;
   if (whole_row)
-    for (int i = static_cast<int>(threadIdx.x); i < p.bt_cols; i += R::kThreads)
+    for (int i = static_cast<int>(threadIdx.x); i < p.bt_cols; i += kAttnThreads)
       pages_s[i] = __ldg(p.bt + b * p.bt_sb + i);
   if (L < 0 || L > p.bt_cols * p.page) {
     if (threadIdx.x == 0 && split == 0) report_status(p.status, SPECQ_STATUS_PLAN_CLAMPED);
@@ -330,7 +321,7 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
   constexpr uint32_t cs2 = static_cast<uint32_t>((2 * NQ + 31) & ~31);   // S buffer: hi columns, lo columns
   constexpr uint32_t kOCols = static_cast<uint32_t>((NQ + 31) & ~31);
   constexpr uint32_t O_col = 2 * cs2;
-  constexpr uint32_t L_col = O_col + kOCols;   // per-lane partial normalisers [128 lanes x NQ]
+  constexpr uint32_t L_col = O_col + kOCols;
   constexpr uint32_t ONES_col = L_col + kOCols;
   auto page_of = [&](int tok) { return p.page_shift >= 0 ? (tok >> p.page_shift) : (tok / p.page); };
   auto slot_of = [&](int tok) { return p.page_shift >= 0 ? (tok & (p.page - 1)) : (tok % p.page); };
@@ -341,7 +332,7 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
   const int pg_first = whole_row ? 0 : page_of(t_begin);
   if (!whole_row) {
     const int pg_count = nblk > 0 ? page_of(t_end - 1) - pg_first + 1 : 0;
-    for (int i = static_cast<int>(threadIdx.x); i < pg_count; i += R::kThreads)
+    for (int i = static_cast<int>(threadIdx.x); i < pg_count; i += kAttnThreads)
       pages_s[i] = __ldg(p.bt + b * p.bt_sb + pg_first + i);
   }
   // page id of token row `row` of block j (-1 past the split end)
@@ -349,7 +340,12 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
     const int tok = t_begin + j * 128 + row;
     return (j < nblk && tok < t_end) ? pages_s[page_of(tok) - pg_first] : -1;
   };
-  // element offset of that token's (page, slot, kv head) in the scales
+  // element offset of that token's (page, slot, kv head) in the KV cache and in the scales
+  auto kv_offset = [&](int j, int row, int page) -> int64_t {
+    const int tok = t_begin + j * 128 + row;
+    return static_cast<int64_t>(page) * p.kv_sp + static_cast<int64_t>(slot_of(tok)) * p.kv_so +
+           static_cast<int64_t>(kvh) * p.kv_sh;
+  };
   auto scale_offset = [&](int j, int row, int page) -> int64_t {
     const int tok = t_begin + j * 128 + row;
     return static_cast<int64_t>(page) * p.s_sp + static_cast<int64_t>(slot_of(tok)) * p.s_so +
@@ -415,8 +411,8 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
   // commit (s_full) comes after PV(i) from the same thread, so it also covers PV(i); only the
   // last two blocks, which have no QK(i+2), commit to pv_done (each buffer once: phase 0).
   // A parity wait is only meaningful when the barrier can be neither behind nor two phases
-  // ahead of the awaited phase: the softmax has seen every earlier S complete, and QK(i+2) can
-  // complete only after V(i) is released, which needs QK(i) complete.
+  // ahead of the awaited phase: the softmax has seen every earlier S complete, and the V warps
+  // see QK(0) / QK(1) complete before they release V(0) / V(1).
   auto wait_pv = [&](int i, int code) -> bool {
     if (i + 2 < nblk) return mbar_wait(&s_full[i & 1], static_cast<uint32_t>((i + 2) >> 1) & 1u, p.status, code);
     return mbar_wait(&pv_done[i & 1], 0u, p.status, code);
@@ -431,13 +427,13 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&v_full[i], kAttnConvWarps);
       mbar_init(&s_full[i], 1u);
-      mbar_init(&p_full[i], static_cast<uint32_t>(R::kSoftWarps));
+      mbar_init(&p_full[i], 8u);
       mbar_init(&pv_done[i], 1u);
     }
-    mbar_init(q_full, static_cast<uint32_t>(R::kSoftWarps));
+    mbar_init(q_full, 8u);
     fence_barrier_init();
   }
-  if (warp == static_cast<uint32_t>(R::kMmaWarp)) {
+  if (warp == kAttnMmaWarp) {
     tmem_alloc(tmem_slot, p.tmem_cols);
     tmem_relinquish();
   }
@@ -449,52 +445,64 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
   bool ok = true;
   if (threadIdx.x == 0) SPECQ_TRACE_POINT(1, 0);
 
-  if (warp < static_cast<uint32_t>(R::kSoftWarps)) {
+  if (warp < 8) {
     // =================================== softmax warps ===================================
-    // Warp w serves TMEM lane quadrant w % 4 (32 tokens of S^T, 32 head dims of O^T) and query
-    // column group w / 4 (16 columns).  Thread = one token row of the block.
-    const int t = static_cast<int>(threadIdx.x);             // 0 .. kSoft-1
+    // Warps w and w+4 share TMEM lane quadrant w: the same 32 tokens of S^T (the same 32 head
+    // dims of O^T).  Warps 0-3 take the first half of the query columns, warps 4-7 the second.
+    const int t = static_cast<int>(threadIdx.x);             // 0..255
     const int tl = t & 127;                                  // token lane of S^T, d lane of O^T
     const int grp = t >> 7;
-    const int col0 = grp * kCols;
+    const int col0 = grp * NQH;
     const uint32_t quad = warp & 3u;
     const uint32_t lane_base = tmem + ((quad * 32u) << 16);
     // Q rows -> int16 with one scale for the CTA (gmax / 32639), split as hi * 256 + lo with
     // hi, lo int8: two int8 operand rows each, so QK^T runs on the INT8 tensor core against
     // the raw K bytes.  One scale makes the score scale a per-token scalar (no per-column
     // constant); the rounding error of every row is relative to the CTA's largest |q|.
-    float qv[16];
-    {
-      const int row = t >> 3;
+    float qv[kItems][16];   // (row, 16 head dims) pieces of this thread, loaded in the prologue
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+      const int it = t + 256 * k;
+      const int row = it >> 3;
+      const int piece = it & 7;
       float amax = 0.f;
-      const uint32_t w[8] = {qraw[0].x, qraw[0].y, qraw[0].z, qraw[0].w, qraw[1].x, qraw[1].y, qraw[1].z, qraw[1].w};
+      if (it < NQ * 8 && row < rows_valid) {
+        const uint4 u0 = qraw[k][0], u1 = qraw[k][1];
+        const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-        qv[2 * i] = f.x;
-        qv[2 * i + 1] = f.y;
+        for (int i = 0; i < 8; ++i) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+          qv[k][2 * i] = f.x;
+          qv[k][2 * i + 1] = f.y;
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(qv[k][i]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) qv[k][i] = 0.f;
       }
-#pragma unroll
-      for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(qv[i]));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-      if ((t & 7) == 0) qamax[row] = amax;
+      if (it < NQ * 8 && piece == 0) qamax[row] = amax;
     }
-    named_barrier_sync(3, kSoft);
+    named_barrier_sync(3, 256);
     if (t == 0) SPECQ_TRACE_POINT(11, 0);
     // the CTA's largest |q|: two rows per lane, one warp reduction (|q| >= 0, so 0 is neutral)
     const float gmax = warp_max_f32(fmaxf(static_cast<int>(lane) < NQ ? qamax[lane] : 0.f,
                                           static_cast<int>(lane) + 32 < NQ ? qamax[lane + 32] : 0.f));
     const float q_inv = gmax > 0.f ? 32639.f / gmax : 0.f;
     const float q_scale = gmax / 32639.f;
-    {
-      const int row = t >> 3;
-      const int piece = t & 7;
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+      const int it = t + 256 * k;
+      if (it >= NQ * 8) break;
+      const int row = it >> 3;
+      const int piece = it & 7;
       uint32_t hw[4] = {0u, 0u, 0u, 0u}, lw[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const int v16 = __float2int_rn(qv[i] * q_inv);       // |v16| <= 32639
+        const int v16 = __float2int_rn(qv[k][i] * q_inv);    // |v16| <= 32639
         const int hi = (v16 + 128) >> 8;                     // in [-127, 127]
         const int lo = v16 - (hi << 8);                      // in [-128, 127]
         hw[i >> 2] |= (static_cast<uint32_t>(hi) & 0xFFu) << (8 * (i & 3));
@@ -511,9 +519,10 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
       alpha_s[t] = 1.f;
       l_s[t] = 0.f;
     }
+    // the constant the MMA issuer copies into a score buffer before each QK (tcgen05.cp)
     // B operand of the bias MMA: fp16 768.0 pairs (see kScoreBias)
-    for (int w = t; w < attn_bias_words(NQ); w += kSoft) bias_s[w] = kBias768x2;
-    if (grp == 0) {   // A operand of the bias MMA in TMEM: 8 columns of fp16 1024.0 (after 8 unused)
+    for (int w = t; w < attn_bias_words(NQ); w += 256) bias_s[w] = kBias768x2;
+    if (grp == 0) {   // A operands in TMEM: 8 columns of fp16 1.0 (normaliser), 8 of 1024.0 (bias)
       uint32_t ones[16];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -522,34 +531,28 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
       }
       tmem_st16(lane_base + ONES_col, ones);
     }
-    {   // the normaliser partials of this thread's lane and columns start at 0
-      uint32_t z[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) z[i] = 0u;
-      tmem_st16(lane_base + L_col + col0, z);
-    }
     tmem_wait_st();
     fence_proxy_async_smem();
     tc_fence_before();
-    named_barrier_sync(3, kSoft);
+    named_barrier_sync(3, 256);
     __syncwarp();
     if (lane == 0) mbar_arrive(q_full);
     if (t == 0) SPECQ_TRACE_POINT(13, 0);
 
     // -max of this thread's query columns, kept in registers (changes only on a rescale)
-    float nmr[kCols];
+    float nmr[NQH];
 #pragma unroll
-    for (int i = 0; i < kCols; ++i) nmr[i] = nm_s[col0 + i];
+    for (int i = 0; i < NQH; ++i) nmr[i] = nm_s[col0 + i];
 
     // Multi-thread roles never leave a loop early: after a wait runs out (ok = false) they skip
     // the remaining waits but still reach every named barrier, so no warp is stranded.
     // One copy of the block body (a plain loop, not unrolled): the softmax, V and MMA roles
     // share each scheduler's instruction cache, so the hot code is kept small.
-    float* ksd = ks_ring + t;     // this thread's K-scale slots (stride kSoft)
+    float* ksd = ks_ring + t;     // this thread's K-scale slots (stride 256)
     uint32_t ksel = 0u;
     const ScaleRow krow = scale_row(tl);
     fetch_scale(p.ks, 0, krow, scale_page(0, krow), ksd, ksel, 0);
-    fetch_scale(p.ks, 1, krow, scale_page(1, krow), ksd + kSoft, ksel, 1);
+    fetch_scale(p.ks, 1, krow, scale_page(1, krow), ksd + 256, ksel, 1);
     int slot = 0;                 // j % 3
 #pragma unroll 1
     for (int j = 0; j < nblk; ++j) {
@@ -564,9 +567,12 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
       if (t == 0) SPECQ_TRACE_POINT(20, j);
       cp_async_wait<1>();   // block j's scale (fetched two blocks ago) has landed
       // this token's score scale: K scale x log2(e) / sqrt(D) x the query scale
-      const float a_t = read_scale(ksd + kSoft * slot, ksel, slot) * p.sm_scale_log2 * q_scale;
-      fetch_scale(p.ks, j + 2, krow, pg2, ksd + kSoft * slot2, ksel, slot2);
+      const float a_t = read_scale(ksd + 256 * slot, ksel, slot) * p.sm_scale_log2 * q_scale;
+      // block j + 2's scale into the slot block j - 1 used (issued here, at the top of the
+      // block, it measured faster than after the P pass)
+      fetch_scale(p.ks, j + 2, krow, pg2, ksd + 256 * slot2, ksel, slot2);
       // S(j) is ready; its commit also covers PV(j-2), so P buffer sb is free as well
+      if (t == 0) SPECQ_TRACE_POINT(23, j);
       ok = ok && mbar_wait(&s_full[sb], par2, status, SPECQ_STATUS_TIMEOUT_MMA);
       tc_fence_after();
       if (t == 0) SPECQ_TRACE_POINT(21, j);
@@ -581,42 +587,50 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
       auto score = [&](uint32_t hb, uint32_t lb) {
         return (fmaf(__uint_as_float(hb), 256.f, __uint_as_float(lb)) - kScoreBias257) * a_t;
       };
-      // this block's contribution to the thread's normaliser partials (the fp16-rounded p the
-      // PV product uses), from the pass whose P is kept
-      float2 psum[kCols / 2];
       // One pass: P against the current max, noting the largest exponent.
       auto write_p = [&](float& xmax) {
-        uint32_t rh[16], rl[16];
-        tmem_ld8(s_addr, *reinterpret_cast<uint32_t(*)[8]>(rh));
-        tmem_ld8(s_addr + 8, *reinterpret_cast<uint32_t(*)[8]>(rh + 8));
-        tmem_ld8(s_addr + NQ, *reinterpret_cast<uint32_t(*)[8]>(rl));
-        tmem_ld8(s_addr + NQ + 8, *reinterpret_cast<uint32_t(*)[8]>(rl + 8));
-        tmem_wait_ld();
-        if (t == 0) SPECQ_TRACE_POINT(28, j);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int qb = col0 + 8 * h;
-          uint32_t pk[4];
-#pragma unroll
-          for (int i = 0; i < 8; i += 2) {
-            const int r0 = 8 * h + i;
-            const float2 hb = make_float2(__uint_as_float(rh[r0]), __uint_as_float(rh[r0 + 1]));
-            const float2 lb = make_float2(__uint_as_float(rl[r0]), __uint_as_float(rl[r0 + 1]));
-            const float2 sv = fadd2(ffma2(hb, make_float2(256.f, 256.f), lb),
-                                    make_float2(-kScoreBias257, -kScoreBias257));
-            float2 x = ffma2(sv, a2, make_float2(nmr[r0], nmr[r0 + 1]));
-            if (!interior) {   // causal window and split end; padding rows
-              const uint32_t span = static_cast<uint32_t>(q_stop - q_first);
-              x.x = static_cast<uint32_t>(qb + i - q_first) < span ? x.x : -INFINITY;
-              x.y = static_cast<uint32_t>(qb + i + 1 - q_first) < span ? x.y : -INFINITY;
-            }
-            xmax = fmax3(xmax, x.x, x.y);
-            const __half2 ph = __floats2half2_rn(fast_exp2(x.x), fast_exp2(x.y));
-            pk[i >> 1] = *reinterpret_cast<const uint32_t*>(&ph);
-            psum[r0 >> 1] = __half22float2(ph);
+        for (int c0 = 0; c0 < NQH; c0 += 16) {   // 16 columns per TMEM round trip (hi and lo)
+          constexpr int kW = 16;
+          // columns past the valid query rows (CTA-uniform) are padding: their P and O^T columns
+          // are never used (every output column of an MMA depends on its own column only)
+          if (col0 + c0 >= rows_valid) break;
+          uint32_t rh[kW], rl[kW];
+          const bool two = c0 + 8 < NQH && col0 + c0 + 8 < rows_valid;
+          tmem_ld8(s_addr + c0, *reinterpret_cast<uint32_t(*)[8]>(rh));
+          tmem_ld8(s_addr + NQ + c0, *reinterpret_cast<uint32_t(*)[8]>(rl));
+          if (two) {
+            tmem_ld8(s_addr + c0 + 8, *reinterpret_cast<uint32_t(*)[8]>(rh + 8));
+            tmem_ld8(s_addr + NQ + c0 + 8, *reinterpret_cast<uint32_t(*)[8]>(rl + 8));
           }
-          *reinterpret_cast<uint4*>(prow + sw128_offset(static_cast<uint32_t>(tl), static_cast<uint32_t>(qb >> 3))) =
-              make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          tmem_wait_ld();
+          if (t == 0 && c0 == 0) SPECQ_TRACE_POINT(28, j);
+          if (t == 0 && c0 == 16) SPECQ_TRACE_POINT(18, j);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (h == 1 && !two) break;
+            const int qb = col0 + c0 + 8 * h;
+            uint32_t pk[4];
+#pragma unroll
+            for (int i = 0; i < 8; i += 2) {
+              const int r0 = 8 * h + i;
+              const float2 hb = make_float2(__uint_as_float(rh[r0]), __uint_as_float(rh[r0 + 1]));
+              const float2 lb = make_float2(__uint_as_float(rl[r0]), __uint_as_float(rl[r0 + 1]));
+              const float2 sv = fadd2(ffma2(hb, make_float2(256.f, 256.f), lb),
+                                      make_float2(-kScoreBias257, -kScoreBias257));
+              float2 x = ffma2(sv, a2, make_float2(nmr[c0 + r0], nmr[c0 + r0 + 1]));
+              if (!interior) {   // causal window and split end; padding rows
+                const uint32_t span = static_cast<uint32_t>(q_stop - q_first);
+                x.x = static_cast<uint32_t>(qb + i - q_first) < span ? x.x : -INFINITY;
+                x.y = static_cast<uint32_t>(qb + i + 1 - q_first) < span ? x.y : -INFINITY;
+              }
+              xmax = fmax3(xmax, x.x, x.y);
+              const __half2 ph = __floats2half2_rn(fast_exp2(x.x), fast_exp2(x.y));
+              pk[i >> 1] = *reinterpret_cast<const uint32_t*>(&ph);
+            }
+            *reinterpret_cast<uint4*>(prow + sw128_offset(static_cast<uint32_t>(tl), static_cast<uint32_t>(qb >> 3))) =
+                make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          }
         }
       };
 #pragma unroll
@@ -628,18 +642,20 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
           float xmax = -INFINITY;
           write_p(xmax);
           if (pass == 1) break;
-          const bool need = named_barrier_or(2, kSoft, xmax > kLazyMaxLog2);
+          if (t == 0) SPECQ_TRACE_POINT(29, j);
+          if (t == 224) SPECQ_TRACE_POINT(19, j);
+          const bool need = named_barrier_or(2, 256, xmax > kLazyMaxLog2);
           if (t == 0) SPECQ_TRACE_POINT(22, j);
           if (!need) break;
         }
         // ---- rescale: some score exceeds the running max by more than 2^8 ----
         if (t == 0) SPECQ_TRACE_POINT(26, j);
-        // the running O^T must be final before it is rescaled
+        // the running O^T / normaliser must be final before they are rescaled
         if (j >= 1) ok = ok && wait_pv(j - 1, SPECQ_STATUS_TIMEOUT_MMA);
         tc_fence_after();
         // block max per query column: warp shuffles, then across the four lane quadrants
 #pragma unroll
-        for (int c0 = 0; c0 < kCols; c0 += 8) {
+        for (int c0 = 0; c0 < NQH; c0 += 8) {
           uint32_t rh[8], rl[8];
           tmem_ld8(s_addr + c0, rh);
           tmem_ld8(s_addr + NQ + c0, rl);
@@ -651,7 +667,7 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
             if (lane == 0) wmax[quad * 64 + q] = y;
           }
         }
-        named_barrier_sync(3, kSoft);
+        named_barrier_sync(3, 256);
         if (t < NQ) {
           const float mb = fmaxf(fmaxf(wmax[t], wmax[64 + t]), fmaxf(wmax[128 + t], wmax[192 + t]));
           const float mo = m_s[t];
@@ -660,25 +676,25 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
           m_s[t] = mn;
           nm_s[t] = -mn;
         }
-        named_barrier_sync(3, kSoft);
+        named_barrier_sync(3, 256);
 #pragma unroll
-        for (int i = 0; i < kCols; ++i) nmr[i] = nm_s[col0 + i];
-        if (j > 0) {   // rescale this thread's lane of O^T and of its normaliser partials
-          tmem_wait_st();
+        for (int i = 0; i < NQH; ++i) nmr[i] = nm_s[col0 + i];
+        if (j > 0) {   // rescale this group's columns of O^T (all lanes) and of the normaliser row
 #pragma unroll
-          for (int c0 = 0; c0 < kCols; c0 += 8) {
-            uint32_t r[8], l8[8];
+          for (int c0 = 0; c0 < NQH; c0 += 8) {
+            uint32_t r[8];
             tmem_ld8(lane_base + O_col + col0 + c0, r);
-            tmem_ld8(lane_base + L_col + col0 + c0, l8);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float al = alpha_s[col0 + c0 + i];
-              r[i] = __float_as_uint(__uint_as_float(r[i]) * al);
-              l8[i] = __float_as_uint(__uint_as_float(l8[i]) * al);
-            }
+            for (int i = 0; i < 8; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha_s[col0 + c0 + i]);
             tmem_st8(lane_base + O_col + col0 + c0, r);
-            tmem_st8(lane_base + L_col + col0 + c0, l8);
+            if (quad == 0) {
+              tmem_ld8(lane_base + L_col + col0 + c0, r);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 8; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha_s[col0 + c0 + i]);
+              tmem_st8(lane_base + L_col + col0 + c0, r);
+            }
           }
           tmem_wait_st();
         }
@@ -689,57 +705,40 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[sb]);
       if (t == 0) SPECQ_TRACE_POINT(24, j);
-      // normaliser partials += this block's p (after the arrive: the MMA issuer does not wait)
-      {
-        tmem_wait_st();
-        uint32_t l16[16];
-        tmem_ld16(lane_base + L_col + col0, l16);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < kCols; i += 2) {
-          const float2 v = fadd2(make_float2(__uint_as_float(l16[i]), __uint_as_float(l16[i + 1])), psum[i >> 1]);
-          l16[i] = __float_as_uint(v.x);
-          l16[i + 1] = __float_as_uint(v.y);
-        }
-        tmem_st16(lane_base + L_col + col0, l16);
-      }
       if (t == 0) SPECQ_TRACE_POINT(27, j);
       slot = slot == 2 ? 0 : slot + 1;
     }
     cp_async_wait<0>();
-    // ---- final normaliser: the sum of the 128 lanes' partials of every column ----
+    // ---- final normaliser and accumulator ----
     if (nblk > 0) {
       // bounded even after a failure: the tensor core must be idle before TMEM is freed
       const int jl = nblk - 1;
       ok = wait_pv(jl, SPECQ_STATUS_TIMEOUT_MMA) && ok;
       tc_fence_after();
       if (t == 0) SPECQ_TRACE_POINT(60, 0);
-    }
-    tmem_wait_st();
-    {
-      uint32_t l16[16];
-      tmem_ld16(lane_base + L_col + col0, l16);
-      tmem_wait_ld();
+      if (quad == 0) {
 #pragma unroll
-      for (int i = 0; i < kCols; ++i) {
-        float v = __uint_as_float(l16[i]);
+        for (int c0 = 0; c0 < NQH; c0 += 8) {
+          uint32_t r[8];
+          tmem_ld8(lane_base + L_col + col0 + c0, r);
+          tmem_wait_ld();
+          if (lane == 0) {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);   // fixed order
-        if (lane == 0) wmax[quad * 64 + col0 + i] = v;
+            for (int i = 0; i < 8; ++i) l_s[col0 + c0 + i] = __uint_as_float(r[i]);
+          }
+        }
       }
     }
-    named_barrier_sync(3, kSoft);
-    if (t < NQ) l_s[t] = (wmax[t] + wmax[64 + t]) + (wmax[128 + t] + wmax[192 + t]);
-    named_barrier_sync(3, kSoft);
-  } else if (warp < static_cast<uint32_t>(R::kMmaWarp)) {
+    named_barrier_sync(3, 256);
+  } else if (warp < kAttnMmaWarp) {
     // =================================== K / V gather ===================================
-    // K (first gather warp) and V (second) arrive by TMA in boxes of box_rows slots of one page
-    // and one KV head, both 128B-swizzled (K in the layout the tensor core reads, V so the V
-    // warps' row reads are free of bank conflicts); lane b issues box b of a block, the two
-    // warps in parallel.  Invalid pages map past the tensor, which the TMA fills with zeros.
-    // Bytes in flight cost no registers here: the ring depth alone sets how much of the HBM
-    // latency is covered.
-    const bool is_v = warp == static_cast<uint32_t>(R::kVWarp);
+    // K (warp 8) and V (warp 9) arrive by TMA in boxes of box_rows slots of one page and one
+    // KV head, both 128B-swizzled (K in the layout the tensor core reads, V so the V warps' row
+    // reads are free of bank conflicts); lane b issues box b of a block, the two warps in
+    // parallel.  Invalid pages map past the tensor, which the TMA fills with zeros.  Bytes in
+    // flight cost no registers here: the ring depth alone sets how much of the HBM latency is
+    // covered.
+    const bool is_v = warp == 9;
     const CUtensorMap* tmap = is_v ? &tmap_v : &tmap_k;
     const uint32_t half_off = is_v ? kAttnKV8 : 0u;
     const int l = static_cast<int>(lane);
@@ -750,7 +749,7 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
     uint32_t phase = 0;
     int issued = 0;
     for (int j = 0; j < nblk; ++j) {
-      if (!mbar_wait(&stage_empty[s], phase ^ 1u, status, SPECQ_STATUS_TIMEOUT_PIPELINE)) {
+      if (!mbar_wait_sleep(&stage_empty[s], phase ^ 1u, 128u, status, SPECQ_STATUS_TIMEOUT_PIPELINE)) {
         ok = false;
         break;
       }
@@ -778,12 +777,13 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
         (void)mbar_wait(&stage_full[jj % n_stages], static_cast<uint32_t>(jj / n_stages) & 1u, status,
                         SPECQ_STATUS_TIMEOUT_PIPELINE);
     }
-  } else if (warp == static_cast<uint32_t>(R::kMmaWarp)) {
+  } else if (warp == kAttnMmaWarp) {
     // =================================== MMA issuer ===================================
     if (elect_one()) {
       const uint32_t id_qk = idesc_i8(128, static_cast<uint32_t>(2 * NQ));       // hi and lo columns
       // V^T (A) and P (B) both MN-major
       const uint32_t id_pv = idesc_f16(128, static_cast<uint32_t>(NQ), 1u, 1u);
+      const uint32_t id_l = idesc_f16(128, static_cast<uint32_t>(NQ), 0u, 1u);
       const uint32_t ring_a = smem_u32(ring), qop_a = smem_u32(qop), pop_a = smem_u32(pop);
       // B of the bias MMA: K-major, no swizzle, both K core matrices (128 B apart) in bias_s and
       // every 8-row group at the same address (stride 0): 256 bytes serve any N
@@ -811,10 +811,10 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
       };
       // QK(0) and QK(1) alone; then, per block i, once the softmax has finished block i (P(i)
       // written and score buffer i read for the last time, both signalled by p_full(i)) and V(i)
-      // is converted: PV(i) interleaved with QK(i+2).  Two independent accumulation chains (O
-      // and the next scores) are then in flight in the tensor pipe instead of one at a time.
-      // The normaliser is not a tensor-core product: the softmax threads keep per-lane partial
-      // sums.  The blocking waits keep this thread off the issue slots the softmax warps need.
+      // is converted: PV(i) interleaved with QK(i+2).  Three independent accumulation chains
+      // (O, the normaliser, the next scores) are then in flight in the tensor pipe instead of
+      // one at a time.  The blocking waits keep this thread off the issue slots the softmax
+      // warps need.
       if (nblk > 0) ok = mbar_wait(q_full, 0u, status, SPECQ_STATUS_TIMEOUT_PIPELINE);
       for (int j = 0; ok && j < min(2, nblk); ++j) {
         ok = mbar_wait(&stage_full[qk_stage], qk_phase, status, SPECQ_STATUS_TIMEOUT_PIPELINE);
@@ -835,9 +835,9 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
         const uint32_t bi = static_cast<uint32_t>(i & 1);   // P / V buffer of block i = score buffer of i + 2
         const uint32_t par = static_cast<uint32_t>(i >> 1) & 1u;
         const bool more = i + 2 < nblk;
-        ok = mbar_wait(&p_full[bi], par, status, SPECQ_STATUS_TIMEOUT_MMA) &&
-             mbar_wait(&v_full[bi], par, status, SPECQ_STATUS_TIMEOUT_PIPELINE) &&
-             (!more || mbar_wait(&stage_full[qk_stage], qk_phase, status, SPECQ_STATUS_TIMEOUT_PIPELINE));
+        ok = mbar_wait_sleep(&p_full[bi], par, 32u, status, SPECQ_STATUS_TIMEOUT_MMA) &&
+             mbar_wait_sleep(&v_full[bi], par, 32u, status, SPECQ_STATUS_TIMEOUT_PIPELINE) &&
+             (!more || mbar_wait_sleep(&stage_full[qk_stage], qk_phase, 32u, status, SPECQ_STATUS_TIMEOUT_PIPELINE));
         if (!ok) break;
         tc_fence_after();
         SPECQ_TRACE_POINT(32, i);
@@ -847,8 +847,11 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
         if (more) reset_scores(bi);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {   // 16 tokens (two 1024-byte atoms) per PV step
-          umma_f16_ss(tmem + O_col, vd + 128u * k, pd + 128u * k, id_pv, (i > 0 || k > 0) ? 1u : 0u);
+          const uint64_t bp = pd + 128u * k;
+          const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
+          umma_f16_ss(tmem + O_col, vd + 128u * k, bp, id_pv, acc);
           if (more && k < 4) umma_i8_ss(tmem + bi * cs2, kd + 2u * k, qdesc0 + 2u * k, id_qk, 1u);
+          umma_f16_ts(tmem + L_col, tmem + ONES_col, bp, id_l, acc);
         }
         if (more) {
           umma_commit(&s_full[bi]);   // QK(i+2) and, before it, PV(i)
@@ -864,24 +867,23 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
   } else {
     // =================================== V warps ===================================
     // Thread c owns token row c of every block: it reads the row's 128 V bytes from the ring
-    // (128B-swizzled, so eight consecutive rows hit eight distinct bank groups) and, once
-    // every row of the stage has been read and QK has consumed the stage's K half, writes the
-    // row converted to fp16 (the token's V scale folded in) over the stage as the PV operand.
-    const int c = static_cast<int>(threadIdx.x) - 32 * R::kConvWarp0;   // 0..127
+    // (128B-swizzled, so eight consecutive rows hit eight distinct bank groups), converts them
+    // to fp16 with the token's V scale folded in and stores the row into the V operand tile.
+    const int c = static_cast<int>(threadIdx.x) - 32 * (kAttnMmaWarp + 1);   // 0..127
     float* vsd = vs_ring + c;     // this thread's V-scale slots (stride 128)
     uint32_t vsel = 0u;
     const ScaleRow vrow_s = scale_row(c);
     fetch_scale(p.vs, 0, vrow_s, scale_page(0, vrow_s), vsd, vsel, 0);
     fetch_scale(p.vs, 1, vrow_s, scale_page(1, vrow_s), vsd + 128, vsel, 1);
     int slot = 0;                 // j % 3
-    int s = 0;                    // ring stage of block j
-    uint32_t sph = 0;
 #pragma unroll 1
     for (int j = 0; j < nblk; ++j) {
       const int slot2 = slot == 0 ? 2 : slot - 1;   // (j + 2) % 3
       const int pg2 = scale_page(j + 2, vrow_s);      // fetched after this block's conversion
+      const int s = j % n_stages;
       const uint32_t sb = static_cast<uint32_t>(j & 1);
-      ok = ok && mbar_wait(&stage_full[s], sph, status, SPECQ_STATUS_TIMEOUT_PIPELINE);
+      ok = ok && mbar_wait_sleep(&stage_full[s], static_cast<uint32_t>(j / n_stages) & 1u, 64u, status,
+                                 SPECQ_STATUS_TIMEOUT_PIPELINE);
       if (c == 0) SPECQ_TRACE_POINT(40, j);
       uint8_t* stage = ring + s * kAttnStage;
       const uint8_t* vrow = stage + kAttnKV8 + c * 128;
@@ -897,7 +899,7 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
       // be overwritten.  QK(j-2) was seen complete two blocks ago and QK(j+2) cannot complete
       // before V(j) is released, so the parity wait observes QK(j) itself.
       named_barrier_sync(4, 32 * kAttnConvWarps);
-      ok = ok && mbar_wait(&s_full[sb], static_cast<uint32_t>(j >> 1) & 1u, status, SPECQ_STATUS_TIMEOUT_MMA);
+      ok = ok && mbar_wait_sleep(&s_full[sb], static_cast<uint32_t>(j >> 1) & 1u, 64u, status, SPECQ_STATUS_TIMEOUT_MMA);
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {
         uint32_t h[8];
@@ -915,10 +917,6 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
       if (c == 0) SPECQ_TRACE_POINT(45, j);
       fetch_scale(p.vs, j + 2, vrow_s, pg2, vsd + 128 * slot2, vsel, slot2);
       slot = slot == 2 ? 0 : slot + 1;
-      if (++s == n_stages) {
-        s = 0;
-        sph ^= 1u;
-      }
     }
     cp_async_wait<0>();
   }
@@ -930,14 +928,14 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
   pdl_launch_dependents();
   // ======================= epilogue: normalise, combine splits, store =======================
   // softmax warps: thread tl owns head dim d = tl (TMEM lane) for its group's query columns
-  const bool soft = warp < static_cast<uint32_t>(R::kSoftWarps);
+  const bool soft = warp < 8;
   const int t = static_cast<int>(threadIdx.x);
   const int tl = t & 127;
-  const int col0 = (t >> 7) * kCols;
+  const int col0 = (t >> 7) * (NQ >> 1);
   const uint32_t o_lane = tmem + (((warp & 3u) * 32u) << 16) + O_col + static_cast<uint32_t>(col0);
   if (p.splits == 1) {
     if (soft && ok) {
-      for (int c0 = 0; c0 < kCols; c0 += 8) {
+      for (int c0 = 0; c0 < (NQ >> 1); c0 += 8) {
         uint32_t r[8];
         if (nblk > 0) {
           tmem_ld8(o_lane + c0, r);
@@ -977,7 +975,7 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
     if (soft) {
       const uint32_t dst = dsmem_map(smem_u32(comb), static_cast<uint32_t>(tl >> lgdr)) +
                            4u * static_cast<uint32_t>(split * NQ * dr + (tl & (dr - 1)));
-      for (int c0 = 0; c0 < kCols; c0 += 8) {
+      for (int c0 = 0; c0 < (NQ >> 1); c0 += 8) {
         uint32_t r[8];
         if (nblk > 0 && ok) {
           tmem_ld8(o_lane + c0, r);
@@ -1021,12 +1019,12 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
 #pragma unroll
         for (int pr = 0; pr < kS; ++pr) wts[pr * NQ + t] = w[pr] * inv;
       }
-      named_barrier_sync(3, kSoft);
+      named_barrier_sync(3, 256);
       if (t == 0) SPECQ_TRACE_POINT(63, 2);
       if (!ok) return;
       // one item = 8 consecutive head dims of one query row
       constexpr int kG8 = 128 / kS / 8;
-      for (int item = t; item < rows_valid * kG8; item += kSoft) {
+      for (int item = t; item < rows_valid * kG8; item += 256) {
         const int q = item / kG8;
         const int d8 = item % kG8;
         float acc[8];
@@ -1067,13 +1065,13 @@ __global__ void __launch_bounds__(AttnRoles<NQ>::kThreads, 1)
       if (t == 0) SPECQ_TRACE_POINT(63, 3);
     }
   }
-  if (threadIdx.x == kSoft) SPECQ_TRACE_POINT(63, 4);
+  if (threadIdx.x == 256) SPECQ_TRACE_POINT(63, 4);
 
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) SPECQ_TRACE_POINT(9, 0);
   SPECQ_TRACE_CTA_END();
-  if (warp == static_cast<uint32_t>(R::kMmaWarp)) {
+  if (warp == kAttnMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, p.tmem_cols);
   }
@@ -1177,13 +1175,10 @@ inline int run_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_
       return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: block table of %d pages per context split", tchunk_max / page);
   }
 
-  // ring of K/V stages + int8 Q (hi, lo) + two P tiles + softmax state + scale rings + block
-  // table + barriers; the ring takes what is left (up to kAttnMaxStages stages)
-  const int threads = attn_threads(p.nq);
-  const int n_soft = 32 * (p.nq / 4);
+  // int8 Q (hi, lo) + two P tiles + softmax state + scale rings + block table + barriers; the
+  // K/V ring takes the rest (up to kAttnMaxStages stages)
   const int fixed = 1024 + p.nq * 256 + 2 * static_cast<int>(kAttnPTile) + 4096 +
-                    (3 * n_soft + 3 * 128 + attn_bias_words(p.nq)) * 4 + kAttnMaxPages * 4 +
-                    (2 * kAttnMaxStages + 17) * 8 + 16;
+                    (3 * 256 + 3 * 128 + attn_bias_words(p.nq)) * 4 + kAttnMaxPages * 4 + (2 * kAttnMaxStages + 17) * 8 + 16;
   p.stages = std::min(kAttnMaxStages, (232448 - fixed) / static_cast<int>(kAttnStage));
   if (p.stages < 3) return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: %d ring stages do not fit", p.stages);
   const int smem = fixed + p.stages * static_cast<int>(kAttnStage);
@@ -1207,7 +1202,7 @@ inline int run_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_
   SPECQ_CUDA_TRY(ensure_dyn_smem(fn, smem));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
-  cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
+  cfg.blockDim = dim3(kAttnThreads, 1, 1);
   cfg.dynamicSmemBytes = static_cast<size_t>(smem);
   cfg.stream = static_cast<cudaStream_t>(stream);
   LaunchAttrs attrs(p.splits);
@@ -1218,7 +1213,7 @@ inline int run_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_
   r.variant = variant;
   r.grid[0] = static_cast<int>(grid.x); r.grid[1] = static_cast<int>(grid.y); r.grid[2] = static_cast<int>(grid.z);
   r.cluster_x = p.splits;
-  r.threads = threads;
+  r.threads = kAttnThreads;
   r.dyn_smem = smem;
   return SPECQ_OK;
 }

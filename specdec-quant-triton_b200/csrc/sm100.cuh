@@ -177,6 +177,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   }
 }
 
+// Bounded wait that sleeps between polls, for waiters whose wake-up latency a pipeline hides
+// (a producer waiting for a free stage, a converter or the MMA issuer waiting for its inputs):
+// a polling warp takes an issue slot on every try, a sleeping one leaves them to the warps
+// doing the arithmetic.  Returns false (and records `code`) when the wait limit runs out.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t sleep_ns, int* status,
+                                                int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    __nanosleep(sleep_ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      report_status(status, code);
+      return false;
+    }
+  }
+}
+
 // 16-byte read-only global load issued where it stands: volatile, so the compiler keeps it in
 // program order with the other volatile operations (ahead of a barrier, say) and its latency
 // overlaps what follows instead of being paid where the value is first used.

@@ -107,10 +107,29 @@ int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int
   p.splits = S;
   p.kb_per_split = ceil_div(p.kb_total, S);
 
-  p.stage_bytes = kW8A8WTile + static_cast<uint32_t>(round_up(p.chunk, 16)) * 128u;
+  // TMA needs 16-byte aligned bases and row strides; otherwise use the register-staged loader.
+  const bool tma_ok = aligned(a, 16) && aligned(w, 16) && (lda % 16 == 0) && (ldw % 16 == 0);
+  // The split's whole activation slice (its K-blocks x the chunk's rows) in one TMA copy before
+  // the main loop, when it is small: the stages then carry only weight tiles, one copy each.
+  const uint32_t a_slice = static_cast<uint32_t>(p.kb_per_split) * static_cast<uint32_t>(p.chunk) * 128u;
+  p.a_once = (tma_ok && p.chunk <= 256 && K % 128 == 0 && a_slice <= 96u * 1024u) ? 1 : 0;
+  CUtensorMap tw;
+  W8A8ActMaps ta;
+  memset(&tw, 0, sizeof(tw));
+  memset(&ta, 0, sizeof(ta));
+  if (p.a_once) {   // [K-block][row][128 B]: dims (128, M, K / 128), strides (lda, 128); else per stage
+    const uint64_t d3[3] = {128u, static_cast<uint64_t>(M), static_cast<uint64_t>(p.kb_total)};
+    const uint64_t s3[2] = {static_cast<uint64_t>(lda), 128u};
+    const uint32_t b3[3] = {128u, static_cast<uint32_t>(p.chunk), static_cast<uint32_t>(p.kb_per_split)};
+    if (encode_tiled(&ta.once, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, a, d3, s3, b3, CU_TENSOR_MAP_SWIZZLE_128B) != SPECQ_OK)
+      p.a_once = 0;
+  }
+  p.a_region_bytes = p.a_once ? a_slice : 0u;
+  p.stage_bytes = kW8A8WTile + (p.a_once ? 0u : static_cast<uint32_t>(round_up(p.chunk, 16)) * 128u);
   // split-K partial tile [128][chunk] int32 (padded rows), parked in the idle ring
   const uint32_t red_bytes = (S > 1) ? 128u * (static_cast<uint32_t>(round_up(p.chunk, 16)) * 4u + 16u) : 0u;
-  const int overhead = 1024 + 256 + (kW8A8MaxChunk + 128) * 4;   // alignment slack, barriers, staged scales
+  // alignment slack, barriers, staged scales (and the activation slice)
+  const int overhead = 1024 + 256 + (kW8A8MaxChunk + 128) * 4 + static_cast<int>(p.a_region_bytes);
   int stages = std::min(8, (kSmemLimit - overhead) / static_cast<int>(p.stage_bytes));
   if (stages < 2) return fail(SPECQ_ERR_UNSUPPORTED, "w8a8: token chunk %d does not fit shared memory", p.chunk);
   while (static_cast<uint32_t>(stages) * p.stage_bytes < red_bytes && stages < 8) ++stages;
@@ -120,12 +139,6 @@ int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int
   if (smem > kSmemLimit) return fail(SPECQ_ERR_UNSUPPORTED, "w8a8: shared memory %d > limit", smem);
   p.tmem_cols = static_cast<uint32_t>(std::max(32, next_pow2(p.chunk)));
 
-  // TMA needs 16-byte aligned bases and row strides; otherwise use the register-staged loader.
-  const bool tma_ok = aligned(a, 16) && aligned(w, 16) && (lda % 16 == 0) && (ldw % 16 == 0);
-  CUtensorMap tw;
-  W8A8ActMaps ta;
-  memset(&tw, 0, sizeof(tw));
-  memset(&ta, 0, sizeof(ta));
   int vec = 0;
   if (tma_ok) {
     const uint64_t dw[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
