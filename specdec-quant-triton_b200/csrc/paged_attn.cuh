@@ -84,7 +84,8 @@ constexpr int kAttnConvWarps = 4;              // one thread per token row of a 
 constexpr int kAttnThreads = 32 * (kAttnMmaWarp + 1) + 32 * kAttnConvWarps;
 constexpr uint32_t kAttnKV8 = 128 * 128;       // int8 K (or V) block: 128 tokens x 128 B
 constexpr uint32_t kAttnStage = 2 * kAttnKV8;  // K + V, both 128B-swizzled
-constexpr int kAttnMaxStages = 6;              // ring stages (the host fits as many as shared memory allows)
+constexpr uint32_t kAttnOp = 128 * 256;        // fp16 V tile: 128 tokens x 128 d
+constexpr int kAttnStages = 3;
 constexpr int kAttnMaxPages = 2048;            // block-table entries of one CTA's context range
 constexpr uint32_t kAttnPTile = 128 * 128;     // fp16 P tile: 128 tokens x 64 query rows
 constexpr float kLazyMaxLog2 = 8.0f;           // rescale once a score exceeds the max by 2^8
@@ -222,12 +223,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // ring stage: [K int8, 128 tokens x 128 B, 128B-swizzled (a tcgen05 operand as it lands)]
   //             [V int8, 128 tokens x 128 B, 128B-swizzled (read row-wise by the V warps)]
-  // Once QK has read a stage's K half, the V warps overwrite the whole stage with the fp16 V
-  // tile [2 atom columns (d 0-63, 64-127)][128 tokens][128 B] the PV product reads; the stage is
-  // refilled after PV has completed.  No separate V buffers: the shared memory goes to ring depth.
-  const int n_stages = p.stages;
   uint8_t* ring = smem;
-  uint8_t* qop = ring + n_stages * kAttnStage;                     // int8 Q: hi rows [0,NQ), lo rows [NQ,2NQ)
+  uint8_t* vop = ring + kAttnStages * kAttnStage;                  // fp16 V tiles x2 [2][128][128 B]
+  uint8_t* qop = vop + 2 * kAttnOp;                                // int8 Q: hi rows [0,NQ), lo rows [NQ,2NQ)
   uint8_t* pop = qop + NQ * 256;                                   // fp16 P x2 [2][128 tokens][128 B]
   float* m_s = reinterpret_cast<float*>(pop + 2 * kAttnPTile);     // [64] running max (log2 units)
   float* nm_s = m_s + 64;                                          // [64] -m_s
@@ -241,8 +239,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   int* pages_s = reinterpret_cast<int*>(bias_s + attn_bias_words(NQ)); // [kAttnMaxPages] this CTA's page ids
   uint64_t* bars = reinterpret_cast<uint64_t*>(pages_s + kAttnMaxPages);
   uint64_t* stage_full = bars;
-  uint64_t* stage_empty = stage_full + n_stages;
-  uint64_t* v_full = stage_empty + n_stages;      // [2]  V(j) converted in its stage
+  uint64_t* stage_empty = stage_full + kAttnStages;
+  uint64_t* v_full = stage_empty + kAttnStages;   // [2]
   uint64_t* s_full = v_full + 2;                  // [2]
   uint64_t* p_full = s_full + 2;                  // [2]  P(j) written, score buffer j % 2 read
   uint64_t* pv_done = p_full + 2;                 // [2]  PV of the last two blocks done (see wait_pv)
@@ -420,9 +418,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   // ---- setup ---------------------------------------------------------------------------------
   if (threadIdx.x == 0) {
-    for (int s = 0; s < n_stages; ++s) {
-      mbar_init(&stage_full[s], 2u);    // the K and the V gather lanes' expect_tx
-      mbar_init(&stage_empty[s], 1u);   // the commit after PV: K and the fp16 V tile are consumed
+    for (int s = 0; s < kAttnStages; ++s) {
+      mbar_init(&stage_full[s], 2u);                     // the K and the V gather lanes' expect_tx
+      mbar_init(&stage_empty[s], 1u + kAttnConvWarps);  // the QK commit + the V warps
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&v_full[i], kAttnConvWarps);
@@ -605,7 +603,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
           tmem_wait_ld();
           if (t == 0 && c0 == 0) SPECQ_TRACE_POINT(28, j);
-          if (t == 0 && c0 == 16) SPECQ_TRACE_POINT(18, j);
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             if (h == 1 && !two) break;
@@ -642,8 +639,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           float xmax = -INFINITY;
           write_p(xmax);
           if (pass == 1) break;
-          if (t == 0) SPECQ_TRACE_POINT(29, j);
-          if (t == 224) SPECQ_TRACE_POINT(19, j);
           const bool need = named_barrier_or(2, 256, xmax > kLazyMaxLog2);
           if (t == 0) SPECQ_TRACE_POINT(22, j);
           if (!need) break;
@@ -765,7 +760,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       ++issued;
       if (!is_v) SPECQ_TRACE_POINT(51, j);
-      if (++s == n_stages) {
+      if (++s == kAttnStages) {
         s = 0;
         phase ^= 1u;
       }
@@ -773,8 +768,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // the TMA copies of an abandoned loop land before the CTA exits: wait (bounded) for the
     // stages this warp armed
     if (!ok) {
-      for (int jj = max(0, issued - n_stages); jj < issued; ++jj)
-        (void)mbar_wait(&stage_full[jj % n_stages], static_cast<uint32_t>(jj / n_stages) & 1u, status,
+      for (int jj = max(0, issued - kAttnStages); jj < issued; ++jj)
+        (void)mbar_wait(&stage_full[jj % kAttnStages], static_cast<uint32_t>(jj / kAttnStages) & 1u, status,
                         SPECQ_STATUS_TIMEOUT_PIPELINE);
     }
   } else if (warp == kAttnMmaWarp) {
@@ -784,7 +779,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // V^T (A) and P (B) both MN-major
       const uint32_t id_pv = idesc_f16(128, static_cast<uint32_t>(NQ), 1u, 1u);
       const uint32_t id_l = idesc_f16(128, static_cast<uint32_t>(NQ), 0u, 1u);
-      const uint32_t ring_a = smem_u32(ring), qop_a = smem_u32(qop), pop_a = smem_u32(pop);
+      const uint32_t ring_a = smem_u32(ring), vop_a = smem_u32(vop), qop_a = smem_u32(qop), pop_a = smem_u32(pop);
       // B of the bias MMA: K-major, no swizzle, both K core matrices (128 B apart) in bias_s and
       // every 8-row group at the same address (stride 0): 256 bytes serve any N
       const uint64_t bias_desc = sdesc_plain(smem_u32(bias_s), 128u, 0u);
@@ -794,7 +789,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // so its per-block instruction count is kept small).
       const uint64_t kdesc0 = sdesc_sw128(ring_a, 16u, 1024u);
       const uint64_t qdesc0 = sdesc_sw128(qop_a, 16u, 1024u);
-      const uint64_t vdesc0 = sdesc_sw128(ring_a, 16384u, 1024u);   // the fp16 V tile of a stage
+      const uint64_t vdesc0 = sdesc_sw128(vop_a, 16384u, 1024u);
       const uint64_t pdesc0 = sdesc_sw128(pop_a, 16384u, 1024u);
       // score buffer sb <- the bias in all 2*NQ hi / lo columns (one MMA, accumulate off); the
       // QK MMAs issued after it by this thread accumulate onto it
@@ -804,7 +799,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       int qk_stage = 0;
       uint32_t qk_phase = 0;
       auto next_stage = [&]() {
-        if (++qk_stage == n_stages) {
+        if (++qk_stage == kAttnStages) {
           qk_stage = 0;
           qk_phase ^= 1u;
         }
@@ -828,9 +823,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int k = 0; k < 4; ++k)   // 32 of the 128 head dims (32 bytes) per step
           umma_i8_ss(tmem + sb * cs2, kd + 2u * k, qdesc0 + 2u * k, id_qk, 1u);
         umma_commit(&s_full[sb]);
+        umma_commit(&stage_empty[qk_stage]);   // the K tile is consumed
         next_stage();
       }
-      int pv_stage = 0;   // ring stage of block i (its fp16 V tile)
       for (int i = 0; ok && i < nblk; ++i) {
         const uint32_t bi = static_cast<uint32_t>(i & 1);   // P / V buffer of block i = score buffer of i + 2
         const uint32_t par = static_cast<uint32_t>(i >> 1) & 1u;
@@ -841,7 +836,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (!ok) break;
         tc_fence_after();
         SPECQ_TRACE_POINT(32, i);
-        const uint64_t vd = vdesc0 + ((static_cast<uint32_t>(pv_stage) * kAttnStage) >> 4);
+        const uint64_t vd = vdesc0 + ((bi * kAttnOp) >> 4);
         const uint64_t pd = pdesc0 + ((bi * kAttnPTile) >> 4);
         const uint64_t kd = kdesc0 + ((static_cast<uint32_t>(qk_stage) * kAttnStage) >> 4);
         if (more) reset_scores(bi);
@@ -855,12 +850,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         if (more) {
           umma_commit(&s_full[bi]);   // QK(i+2) and, before it, PV(i)
+          umma_commit(&stage_empty[qk_stage]);
           next_stage();
         } else {
           umma_commit(&pv_done[bi]);
         }
-        umma_commit(&stage_empty[pv_stage]);   // K(i) and V(i) consumed: the stage may be refilled
-        if (++pv_stage == n_stages) pv_stage = 0;
         SPECQ_TRACE_POINT(33, i);
       }
     }
@@ -880,13 +874,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int j = 0; j < nblk; ++j) {
       const int slot2 = slot == 0 ? 2 : slot - 1;   // (j + 2) % 3
       const int pg2 = scale_page(j + 2, vrow_s);      // fetched after this block's conversion
-      const int s = j % n_stages;
+      const int s = j % kAttnStages;
       const uint32_t sb = static_cast<uint32_t>(j & 1);
-      ok = ok && mbar_wait_sleep(&stage_full[s], static_cast<uint32_t>(j / n_stages) & 1u, 64u, status,
+      ok = ok && mbar_wait_sleep(&stage_full[s], static_cast<uint32_t>(j / kAttnStages) & 1u, 64u, status,
                                  SPECQ_STATUS_TIMEOUT_PIPELINE);
       if (c == 0) SPECQ_TRACE_POINT(40, j);
-      uint8_t* stage = ring + s * kAttnStage;
-      const uint8_t* vrow = stage + kAttnKV8 + c * 128;
+      const uint8_t* vrow = ring + s * kAttnStage + kAttnKV8 + c * 128;
       uint4 raw[8];
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch)
@@ -895,11 +888,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // the token's V scale in fp16 (exact for fp16 scales; one rounding for fp32 scales), so
       // the per-element multiply stays on the fp16 pipe
       const __half2 s2 = __half2half2(__float2half_rn(read_scale(vsd + 128 * slot, vsel, slot)));
-      // every V row of the stage is in registers, and QK(j) has read the K half: the stage may
-      // be overwritten.  QK(j-2) was seen complete two blocks ago and QK(j+2) cannot complete
-      // before V(j) is released, so the parity wait observes QK(j) itself.
-      named_barrier_sync(4, 32 * kAttnConvWarps);
-      ok = ok && mbar_wait_sleep(&s_full[sb], static_cast<uint32_t>(j >> 1) & 1u, 64u, status, SPECQ_STATUS_TIMEOUT_MMA);
+      // V buffer sb is free once PV(j-2) has completed
+      if (j >= 2) ok = ok && wait_pv(j - 2, SPECQ_STATUS_TIMEOUT_MMA);
+      uint8_t* vdst = vop + sb * kAttnOp;
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {
         uint32_t h[8];
@@ -909,11 +900,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           __half2 o = __hmul2(*reinterpret_cast<__half2*>(&h[i]), s2);
           h[i] = *reinterpret_cast<uint32_t*>(&o);
         }
-        store_f16_chunk_pair(stage, c, ch, h);
+        store_f16_chunk_pair(vdst, c, ch, h);
       }
       fence_proxy_async_smem();
+      // Blocks 0 and 1: see QK(j) complete before releasing V(j).  QK(j + 2) cannot complete
+      // before V(j) is released, so the parity waits in wait_pv(j) two blocks later find
+      // s_full[j & 1] one phase ahead at most (costs nothing: PV(j) follows QK(j) anyway).
+      if (j < 2) ok = ok && mbar_wait(&s_full[j], 0u, status, SPECQ_STATUS_TIMEOUT_MMA);
       __syncwarp();
-      if (lane == 0) mbar_arrive(&v_full[sb]);
+      if (lane == 0) {
+        mbar_arrive(&v_full[sb]);
+        mbar_arrive(&stage_empty[s]);   // the V half of the stage is consumed
+      }
       if (c == 0) SPECQ_TRACE_POINT(45, j);
       fetch_scale(p.vs, j + 2, vrow_s, pg2, vsd + 128 * slot2, vsel, slot2);
       slot = slot == 2 ? 0 : slot + 1;
@@ -1160,6 +1158,7 @@ inline int run_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_
   // one wave.  Splits of fewer than 512 tokens are not made.
   const int by_heads = H_KV >= 8 ? 2 : (H_KV >= 2 ? 4 : 8);
   p.splits = std::min(8, next_pow2(std::max({1, ceil_div(max_ctx, 2048), std::min(by_heads, ceil_div(max_ctx, 512))})));
+  p.stages = kAttnStages;
   p.sm_scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
   // TMEM: two score buffers (hi and lo int32 columns), O^T, normaliser, 16 columns of constant
   // A operands (fp16 ones for the normaliser, fp16 1024.0 for the bias MMA)
@@ -1175,13 +1174,12 @@ inline int run_paged_attention(const void* q, int64_t q_sb, int64_t q_st, int64_
       return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: block table of %d pages per context split", tchunk_max / page);
   }
 
-  // int8 Q (hi, lo) + two P tiles + softmax state + scale rings + block table + barriers; the
-  // K/V ring takes the rest (up to kAttnMaxStages stages)
-  const int fixed = 1024 + p.nq * 256 + 2 * static_cast<int>(kAttnPTile) + 4096 +
-                    (3 * 256 + 3 * 128 + attn_bias_words(p.nq)) * 4 + kAttnMaxPages * 4 + (2 * kAttnMaxStages + 17) * 8 + 16;
-  p.stages = std::min(kAttnMaxStages, (232448 - fixed) / static_cast<int>(kAttnStage));
-  if (p.stages < 3) return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: %d ring stages do not fit", p.stages);
-  const int smem = fixed + p.stages * static_cast<int>(kAttnStage);
+  // K ring + two fp16 V tiles + int8 Q (hi, lo) + two P tiles + softmax state + barriers
+  const int smem = 1024 + p.stages * static_cast<int>(kAttnStage) + 2 * static_cast<int>(kAttnOp) +
+                   p.nq * 256 + 2 * static_cast<int>(kAttnPTile) + 4096 + (3 * 256 + 3 * 128 + attn_bias_words(p.nq)) * 4 +
+                   kAttnMaxPages * 4 +
+                   (2 * p.stages + 17) * 8 + 16;
+  if (smem > 232448) return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: shared memory %d too large", smem);
   if ((p.nq * 128 + 3 * p.splits * p.nq) * 4 > p.stages * static_cast<int>(kAttnStage))
     return fail(SPECQ_ERR_UNSUPPORTED, "paged_attention: combine buffer does not fit");
 
