@@ -86,8 +86,14 @@ int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int
   p.m_rows = M; p.N = N; p.K = K;
 
   // One token chunk per CTA up to kW8A8MaxChunk tokens (past 256 rows: a multiple of 32, so a
-  // whole chunk arrives in two TMA boxes of chunk / 2 rows).
-  const int n_chunks = ceil_div(M, kW8A8MaxChunk);
+  // whole chunk arrives in two TMA boxes of chunk / 2 rows) for plan-buffer grids -- the same
+  // grid and split-K as eager calls at the small active M a graph mostly serves -- and for
+  // shapes with at least one channel tile per SM.  Eager calls of narrower shapes keep chunks
+  // of at most 256 tokens: two chunks of 144 at M = 288 halve the split-K partials that the
+  // cluster reduces (measured: o_proj 4096 x 4096 at M = 288 runs 11.5 us vs 17.7 us).
+  // Int32 accumulation is exact, so the chunking never changes the bits.
+  const int max_chunk = (plan != nullptr || ceil_div(N, 128) >= dev->sm_count) ? kW8A8MaxChunk : 256;
+  const int n_chunks = ceil_div(M, max_chunk);
   p.chunk = round_up(ceil_div(M, n_chunks), 16);
   if (p.chunk > 256) p.chunk = round_up(p.chunk, 32);
   p.chunk_box = p.chunk > 256 ? p.chunk / 2 : p.chunk;
@@ -107,29 +113,10 @@ int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int
   p.splits = S;
   p.kb_per_split = ceil_div(p.kb_total, S);
 
-  // TMA needs 16-byte aligned bases and row strides; otherwise use the register-staged loader.
-  const bool tma_ok = aligned(a, 16) && aligned(w, 16) && (lda % 16 == 0) && (ldw % 16 == 0);
-  // The split's whole activation slice (its K-blocks x the chunk's rows) in one TMA copy before
-  // the main loop, when it is small: the stages then carry only weight tiles, one copy each.
-  const uint32_t a_slice = static_cast<uint32_t>(p.kb_per_split) * static_cast<uint32_t>(p.chunk) * 128u;
-  p.a_once = (tma_ok && p.chunk <= 256 && K % 128 == 0 && a_slice <= 96u * 1024u) ? 1 : 0;
-  CUtensorMap tw;
-  W8A8ActMaps ta;
-  memset(&tw, 0, sizeof(tw));
-  memset(&ta, 0, sizeof(ta));
-  if (p.a_once) {   // [K-block][row][128 B]: dims (128, M, K / 128), strides (lda, 128); else per stage
-    const uint64_t d3[3] = {128u, static_cast<uint64_t>(M), static_cast<uint64_t>(p.kb_total)};
-    const uint64_t s3[2] = {static_cast<uint64_t>(lda), 128u};
-    const uint32_t b3[3] = {128u, static_cast<uint32_t>(p.chunk), static_cast<uint32_t>(p.kb_per_split)};
-    if (encode_tiled(&ta.once, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, a, d3, s3, b3, CU_TENSOR_MAP_SWIZZLE_128B) != SPECQ_OK)
-      p.a_once = 0;
-  }
-  p.a_region_bytes = p.a_once ? a_slice : 0u;
-  p.stage_bytes = kW8A8WTile + (p.a_once ? 0u : static_cast<uint32_t>(round_up(p.chunk, 16)) * 128u);
+  p.stage_bytes = kW8A8WTile + static_cast<uint32_t>(round_up(p.chunk, 16)) * 128u;
   // split-K partial tile [128][chunk] int32 (padded rows), parked in the idle ring
   const uint32_t red_bytes = (S > 1) ? 128u * (static_cast<uint32_t>(round_up(p.chunk, 16)) * 4u + 16u) : 0u;
-  // alignment slack, barriers, staged scales (and the activation slice)
-  const int overhead = 1024 + 256 + (kW8A8MaxChunk + 128) * 4 + static_cast<int>(p.a_region_bytes);
+  const int overhead = 1024 + 256 + (kW8A8MaxChunk + 128) * 4;   // alignment slack, barriers, staged scales
   int stages = std::min(8, (kSmemLimit - overhead) / static_cast<int>(p.stage_bytes));
   if (stages < 2) return fail(SPECQ_ERR_UNSUPPORTED, "w8a8: token chunk %d does not fit shared memory", p.chunk);
   while (static_cast<uint32_t>(stages) * p.stage_bytes < red_bytes && stages < 8) ++stages;
@@ -139,6 +126,12 @@ int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int
   if (smem > kSmemLimit) return fail(SPECQ_ERR_UNSUPPORTED, "w8a8: shared memory %d > limit", smem);
   p.tmem_cols = static_cast<uint32_t>(std::max(32, next_pow2(p.chunk)));
 
+  // TMA needs 16-byte aligned bases and row strides; otherwise use the register-staged loader.
+  const bool tma_ok = aligned(a, 16) && aligned(w, 16) && (lda % 16 == 0) && (ldw % 16 == 0);
+  CUtensorMap tw;
+  W8A8ActMaps ta;
+  memset(&tw, 0, sizeof(tw));
+  memset(&ta, 0, sizeof(ta));
   int vec = 0;
   if (tma_ok) {
     const uint64_t dw[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
@@ -269,7 +262,8 @@ int run_w4a16(const void* a, int64_t lda, const uint8_t* wp, int64_t ldwp, const
     while (ws < 16 && static_cast<uint32_t>(ws * kW4A16PackTile + xs * p.stage_bytes) < red_bytes &&
            fixed + (ws + 1) * static_cast<int>(kW4A16PackTile) + xs * static_cast<int>(p.stage_bytes) <= kSmemLimit)
       ++ws;
-    if (ws >= 2 && static_cast<uint32_t>(ws * kW4A16PackTile + xs * p.stage_bytes) >= red_bytes) {
+    // >= 4 weight stages: the dequant groups' parity waits on a stage rely on it (w4a16.cuh)
+    if (ws >= 4 && static_cast<uint32_t>(ws * kW4A16PackTile + xs * p.stage_bytes) >= red_bytes) {
       p.stages = ws;
       p.xstages = xs;
       smem = fixed + ws * static_cast<int>(kW4A16PackTile) + xs * static_cast<int>(p.stage_bytes);

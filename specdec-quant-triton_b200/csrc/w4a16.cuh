@@ -213,7 +213,8 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
       int s = 0;
       uint32_t ph = 0;
       for (int i = 0; i < nkb; ++i) {
-        if (!mbar_wait(&empty[s], ph ^ 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
+        // (a sleeping wait: the 16-stage ring hides its wake-up, the dequant warps need the slots)
+        if (!mbar_wait_sleep(&empty[s], ph ^ 1u, 128u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
         SPECQ_TRACE_POINT(2, i);
         mbar_arrive_expect_tx(&full[s], kW4A16PackTile);
         tma_load_2d(ring + s * kW4A16PackTile, &tmap_wp, &full[s], kblock(i) * 64, n0, pol_w);   // 64B-swizzled rows
@@ -237,7 +238,7 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
       int s = 0;
       uint32_t ph = 0;
       for (int i = 0; i < nkb; ++i) {
-        if (!mbar_wait(&xempty[s], ph ^ 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
+        if (!mbar_wait_sleep(&xempty[s], ph ^ 1u, 128u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
         uint8_t* alo = xring + s * p.stage_bytes;
         uint8_t* ahi = alo + a_bytes;
         const int kb = kblock(i);
@@ -271,14 +272,17 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
       // This thread shares its scheduler with four busy dequant warps, so its loop is kept
       // short: ring indices and phases by counters (no divisions), operand descriptors by
       // adding address offsets (in 16-byte units) to one precomputed descriptor.
-      // One wait per K-block: the dequant group's afull arrival comes after one of its warps
-      // has seen the activation tile land (xfull), so afull covers both operands.
+      // Two waits per K-block, both in block order: the dequantised A slot (afull) and the
+      // activation tile (xfull).  This thread is the only consumer that waits on xfull, and it
+      // consumed the stage's previous tile before the producer could reissue it, so the parity
+      // wait can neither alias a phase behind nor two ahead.
       const uint32_t idesc = idesc_f16(128, n_pad);
       const uint64_t xdesc0 = sdesc_sw128(smem_u32(xring), 16u, 1024u);
       int s = 0, d = 0;
       uint32_t xph = 0, aph = 0;
       for (int i = 0; i < nkb; ++i) {
-        if (!mbar_wait(&afull[d], aph, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) {
+        if (!mbar_wait_sleep(&afull[d], aph, 32u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE) ||
+            !mbar_wait(&xfull[s], xph, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) {
           *abort_flag = 1;
           break;
         }
@@ -344,13 +348,14 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
     // i % aslots = grp (the host sizes aslots == kW4A16Groups), its phase flips every turn.
     int s = grp % p.stages;
     uint32_t wph = static_cast<uint32_t>(grp / p.stages) & 1u;
-    int xs = grp % p.xstages;                                       // activation stage of block i
-    uint32_t xph = static_cast<uint32_t>(grp / p.xstages) & 1u;
     const int d = grp;
     uint32_t aph = 0;
+    // The A slot first: once the MMA has consumed block i - 4 (this group's previous block),
+    // every block <= i - 4 has landed, so with >= 4 weight stages (host-enforced) the previous
+    // tile of stage s has completed its phase and the parity wait on full[s] cannot alias it.
     for (int i = grp; i < nkb; i += kW4A16Groups) {
-      if (!mbar_wait(&full[s], wph, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE) ||
-          !mbar_wait(&aempty[d], aph ^ 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) {
+      if (!mbar_wait(&aempty[d], aph ^ 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE) ||
+          !mbar_wait(&full[s], wph, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) {
         *abort_flag = 1;
         break;
       }
@@ -385,15 +390,11 @@ __global__ void __launch_bounds__(kW4A16Threads, 1)
       }
       tmem_wait_st();
       tc_fence_before();
-      // the group's quadrant-0 warp also waits for block i's activation tile (loaded far ahead,
-      // so this rarely waits): the MMA thread then needs the afull wait alone
-      if (quad == 0 && !mbar_wait(&xfull[xs], xph, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) *abort_flag = 1;
       __syncwarp();
       if (lane == 0) mbar_arrive(&afull[d]);
       if (td == 0) SPECQ_TRACE_POINT(11, i);
       aph ^= 1u;
       for (s += kW4A16Groups; s >= p.stages; s -= p.stages) wph ^= 1u;
-      for (xs += kW4A16Groups; xs >= p.xstages; xs -= p.xstages) xph ^= 1u;
     }
   }
   __syncwarp();

@@ -10,8 +10,9 @@
 //     32 x 9) for its 128 channels in TMEM -- two MMAs per K step past 256 tokens, the
 //     instruction's N limit -- so the weights are streamed from HBM once whatever
 //     M = B*(k+1) is: there is no M-tile staircase (the reference re-streams the weights for
-//     every BLOCK_M rows), and a plan-buffer graph sized for M = 288 has the same grid and
-//     split-K as an eager call at any smaller M.
+//     every BLOCK_M rows).  A plan-buffer graph sized for M = 288 then has the same grid and
+//     split-K as an eager call at any smaller M; eager calls of narrow shapes (fewer channel
+//     tiles than SMs) keep chunks of at most 256 tokens, whose split-K partials are smaller.
 //   * TMA loads 128-byte-swizzled [128 x 128 B] weight tiles and the token chunk's activations
 //     (one box of the whole chunk, or 16-row boxes for a ragged last chunk) into a multi-stage
 //     mbarrier ring; one elected thread issues tcgen05.mma kind::i8 (M=128, N=tokens rounded
@@ -53,8 +54,6 @@ struct W8A8Params {
   int splits;          // cluster size along grid.x
   int stages;          // pipeline depth
   uint32_t stage_bytes;   // of the launch's largest token chunk
-  int a_once;             // the split's whole activation slice arrives in one TMA box before the loop
-  uint32_t a_region_bytes;   // its shared-memory region: kb_per_split x chunk rows x 128 B
   uint32_t ring_bytes;    // stages * stage_bytes: the ring, re-cut at run time for the active chunk
   uint32_t tmem_cols;
 };
@@ -70,7 +69,6 @@ constexpr int kW8A8MaxChunk = 288;          // tokens per CTA: 256 + 32 in a sec
 struct W8A8ActMaps {
   CUtensorMap rows[4];   // 16, 32, 64, 128 rows x 128 bytes
   CUtensorMap chunk;     // chunk_box rows x 128 bytes
-  CUtensorMap once;      // 3-D view [K-block][row][128 B]: one box = a split's K-blocks x chunk rows
 };
 
 // VEC = 0: TMA producer; VEC in {16, 8, 4, 2, 1}: register-staged loads of that width.
@@ -82,14 +80,12 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
   SPECQ_TRACE_INIT();
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;
-  uint8_t* a_region = smem + p.ring_bytes;                    // a_once: [K-block][chunk rows][128 B]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(a_region + p.a_region_bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.ring_bytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + kW8A8MaxStages;
   uint64_t* acc_full = bars + 2 * kW8A8MaxStages;
   uint64_t* red_full = acc_full + 1;                          // split-K: the peers' rows landed
-  uint64_t* a_full = red_full + 1;                            // a_once: the activation slice landed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kW8A8MaxStages + 3);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kW8A8MaxStages + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* sa_s = reinterpret_cast<float*>(tmem_slot + 4);      // [kW8A8MaxChunk] token scales of this chunk
   float* sw_s = sa_s + kW8A8MaxChunk;                         // [128] channel scales of this tile
@@ -135,8 +131,7 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
   // The ring is cut for the ACTIVE chunk: under a plan-buffer graph the launch is sized for
   // the largest M, and a smaller active M then gets more, smaller stages (more weight bytes
   // in flight) from the same shared memory.
-  const bool a_once = VEC == 0 && p.a_once;
-  const uint32_t stage_bytes = kW8A8WTile + (a_once ? 0u : a_bytes);   // a multiple of 2048: TMA-aligned stages
+  const uint32_t stage_bytes = kW8A8WTile + a_bytes;   // a multiple of 2048: TMA-aligned stages
   const int stages = min(kW8A8MaxStages, static_cast<int>(p.ring_bytes / stage_bytes));
   if (threadIdx.x == 0) SPECQ_TRACE_POINT(0, 0);
 
@@ -148,7 +143,6 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
     }
     mbar_init(acc_full, 1u);
     mbar_init(red_full, 1u);
-    mbar_init(a_full, 1u);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -156,7 +150,6 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
     tma_prefetch_desc(&tmap_w);
     for (int i = 0; i < 4; ++i) tma_prefetch_desc(&tmap_a.rows[i]);
     tma_prefetch_desc(&tmap_a.chunk);
-    if (p.a_once) tma_prefetch_desc(&tmap_a.once);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, p.tmem_cols);
@@ -176,20 +169,15 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
       int issued = 0;
       int s = 0;
       uint32_t ph = 0;
-      if (a_once) {   // the split's K-blocks x the chunk's rows in one copy (TMA issue is serial)
-        mbar_arrive_expect_tx(a_full, p.a_region_bytes);
-        tma_load_3d(a_region, &tmap_a.once, a_full, 0, m0, kb0, pol_a);
-      }
       for (int i = 0; i < nkb; ++i) {
         if (!mbar_wait(&empty[s], ph ^ 1u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
         SPECQ_TRACE_POINT(2, i);
         uint8_t* wt = ring + s * stage_bytes;
         uint8_t* at = wt + kW8A8WTile;
-        mbar_arrive_expect_tx(&full[s], kW8A8WTile + (a_once ? 0u : a_bytes));
+        mbar_arrive_expect_tx(&full[s], kW8A8WTile + a_bytes);
         const int kx = kblock(i) * 128;
         tma_load_2d(wt, &tmap_w, &full[s], kx, n0, pol_w);
-        if (a_once) {
-        } else if (a_rows == p.chunk) {   // a whole chunk: one box, or two past 256 rows (TMA issue is serial)
+        if (a_rows == p.chunk) {   // a whole chunk: one box, or two past 256 rows (TMA issue is serial)
           for (int r = 0; r < a_rows; r += p.chunk_box) tma_load_2d(at + r * 128, &tmap_a.chunk, &full[s], kx, m0 + r, pol_a);
         } else {   // a ragged chunk (the last one, or the active rows of a plan-graph launch)
           int r = 0;
@@ -207,7 +195,6 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
         for (int i = max(0, issued - stages); i < issued; ++i)
           mbar_wait(&full[i % stages], static_cast<uint32_t>(i / stages) & 1u, p.status,
                     SPECQ_STATUS_TIMEOUT_PIPELINE);
-        if (a_once) mbar_wait(a_full, 0u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE);
       }
     }
   } else if (warp == 1) {
@@ -219,19 +206,14 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
       const uint32_t idesc_hi = idesc_i8(128, n_hi > 0u ? n_hi : 16u);
       // descriptors advanced by address offsets in 16-byte units; ring index by a counter
       const uint64_t wdesc0 = sdesc_sw128(smem_u32(ring), 16u, 1024u);
-      const uint64_t adesc_once = sdesc_sw128(smem_u32(a_region), 16u, 1024u);
-      const uint32_t a_tile_16 = (static_cast<uint32_t>(p.chunk) * 128u) >> 4;   // one K-block of the slice
       int s = 0;
       uint32_t ph = 0;
-      bool a_ok = !a_once || mbar_wait_sleep(a_full, 0u, 32u, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE);
-      if (!a_ok) *abort_flag = 1;
-      for (int i = 0; a_ok && i < nkb; ++i) {
+      for (int i = 0; i < nkb; ++i) {
         if (!mbar_wait(&full[s], ph, p.status, SPECQ_STATUS_TIMEOUT_PIPELINE)) { *abort_flag = 1; break; }
         tc_fence_after();
         SPECQ_TRACE_POINT(3, i);
         const uint64_t wd = wdesc0 + ((static_cast<uint32_t>(s) * stage_bytes) >> 4);
-        const uint64_t ad = a_once ? adesc_once + static_cast<uint32_t>(kblock(i) - kb0) * a_tile_16
-                                   : wd + (kW8A8WTile >> 4);
+        const uint64_t ad = wd + (kW8A8WTile >> 4);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {   // 32 K bytes per step
           umma_i8_ss(tmem_acc, wd + 2u * k, ad + 2u * k, idesc, (i > 0 || k > 0) ? 1u : 0u);

@@ -134,16 +134,36 @@ def test_plan_value_out_of_range_is_clamped_and_flagged(cuda):
     assert specq.get_status(clear=True) & 0x100
 
 
-@pytest.mark.parametrize("M,chunks", [(257, 1), (272, 1), (288, 1), (289, 2), (600, 3)])
-def test_token_chunks_past_one_mma(cuda, M, chunks):
-    """Up to 288 tokens (32 sequences x 9) share one CTA per channel tile: past 256 the second
-    MMA of each K step covers tokens 256.. at TMEM column 256.  More tokens take more chunks."""
+@pytest.mark.parametrize("M,chunks", [(257, 2), (288, 2), (289, 2), (600, 3)])
+def test_token_chunks_eager(cuda, M, chunks):
+    """Eager calls of a narrow shape (fewer channel tiles than SMs) split the tokens into chunks
+    of at most 256 (smaller split-K partials); every split gives the exact int32 sums."""
     import specq
     a, sa, w, sw = _inputs(M, 384, 768, M)
     out, ck = specq.w8a8_matmul(a.cuda(), sa.cuda(), w.cuda(), sw.cuda())
     torch.cuda.synchronize()
     assert ck.grid[1] == chunks      # grid = (split, token chunk, channel tile)
     assert np.array_equal(_bits(out), O.w8a8_ref(a.numpy(), sa.numpy(), w.numpy(), sw.numpy()).view(np.uint16))
+
+
+def test_plan_grid_of_288_tokens_is_one_chunk(cuda):
+    """A plan-buffer grid sized for 288 tokens (32 sequences x 9) keeps them in one CTA per
+    channel tile: past 256 tokens a second MMA per K step covers tokens 256.. at TMEM column
+    256.  Checked against the oracle at active M on both sides of 256."""
+    import specq
+    MMAX, N, K = 288, 384, 768
+    a, sa, w, sw = _inputs(MMAX, N, K, 31)
+    ad, sad, wd, swd = a.cuda(), sa.cuda(), w.cuda(), sw.cuda()
+    plan = torch.zeros(8, dtype=torch.int32, device="cuda")
+    for M in (288, 272, 257, 256, 40):
+        plan[0] = M
+        out = torch.full((MMAX, N), 7.0, dtype=torch.float16, device="cuda")
+        _, ck = specq.w8a8_matmul(ad, sad, wd, swd, out=out, plan=plan, grid_m_max=MMAX)
+        torch.cuda.synchronize()
+        assert ck.grid[1] == 1
+        ref = O.w8a8_ref(a[:M].numpy(), sa[:M].numpy(), w.numpy(), sw.numpy())
+        assert np.array_equal(_bits(out[:M]), ref.view(np.uint16)), M
+        assert bool((out[M:] == 7.0).all())
 
 
 def test_strided_and_transposed_outputs(cuda):
