@@ -570,7 +570,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // block, it measured faster than after the P pass)
       fetch_scale(p.ks, j + 2, krow, pg2, ksd + 256 * slot2, ksel, slot2);
       // S(j) is ready; its commit also covers PV(j-2), so P buffer sb is free as well
-      if (t == 0) SPECQ_TRACE_POINT(23, j);
       ok = ok && mbar_wait(&s_full[sb], par2, status, SPECQ_STATUS_TIMEOUT_MMA);
       tc_fence_after();
       if (t == 0) SPECQ_TRACE_POINT(21, j);
@@ -590,11 +589,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
         for (int c0 = 0; c0 < NQH; c0 += 16) {   // 16 columns per TMEM round trip (hi and lo)
           constexpr int kW = 16;
-          // columns past the valid query rows (CTA-uniform) are padding: their P and O^T columns
-          // are never used (every output column of an MMA depends on its own column only)
-          if (col0 + c0 >= rows_valid) break;
           uint32_t rh[kW], rl[kW];
-          const bool two = c0 + 8 < NQH && col0 + c0 + 8 < rows_valid;
+          const bool two = c0 + 8 < NQH;
           tmem_ld8(s_addr + c0, *reinterpret_cast<uint32_t(*)[8]>(rh));
           tmem_ld8(s_addr + NQ + c0, *reinterpret_cast<uint32_t(*)[8]>(rl));
           if (two) {
@@ -744,7 +740,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     uint32_t phase = 0;
     int issued = 0;
     for (int j = 0; j < nblk; ++j) {
-      if (!mbar_wait_sleep(&stage_empty[s], phase ^ 1u, 128u, status, SPECQ_STATUS_TIMEOUT_PIPELINE)) {
+      if (!mbar_wait(&stage_empty[s], phase ^ 1u, status, SPECQ_STATUS_TIMEOUT_PIPELINE)) {
         ok = false;
         break;
       }
@@ -830,9 +826,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t bi = static_cast<uint32_t>(i & 1);   // P / V buffer of block i = score buffer of i + 2
         const uint32_t par = static_cast<uint32_t>(i >> 1) & 1u;
         const bool more = i + 2 < nblk;
-        ok = mbar_wait_sleep(&p_full[bi], par, 32u, status, SPECQ_STATUS_TIMEOUT_MMA) &&
-             mbar_wait_sleep(&v_full[bi], par, 32u, status, SPECQ_STATUS_TIMEOUT_PIPELINE) &&
-             (!more || mbar_wait_sleep(&stage_full[qk_stage], qk_phase, 32u, status, SPECQ_STATUS_TIMEOUT_PIPELINE));
+        ok = mbar_wait(&p_full[bi], par, status, SPECQ_STATUS_TIMEOUT_MMA) &&
+             mbar_wait(&v_full[bi], par, status, SPECQ_STATUS_TIMEOUT_PIPELINE) &&
+             (!more || mbar_wait(&stage_full[qk_stage], qk_phase, status, SPECQ_STATUS_TIMEOUT_PIPELINE));
         if (!ok) break;
         tc_fence_after();
         SPECQ_TRACE_POINT(32, i);
@@ -876,8 +872,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const int pg2 = scale_page(j + 2, vrow_s);      // fetched after this block's conversion
       const int s = j % kAttnStages;
       const uint32_t sb = static_cast<uint32_t>(j & 1);
-      ok = ok && mbar_wait_sleep(&stage_full[s], static_cast<uint32_t>(j / kAttnStages) & 1u, 64u, status,
-                                 SPECQ_STATUS_TIMEOUT_PIPELINE);
+      ok = ok && mbar_wait(&stage_full[s], static_cast<uint32_t>(j / kAttnStages) & 1u, status,
+                           SPECQ_STATUS_TIMEOUT_PIPELINE);
       if (c == 0) SPECQ_TRACE_POINT(40, j);
       const uint8_t* vrow = ring + s * kAttnStage + kAttnKV8 + c * 128;
       uint4 raw[8];

@@ -146,10 +146,15 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 0 && VEC == 0 && lane == 0) {
+  if (warp == 0 && VEC == 0 && lane == 0) {   // only the maps this CTA's copies use
     tma_prefetch_desc(&tmap_w);
-    for (int i = 0; i < 4; ++i) tma_prefetch_desc(&tmap_a.rows[i]);
-    tma_prefetch_desc(&tmap_a.chunk);
+    if (a_rows == p.chunk) {
+      tma_prefetch_desc(&tmap_a.chunk);
+    } else {
+      if (a_rows >= 128) tma_prefetch_desc(&tmap_a.rows[3]);
+      for (int b = 0; b < 3; ++b)
+        if (a_rows & (16 << b)) tma_prefetch_desc(&tmap_a.rows[b]);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, p.tmem_cols);
@@ -214,11 +219,16 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
         SPECQ_TRACE_POINT(3, i);
         const uint64_t wd = wdesc0 + ((static_cast<uint32_t>(s) * stage_bytes) >> 4);
         const uint64_t ad = wd + (kW8A8WTile >> 4);
+        if (n_hi == 0u) {   // (two loops: a branch per instruction measured slower)
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {   // 32 K bytes per step
-          umma_i8_ss(tmem_acc, wd + 2u * k, ad + 2u * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
-          if (n_hi > 0u)   // token rows 256.. start 256 * 128 bytes into the activation tile
+          for (int k = 0; k < 4; ++k)   // 32 K bytes per step
+            umma_i8_ss(tmem_acc, wd + 2u * k, ad + 2u * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+        } else {   // token rows 256.. start 256 * 128 bytes into the activation tile
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            umma_i8_ss(tmem_acc, wd + 2u * k, ad + 2u * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
             umma_i8_ss(tmem_acc + 256u, wd + 2u * k, ad + 2048u + 2u * k, idesc_hi, (i > 0 || k > 0) ? 1u : 0u);
+          }
         }
         umma_commit(&empty[s]);   // stage is free once these MMAs have read it
         SPECQ_TRACE_POINT(4, i);
@@ -269,8 +279,7 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
   const int row = static_cast<int>(quad * 32 + lane);   // channel within the tile
   bool ok = true;
   if (epi) {
-    // (the whole main loop long: a sleeping wait leaves the issue slots to the producer and MMA)
-    ok = mbar_wait_sleep(acc_full, 0u, 32u, p.status, SPECQ_STATUS_TIMEOUT_MMA) && (*abort_flag == 0);
+    ok = mbar_wait(acc_full, 0u, p.status, SPECQ_STATUS_TIMEOUT_MMA) && (*abort_flag == 0);
     tc_fence_after();
     named_barrier_sync(1, 128);   // every epilogue thread's staged scales are visible
     if (warp == 2 && lane == 0) SPECQ_TRACE_POINT(5, 0);
