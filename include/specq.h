@@ -42,6 +42,7 @@ extern "C" {
 #define SPECQ_STATUS_TIMEOUT_PIPELINE 0x01 /* a producer/consumer mbarrier wait ran out            */
 #define SPECQ_STATUS_TIMEOUT_MMA 0x02      /* waiting for tensor-core completion ran out           */
 #define SPECQ_STATUS_TIMEOUT_TEST 0x04     /* specq_selftest_wait_timeout's deliberate wait         */
+#define SPECQ_STATUS_TIMEOUT_PEER 0x08     /* a peer GPU's exchange signal did not arrive in time   */
 #define SPECQ_STATUS_PLAN_CLAMPED 0x100    /* a plan value was outside [0, max] and was clamped     */
 
 /* ---- dtypes for scale tensors ----------------------------------------------------------- */
@@ -194,6 +195,25 @@ int specq_selftest_wait_timeout(uint64_t limit_ns, void* stream);
  */
 int specq_mma_peak(int kind, int n, int a_mn_major, int b_mn_major, int a_tmem, int busy_warps, int busy_iters,
                    int iters, int ctas, uint32_t* sink, void* stream);
+
+/*
+ * All-gather of row blocks over NVLink for tensor parallelism.  No reference counterpart (the
+ * reference runs on one GPU): it is the exchange step of the tensor-parallel verification stack.
+ * Rank `rank` of `world` (1..8) copies its block src [rows x row_bytes] (row stride ld_src
+ * bytes) into byte columns [dst_off, dst_off + row_bytes) of EVERY rank's full buffer dst[q]
+ * (row stride ld_dst bytes; memory that every rank can write, e.g. symmetric memory), signals
+ * each peer q through flags[q][rank], and waits until flags[rank][q] shows that every peer's
+ * block has landed (bounded: after 1 s it records SPECQ_STATUS_TIMEOUT_PEER and returns).
+ * dst and flags are HOST arrays of `world` device pointers; flags[q] is rank q's uint32 [world]
+ * flag array of this exchange and `state` this rank's device uint32 [2], both zero before the
+ * first call.  Every rank must issue the same sequence of calls on each exchange.
+ * max_out (optional): one float per rank and row (row_bytes = 4, ld_dst = 4 * world,
+ * dst_off = 4 * rank); after the wait max_out[m] = the maximum over the ranks of row m.
+ * plan (optional): plan[0] = the active rows (rows is the maximum).
+ */
+int specq_peer_gather(const void* src, int64_t ld_src, int row_bytes, const int32_t* plan, int rows,
+                      void* const* dst, int64_t ld_dst, int64_t dst_off, uint32_t* const* flags, uint32_t* state,
+                      float* max_out, int rank, int world, void* stream);
 
 /*
  * Pipeline tracing (builds compiled with -DSPECQ_TRACE only; other builds return

@@ -11,6 +11,7 @@
 #include "paged_attn.cuh"
 #include "rowops.cuh"
 #include "mma_peak.cuh"
+#include "peer_gather.cuh"
 
 namespace specq {
 
@@ -505,6 +506,14 @@ int specq_mma_peak(int kind, int n, int a_mn_major, int b_mn_major, int a_tmem, 
   r.threads = threads;
   r.dyn_smem = kPeakSmem;
   return SPECQ_OK;
+}
+
+int specq_peer_gather(const void* src, int64_t ld_src, int row_bytes, const int32_t* plan, int rows,
+                      void* const* dst, int64_t ld_dst, int64_t dst_off, uint32_t* const* flags, uint32_t* state,
+                      float* max_out, int rank, int world, void* stream) {
+  last_launch_ref() = LaunchRecord();
+  return run_peer_gather(src, ld_src, row_bytes, plan, rows, dst, ld_dst, dst_off, flags, state, max_out, rank,
+                         world, stream);
 }
 
 int specq_selftest_wait_timeout(uint64_t limit_ns, void* stream) {

@@ -22,6 +22,7 @@ SPECQ_ERR_NO_DEVICE = 4
 SPECQ_STATUS_TIMEOUT_PIPELINE = 0x01
 SPECQ_STATUS_TIMEOUT_MMA = 0x02
 SPECQ_STATUS_TIMEOUT_TEST = 0x04
+SPECQ_STATUS_TIMEOUT_PEER = 0x08
 SPECQ_STATUS_PLAN_CLAMPED = 0x100
 
 SPECQ_DTYPE_F16 = 0
@@ -49,6 +50,7 @@ SIGNATURES = {
     "specq_get_status": (_i32, [_pi32, _i32]),
     "specq_selftest_wait_timeout": (_i32, [_u64, _vp]),
     "specq_mma_peak": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
+    "specq_peer_gather": (_i32, [_vp, _i64, _i32, _vp, _i32, _vp, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _vp]),
     "specq_trace_configure": (_i32, [_vp, _i32]),
 }
 

@@ -8,21 +8,25 @@ Rank r of g holds (survey config 4 extended to g GPUs):
   gu    gate and up channels with matching ranges, so silu(gate) * up stays local;
   down  output channels [r hid/g, (r+1) hid/g).
 
-The residual stream h is replicated.  Per layer the ranks exchange, by NCCL all-gather over
-NVLink, the attention output (fp16), the o-projection output (fp16), the quantised MLP
-activation (int8) and the down-projection output (fp16), plus one all-reduce (MAX) of the MLP
-activation's per-token amax, so every rank quantises its slice with the whole row's scale.
+The residual stream h is replicated.  Per layer the ranks all-gather the attention output
+(fp16), the o-projection output (fp16), the quantised MLP activation (int8) and the
+down-projection output (fp16), plus one all-reduce (MAX) of the MLP activation's per-token
+amax, so every rank quantises its slice with the whole row's scale.  With exchange="peer" (the
+command line's default) each of these is one `specq_peer_gather` launch that stores the rank's
+block over NVLink straight into every rank's symmetric full buffer (specq/peer.py); with
+exchange="nccl" they are NCCL collectives followed by a re-layout copy.
 Every kernel computes each output column exactly as the single-GPU stack does (W8A8 sums in
 int32 whatever the column split), so the tensor-parallel residual stream equals the single-GPU
 one bit for bit whenever the attention splits each context the same way on both (the split
 count follows the context length and the KV heads a GPU holds; at the stack's 1024-token
 contexts it is 2 on one GPU and on a 2-way shard).
 
-Under the plan graph the collectives move the maximum grid's rows (a graph fixes their sizes);
-eager steps move the active rows.
+Under the plan graph the NCCL collectives move the maximum grid's rows (a graph fixes their
+sizes) while the peer-store kernel reads the active rows from the plan buffer; eager steps move
+the active rows.
 
     python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 \\
-        -m specq.stack_tp [--layers 4] [--steps 200] [--check]
+        -m specq.stack_tp [--layers 4] [--steps 200] [--exchange peer|nccl] [--check]
 """
 from __future__ import annotations
 
@@ -72,8 +76,10 @@ def gathered_to_rows(buf: torch.Tensor, world: int, rows: int, out: torch.Tensor
 
 class StackTP:
     def __init__(self, world, rank, layers=4, hid=4096, ff=14336, heads=32, kv_heads=8, head_dim=128, ctx=1024,
-                 b_max=32, ks=(0, 2, 4, 8), page=16, seed=0, device="cuda", group=None):
-        self.g, self.r, self.group = world, rank, group
+                 b_max=32, ks=(0, 2, 4, 8), page=16, seed=0, device="cuda", group=None, exchange="nccl"):
+        if exchange not in ("nccl", "peer"):
+            raise ValueError(f"exchange {exchange!r}: 'nccl' or 'peer'")
+        self.g, self.r, self.group, self.exchange = world, rank, group, exchange
         self.L, self.hid, self.ff, self.H, self.H_KV, self.D = layers, hid, ff, heads, kv_heads, head_dim
         self.b_max, self.ks = b_max, tuple(ks)
         self.ql_max = max(ks) + 1
@@ -104,6 +110,16 @@ class StackTP:
         self.down_l, self.down = mk(M, hid // g), mk(M, hid)
         self.bufs = {n: torch.empty(g * t.numel(), dtype=t.dtype, device=device).view(g * M, t.shape[1])
                      for n, t in (("attn", self.attn_l), ("o", self.o_l), ("f8", self.f8_l), ("down", self.down_l))}
+        if exchange == "peer":
+            # the gathered rows land in symmetric full buffers written by every rank's kernel
+            from .peer import PeerExchange
+            self.px = PeerExchange(group)
+            self.attn = self.px.add("attn", M, self.Hl * D, torch.float16)
+            self.o = self.px.add("o", M, hid // g, torch.float16)
+            self.f8 = self.px.add("f8", M, ff // g, torch.int8)
+            self.down = self.px.add("down", M, hid // g, torch.float16)
+            self.px.add("amax", M, 1, torch.float32)
+            self.bufs = {}
         self.plan = torch.zeros(4, dtype=torch.int32, device=device)
         self.plan_host = torch.zeros(1024, 4, dtype=torch.int32).pin_memory()
         self._slot = 0
@@ -128,10 +144,19 @@ class StackTP:
         h[0], h[1], h[2] = B * ql, B, ql
         self.plan.copy_(h, non_blocking=True)
 
-    def _gather(self, name, local, full, rows):
+    def _gather(self, name, local, full, rows, plan=None):
+        if self.exchange == "peer":
+            self.px.gather(name, local, rows, plan=plan)   # lands in `full` (the symmetric buffer)
+            return
         buf = self.bufs[name]
         dist.all_gather_into_tensor(buf[: self.g * rows], local[:rows], group=self.group)
         gathered_to_rows(buf, self.g, rows, full)
+
+    def _amax_all_ranks(self, rows, plan=None):
+        if self.exchange == "peer":
+            self.px.all_max("amax", self.amax, self.amax, rows, plan=plan)
+        else:
+            dist.all_reduce(self.amax[:rows], op=dist.ReduceOp.MAX, group=self.group)
 
     # ---- one verification pass ----------------------------------------------------------------
     def step(self, B, ql, use_plan=False):
@@ -156,20 +181,20 @@ class StackTP:
                           ql_max=qlg)
             ops.paged_attention_packed(self.qkv, 0, self.attn_l, kc, vc, ks, vs, bt[:Bg], cl[:Bg], ql, Hl, B=Bg,
                                        ql_max=qlg, QPP=self.ql_max, plan=pa)
-            self._gather("attn", self.attn_l, self.attn, M)
+            self._gather("attn", self.attn_l, self.attn, M, pl)
             ops.quant_rows(self.attn[rows], q=self.x8[rows], s=self.sx[rows], plan=pl)
             ops.w8a8_matmul(self.x8[rows], self.sx[rows], *lw["o"], out=self.o_l[rows], **gm)
-            self._gather("o", self.o_l, self.o, M)
+            self._gather("o", self.o_l, self.o, M, pl)
             ops.quant_rows(self.o[rows], mode=ops.QUANT_RESIDUAL, residual=self.h[rows], q=self.x8[rows],
                            s=self.sx[rows], plan=pl)
             ops.w8a8_matmul(self.x8[rows], self.sx[rows], *lw["gu"], out=self.gu_l[rows], **gm)
             ops.quant_rows(self.gu_l[rows], mode=ops.QUANT_SILU_MUL, amax_out=self.amax[rows], plan=pl)
-            dist.all_reduce(self.amax[rows], op=dist.ReduceOp.MAX, group=self.group)
+            self._amax_all_ranks(M, pl)
             ops.quant_rows(self.gu_l[rows], mode=ops.QUANT_SILU_MUL, q=self.f8_l[rows], s=self.sf[rows], plan=pl,
                            amax_in=self.amax[rows])
-            self._gather("f8", self.f8_l, self.f8, M)
+            self._gather("f8", self.f8_l, self.f8, M, pl)
             ops.w8a8_matmul(self.f8[rows], self.sf[rows], *lw["down"], out=self.down_l[rows], **gm)
-            self._gather("down", self.down_l, self.down, M)
+            self._gather("down", self.down_l, self.down, M, pl)
         ops.quant_rows(self.down[rows], mode=ops.QUANT_RESIDUAL, residual=self.h[rows], q=self.x8[rows],
                        s=self.sx[rows], plan=pl)
 
@@ -191,17 +216,17 @@ def _max_over_ranks(x: float, group=None) -> float:
     return float(t.item())
 
 
-def run(world, rank, layers=4, steps=200, b_max=32, ks=(0, 2, 4, 8), ctx=1024, seed=0, check=False):
+def run(world, rank, layers=4, steps=200, b_max=32, ks=(0, 2, 4, 8), ctx=1024, seed=0, check=False, exchange="nccl"):
     """Eager and plan-graph latency of the tensor-parallel stack over a seeded (B, k) trace;
     times are device times (CUDA events) per step, the max over ranks.  check: rank 0 also runs
     the single-GPU stack and reports the largest difference of the residual streams."""
-    st = StackTP(world, rank, layers=layers, b_max=b_max, ks=ks, ctx=ctx, seed=seed)
+    st = StackTP(world, rank, layers=layers, b_max=b_max, ks=ks, ctx=ctx, seed=seed, exchange=exchange)
     st.snapshot()
     ql_max = st.ql_max
     rng = random.Random(seed)
     trace = [(rng.randint(1, b_max), rng.choice(ks)) for _ in range(steps)]
     res = {"config": dict(world=world, layers=layers, b_max=b_max, ks=list(ks), ctx=ctx, m_max=st.m_max,
-                          steps=steps, parallelism=f"tp{world}")}
+                          steps=steps, parallelism=f"tp{world}", exchange=exchange)}
     for B, k in sorted(set(trace))[:4]:
         st.step(B, k + 1)
     torch.cuda.synchronize()
@@ -264,6 +289,8 @@ def main():
     ap.add_argument("--ctx", type=int, default=1024)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--check", action="store_true", help="compare with the single-GPU stack on rank 0")
+    ap.add_argument("--exchange", choices=("nccl", "peer"), default="peer",
+                    help="all-gathers by NCCL or by the library's peer-store kernel")
     args = ap.parse_args()
     rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -271,7 +298,8 @@ def main():
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     try:
         res = run(world, rank, layers=args.layers, steps=args.steps, b_max=args.b_max,
-                  ks=tuple(int(k) for k in args.ks.split(",")), ctx=args.ctx, seed=args.seed, check=args.check)
+                  ks=tuple(int(k) for k in args.ks.split(",")), ctx=args.ctx, seed=args.seed, check=args.check,
+                  exchange=args.exchange)
         if rank == 0:
             print(json.dumps(res), flush=True)
     finally:

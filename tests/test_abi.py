@@ -75,6 +75,27 @@ def test_invalid_shapes_rejected_on_host():
     assert rc == _lib.SPECQ_ERR_INVALID_ARG
 
 
+def test_peer_gather_arguments_rejected_on_host():
+    from specq import _lib
+    lib = _lib.load()
+    ptrs = (C.c_void_p * 2)(16, 32)
+    ok = dict(src=16, ld_src=64, row_bytes=64, plan=None, rows=4, dst=ptrs, ld_dst=128, dst_off=0, flags=ptrs,
+              state=16, max_out=None, rank=0, world=2, stream=None)
+
+    def call(**kw):
+        a = dict(ok, **kw)
+        return lib.specq_peer_gather(a["src"], a["ld_src"], a["row_bytes"], a["plan"], a["rows"], a["dst"],
+                                     a["ld_dst"], a["dst_off"], a["flags"], a["state"], a["max_out"], a["rank"],
+                                     a["world"], a["stream"])
+
+    assert call(world=9) == _lib.SPECQ_ERR_INVALID_ARG          # more ranks than the kernel holds
+    assert call(rank=2) == _lib.SPECQ_ERR_INVALID_ARG
+    assert call(row_bytes=6) == _lib.SPECQ_ERR_INVALID_ARG      # not a multiple of 4
+    assert call(dst_off=96) == _lib.SPECQ_ERR_INVALID_ARG       # block past the full row
+    assert call(state=None) == _lib.SPECQ_ERR_INVALID_ARG
+    assert call(max_out=16) == _lib.SPECQ_ERR_INVALID_ARG       # max mode takes one float per rank
+
+
 def test_python_wrappers_reject_cpu_tensors():
     import specq
     a = torch.zeros(4, 128, dtype=torch.int8)

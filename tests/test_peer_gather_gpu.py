@@ -1,0 +1,85 @@
+"""specq_peer_gather on one GPU: the copy into every rank's full buffer, the epoch protocol and
+the max reduction, with the peer's side emulated by buffers on the same GPU whose signal is
+set before the launch (one launch, nothing waits on another launch), and the bounded wait
+running out when no peer ever signals (status bit, no hang).  The two-rank exchange over
+NVLink is covered by test_stack_tp_gpu.py."""
+import ctypes as C
+
+import pytest
+import torch
+
+from specq import _lib
+
+pytestmark = pytest.mark.gpu
+
+
+def _call(src, rows, dsts, ld_dst, dst_off, flags, state, rank, world, plan=None, max_out=None):
+    lib = _lib.load()
+    esz = src.element_size()
+    _lib.check(lib.specq_peer_gather(
+        src.data_ptr(), src.stride(0) * esz, src.shape[1] * esz, None if plan is None else plan.data_ptr(), rows,
+        (C.c_void_p * world)(*[d.data_ptr() for d in dsts]), ld_dst, dst_off,
+        (C.c_void_p * world)(*[f.data_ptr() for f in flags]), state.data_ptr(),
+        None if max_out is None else max_out.data_ptr(), rank, world, torch.cuda.current_stream().cuda_stream))
+
+
+def test_single_rank_copy_and_plan_rows(cuda):
+    g = torch.Generator(device="cuda").manual_seed(0)
+    for dtype, n in ((torch.float16, 2048), (torch.int8, 7168), (torch.float16, 6)):
+        src = torch.randint(-100, 100, (40, n), generator=g, device="cuda").to(dtype)
+        full = torch.full((40, n), 7, dtype=dtype, device="cuda")
+        flags = torch.zeros(1, dtype=torch.int32, device="cuda")
+        state = torch.zeros(2, dtype=torch.int32, device="cuda")
+        plan = torch.tensor([29], dtype=torch.int32, device="cuda")
+        _call(src, 40, [full], full.stride(0) * full.element_size(), 0, [flags], state, 0, 1, plan=plan)
+        torch.cuda.synchronize()
+        assert torch.equal(full[:29], src[:29])
+        assert (full[29:] == 7).all()                      # rows past the plan's are not touched
+        assert state.tolist() == [1, 0]                    # one epoch, arrivals reset
+    assert _lib.get_status() == 0
+
+
+def test_two_rank_emulation_copy_signal_and_max(cuda):
+    g = torch.Generator(device="cuda").manual_seed(1)
+    rows, n, world = 24, 512, 2
+    src = torch.randn(rows, n, generator=g, device="cuda").half()
+    full = [torch.zeros(rows, world * n, dtype=torch.float16, device="cuda") for _ in range(world)]
+    flags = [torch.zeros(world, dtype=torch.int32, device="cuda") for _ in range(world)]
+    flags[0][1] = 1           # rank 1's signal for epoch 1 is already there
+    state = torch.zeros(2, dtype=torch.int32, device="cuda")
+    ld = full[0].stride(0) * 2
+    # rank 0 writes columns [0, n) of both full buffers and signals flags[1][0]
+    _call(src, rows, full, ld, 0, flags, state, 0, world)
+    torch.cuda.synchronize()
+    for f in full:
+        assert torch.equal(f[:, :n], src)
+        assert (f[:, n:] == 0).all()
+    assert flags[1].tolist() == [1, 0] and state.tolist() == [1, 0]
+    # max mode: rank 0's amax column against a pre-filled peer column
+    a0 = torch.rand(rows, generator=g, device="cuda")
+    fm = [torch.zeros(rows, world, dtype=torch.float32, device="cuda") for _ in range(world)]
+    fm[0][:, 1] = torch.rand(rows, generator=g, device="cuda")
+    fl = [torch.zeros(world, dtype=torch.int32, device="cuda") for _ in range(world)]
+    fl[0][1] = 1
+    st = torch.zeros(2, dtype=torch.int32, device="cuda")
+    out = torch.zeros(rows, dtype=torch.float32, device="cuda")
+    _call(a0.view(-1, 1), rows, fm, 4 * world, 0, fl, st, 0, world, max_out=out)
+    torch.cuda.synchronize()
+    assert torch.equal(out, torch.maximum(a0, fm[0][:, 1]))
+    assert torch.equal(fm[1][:, 0], a0)
+    assert _lib.get_status() == 0
+
+
+def test_missing_peer_signal_times_out_with_status(cuda):
+    rows, n, world = 8, 64, 2
+    src = torch.ones(rows, n, dtype=torch.float16, device="cuda")
+    full = [torch.zeros(rows, world * n, dtype=torch.float16, device="cuda") for _ in range(world)]
+    flags = [torch.zeros(world, dtype=torch.int32, device="cuda") for _ in range(world)]   # nobody signals
+    state = torch.zeros(2, dtype=torch.int32, device="cuda")
+    _lib.get_status()
+    _call(src, rows, full, full[0].stride(0) * 2, 0, flags, state, 0, world)
+    torch.cuda.synchronize()                               # returns after the 1 s limit
+    assert _lib.get_status() & _lib.SPECQ_STATUS_TIMEOUT_PEER
+    assert torch.equal(full[0][:, :n], src)
+    torch.zeros(1, device="cuda").add_(1)                  # the context is still usable
+    torch.cuda.synchronize()
