@@ -10,15 +10,17 @@
 // kernel completes, this rank's full buffer holds all blocks and the next kernel on the stream
 // can read it.
 //
-// Protocol (per exchange buffer, one epoch per launch; every rank launches the same sequence):
+// Protocol (per exchange buffer; every rank launches the same sequence with the same grid):
 //   1. the CTAs copy the block with 16-byte (or 4-byte) loads and peer stores;
-//   2. each thread fences at system scope, then each CTA counts itself in on a local counter;
-//   3. the last CTA advances the epoch, release-stores it into flag[rank] of every peer's flag
-//      array, and polls its own flag array (acquire, system scope) until every peer's entry has
-//      reached the epoch -- a bounded wait (1 s) that records SPECQ_STATUS_TIMEOUT_PEER and
-//      returns instead of hanging;
-//   4. in max mode (the per-token amax of row-split activations) that CTA then reduces the
-//      gathered [rows, world] floats to their per-row maximum.
+//   2. once its threads are done (CTA barrier), each CTA adds 1 to flag[rank] of every peer's
+//      flag array with a release reduction at system scope (cumulative: it publishes the whole
+//      CTA's stores), so the flags count the CTAs that have landed, launch after launch;
+//   3. CTA 0 advances this rank's running total by the grid size and polls its own flag array
+//      (acquire, system scope) until every peer's count has reached that total -- a bounded
+//      wait (1 s) that records SPECQ_STATUS_TIMEOUT_PEER and returns instead of hanging; the
+//      kernel is complete once CTA 0 returns;
+//   4. in max mode (the per-token amax of row-split activations) CTA 0 then reduces the
+//      gathered [rows, world] floats to their per-row maximum (the grid is one CTA then).
 // A rank cannot overwrite a peer's full buffer while the peer still reads the previous contents:
 // the stack cycles through four exchange buffers per layer, and a rank reaches the next use of a
 // buffer only after later exchanges whose epochs show every peer has moved past its reads.
@@ -43,14 +45,14 @@ struct PeerGatherParams {
   int64_t ld_dst;                  // row stride of the full buffers, bytes
   int64_t dst_off;                 // byte offset of this rank's block in a full row
   uint32_t* flags[kPeerMaxWorld];  // every rank's flag array [world] for this exchange
-  uint32_t* state;                 // this rank's [2]: epoch, CTA arrivals (zero-initialised)
+  uint32_t* state;                 // this rank's [2]: running CTA total, unused (zero-initialised)
   float* max_out;                  // max mode: [rows] per-row maximum of the gathered floats
   int rank, world;
   int* status;
 };
 
-__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void red_release_sys_add_u32(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
   uint32_t v;
@@ -59,8 +61,8 @@ __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
 }
 
 __global__ void __launch_bounds__(kPeerThreads) peer_gather_kernel(const __grid_constant__ PeerGatherParams p) {
-  __shared__ int last_cta;
-  pdl_wait();   // the block was written by the previous kernel on the stream
+  pdl_launch_dependents();   // the next kernel may begin launching (it waits for this grid)
+  pdl_wait();                // the block was written by the previous kernel on the stream
   int rows = p.rows;
   if (p.plan != nullptr) {
     const int pm = __ldg(p.plan);
@@ -84,25 +86,21 @@ __global__ void __launch_bounds__(kPeerThreads) peer_gather_kernel(const __grid_
       for (int q = 0; q < p.world; ++q) *reinterpret_cast<uint32_t*>(p.dst[q] + o) = v;
     }
   }
-  // 2. every thread's stores are visible system-wide before its CTA counts itself in
-  __threadfence_system();
+  // 2. the CTA's stores are done (barrier); one release reduction per peer publishes them
   __syncthreads();
-  if (threadIdx.x == 0) last_cta = (atomicAdd(&p.state[1], 1u) == gridDim.x - 1) ? 1 : 0;
-  __syncthreads();
-  if (!last_cta) return;
-  // 3. the last CTA: every CTA's stores precede its arrival, so they precede the signals
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    const uint32_t epoch = p.state[0] + 1u;
-    p.state[0] = epoch;
-    p.state[1] = 0u;
+  if (threadIdx.x == 0)
     for (int q = 0; q < p.world; ++q)
-      if (q != p.rank) st_release_sys_u32(p.flags[q] + p.rank, epoch);
+      if (q != p.rank) red_release_sys_add_u32(p.flags[q] + p.rank, 1u);
+  if (blockIdx.x != 0) return;
+  // 3. CTA 0: wait until every peer's CTAs of this launch have landed here
+  if (threadIdx.x == 0) {
+    const uint32_t landed = p.state[0] + gridDim.x;   // peer CTAs landed here, all launches
+    p.state[0] = landed;
     const uint64_t t0 = globaltimer_ns();
     bool timed_out = false;
     for (int q = 0; q < p.world && !timed_out; ++q) {
       if (q == p.rank) continue;
-      while (static_cast<int32_t>(ld_acquire_sys_u32(p.flags[p.rank] + q) - epoch) < 0) {
+      while (static_cast<int32_t>(ld_acquire_sys_u32(p.flags[p.rank] + q) - landed) < 0) {
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
           report_status(p.status, SPECQ_STATUS_TIMEOUT_PEER);
           timed_out = true;
@@ -165,8 +163,11 @@ inline int run_peer_gather(const void* src, int64_t ld_src, int row_bytes, const
   p.world = world;
   p.status = dev->status;
   const int64_t units = static_cast<int64_t>(rows) * (row_bytes / (v16 ? 16 : 4));
-  // about four units per thread, at most one CTA per SM
-  const int ctas = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(dev->sm_count, (units + 4 * kPeerThreads - 1) / (4 * kPeerThreads))));
+  // about four units per thread, at most one CTA per SM; one CTA in max mode (CTA 0 reduces
+  // the rows, its own column included, after the wait).  The grid depends on the call's
+  // arguments only, so every rank launches the same grid.
+  const int ctas = max_out != nullptr ? 1 : static_cast<int>(std::max<int64_t>(
+      1, std::min<int64_t>(dev->sm_count, (units + 4 * kPeerThreads - 1) / (4 * kPeerThreads))));
   SPECQ_CUDA_TRY(launch_plain(peer_gather_kernel, dim3(ctas), dim3(kPeerThreads), static_cast<cudaStream_t>(stream), p));
   SPECQ_CUDA_TRY(cudaGetLastError());
   return SPECQ_OK;

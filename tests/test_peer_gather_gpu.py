@@ -35,7 +35,7 @@ def test_single_rank_copy_and_plan_rows(cuda):
         torch.cuda.synchronize()
         assert torch.equal(full[:29], src[:29])
         assert (full[29:] == 7).all()                      # rows past the plan's are not touched
-        assert state.tolist() == [1, 0]                    # one epoch, arrivals reset
+        assert state[0].item() >= 1 and state[1].item() == 0   # the launch's CTAs counted
     assert _lib.get_status() == 0
 
 
@@ -45,7 +45,7 @@ def test_two_rank_emulation_copy_signal_and_max(cuda):
     src = torch.randn(rows, n, generator=g, device="cuda").half()
     full = [torch.zeros(rows, world * n, dtype=torch.float16, device="cuda") for _ in range(world)]
     flags = [torch.zeros(world, dtype=torch.int32, device="cuda") for _ in range(world)]
-    flags[0][1] = 1           # rank 1's signal for epoch 1 is already there
+    flags[0][1] = 1 << 20     # rank 1's CTAs have all signalled already
     state = torch.zeros(2, dtype=torch.int32, device="cuda")
     ld = full[0].stride(0) * 2
     # rank 0 writes columns [0, n) of both full buffers and signals flags[1][0]
@@ -54,13 +54,14 @@ def test_two_rank_emulation_copy_signal_and_max(cuda):
     for f in full:
         assert torch.equal(f[:, :n], src)
         assert (f[:, n:] == 0).all()
-    assert flags[1].tolist() == [1, 0] and state.tolist() == [1, 0]
+    # one release-add per CTA of rank 0 in rank 1's flag array; rank 0's running total matches
+    assert flags[1][1].item() == 0 and flags[1][0].item() == state[0].item() >= 1
     # max mode: rank 0's amax column against a pre-filled peer column
     a0 = torch.rand(rows, generator=g, device="cuda")
     fm = [torch.zeros(rows, world, dtype=torch.float32, device="cuda") for _ in range(world)]
     fm[0][:, 1] = torch.rand(rows, generator=g, device="cuda")
     fl = [torch.zeros(world, dtype=torch.int32, device="cuda") for _ in range(world)]
-    fl[0][1] = 1
+    fl[0][1] = 1 << 20
     st = torch.zeros(2, dtype=torch.int32, device="cuda")
     out = torch.zeros(rows, dtype=torch.float32, device="cuda")
     _call(a0.view(-1, 1), rows, fm, 4 * world, 0, fl, st, 0, world, max_out=out)
