@@ -476,23 +476,40 @@ def run_ours(args):
     # e2e: public API, pinned host inputs, H2D + 3 calls + D2H every step.  The step's three
     # calls are independent, so each runs as its own chain (H2D of its inputs -> call -> D2H of
     # its output) on its own stream, as a serving loop would issue them: one call's copies
-    # overlap another's kernel.
-    x = inputs[0]
+    # overlap another's kernel.  A call's inputs are staged in one pinned host block and land
+    # with one copy in one device block whose views are the tensors the call takes.
+    x = dict(inputs[0])
     chains = [(("a8", "sa"), "w8a8", "o8"), (("a4",), "w4a16", "o4"), (("q",), "paged_attention", "oa")]
-    host_in = {k: x[k].cpu().pin_memory() for ins, _, _ in chains for k in ins}
+
+    def _stage(keys):
+        offs, tot = [], 0
+        for k in keys:
+            offs.append(tot)
+            tot += -(-x[k].numel() * x[k].element_size() // 256) * 256
+        dev_blk = torch.empty(tot, dtype=torch.uint8, device=dev)
+        host_blk = torch.empty(tot, dtype=torch.uint8).pin_memory()
+        for k, o in zip(keys, offs):
+            t = x[k].contiguous()
+            nb = t.numel() * t.element_size()
+            view = dev_blk[o:o + nb].view(t.dtype).view(t.shape)
+            view.copy_(t)
+            host_blk[o:o + nb].copy_(t.reshape(-1).view(torch.uint8).cpu())
+            x[k] = view
+        return host_blk, dev_blk
+
+    staged = [_stage(ins) for ins, _, _ in chains]
     host_out = {o: torch.empty(x[o].shape, dtype=x[o].dtype).pin_memory() for _, _, o in chains}
-    h2d = sum(t.numel() * t.element_size() for t in host_in.values())
+    h2d = sum(h.numel() for h, _ in staged)
     d2h = sum(t.numel() * t.element_size() for t in host_out.values())
     fns = _kernels(x)
     streams = [torch.cuda.Stream() for _ in chains]
 
     def e2e_step():
-        for st, (ins, name, o) in zip(streams, chains):
-            with torch.cuda.stream(st):
-                for k in ins:
-                    x[k].copy_(host_in[k], non_blocking=True)
-                fns[name]()
-                host_out[o].copy_(x[o], non_blocking=True)
+        for st, (hb, db), (_, name, o) in zip(streams, staged, chains):
+            torch.cuda.set_stream(st)
+            db.copy_(hb, non_blocking=True)
+            fns[name]()
+            host_out[o].copy_(x[o], non_blocking=True)
 
     def e2e_run(n):
         main = torch.cuda.current_stream()
@@ -500,6 +517,7 @@ def run_ours(args):
             st.wait_stream(main)
         for _ in range(n):
             e2e_step()
+        torch.cuda.set_stream(main)
         for st in streams:
             main.wait_stream(st)
 
@@ -562,8 +580,8 @@ def run_ours(args):
                              f"(3 launches each, programmatic dependent launch), after {warm_steps} warm-up steps "
                              "from a graph of their own; per-kernel: events around replays of captured chains "
                              f"of {chain_len} launches of that kernel over the copies",
-                   "e2e": "steps back to back; each call's chain (H2D of its inputs, the call, D2H of its "
-                          "output) on its own stream"},
+                   "e2e": "steps back to back; each call's chain (one H2D copy of its inputs staged in one "
+                          "pinned block, the call, D2H of its output) on its own stream"},
         "kernels": kern,
         "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": traffic,

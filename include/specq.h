@@ -171,6 +171,10 @@ int specq_kernel_info(int which, int variant, int* num_regs, int* local_bytes, i
 int specq_last_launch(int* variant, int* grid_x, int* grid_y, int* grid_z, int* cluster_x, int* threads,
                       int* dynamic_smem);
 
+/* The same record as one array: record[0..6] = variant, grid x, y, z, cluster x, threads,
+ * dynamic smem (one pointer argument: the Python wrappers read it after every call). */
+int specq_last_launch_packed(int* record);
+
 /* Read (and with clear != 0, reset) the status word of the current device. Synchronous. */
 int specq_get_status(int* status, int clear);
 

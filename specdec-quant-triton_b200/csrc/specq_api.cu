@@ -447,6 +447,19 @@ int specq_last_launch(int* variant, int* grid_x, int* grid_y, int* grid_z, int* 
   return SPECQ_OK;
 }
 
+int specq_last_launch_packed(int* record) {
+  if (record == nullptr) return fail(SPECQ_ERR_INVALID_ARG, "last_launch_packed: null record");
+  const LaunchRecord& r = last_launch_ref();
+  record[0] = r.variant;
+  record[1] = r.grid[0];
+  record[2] = r.grid[1];
+  record[3] = r.grid[2];
+  record[4] = r.cluster_x;
+  record[5] = r.threads;
+  record[6] = r.dyn_smem;
+  return SPECQ_OK;
+}
+
 int specq_get_status(int* status, int clear) {
   DeviceState* dev = nullptr;
   if (int rc = get_device_state(&dev)) return rc;

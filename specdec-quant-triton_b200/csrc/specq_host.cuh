@@ -128,9 +128,44 @@ inline PFN_encodeTiled get_encode_tiled() {
 
 // Encode a tiled tensor map of rank 2 to 4.  dims/strides_bytes/box are innermost first;
 // strides_bytes[i] is the byte stride of dimension i+1.
+// Tensor-map encoding is a driver call made several times per operator call; a map depends only
+// on its arguments (never on the data), so recently encoded maps are reused from a small
+// per-thread table keyed by every argument.
+struct TensorMapKey {
+  uint64_t words[17];
+  bool operator==(const TensorMapKey& o) const { return memcmp(words, o.words, sizeof(words)) == 0; }
+};
+
 inline int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
                         const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                         CUtensorMapSwizzle swizzle) {
+  if (rank < 1 || rank > 5) return fail(SPECQ_ERR_INVALID_ARG, "tensor map of rank %d", rank);
+  TensorMapKey key;
+  memset(&key, 0, sizeof(key));
+  key.words[0] = (static_cast<uint64_t>(dtype) << 32) | (static_cast<uint64_t>(swizzle) << 8) | static_cast<uint64_t>(rank);
+  key.words[1] = reinterpret_cast<uint64_t>(base);
+  for (int i = 0; i < rank; ++i) {
+    key.words[2 + i] = dims[i];
+    key.words[7 + i] = box[i];
+    if (i + 1 < rank) key.words[12 + i] = strides_bytes[i];
+  }
+  int dev = -1;
+  cudaGetDevice(&dev);
+  key.words[16] = static_cast<uint64_t>(static_cast<int64_t>(dev));
+  constexpr int kSlots = 64;
+  struct Entry {
+    TensorMapKey key;
+    CUtensorMap map;
+    bool valid;
+  };
+  static thread_local Entry cache[kSlots];
+  uint64_t h = 1469598103934665603ull;
+  for (uint64_t w : key.words) h = (h ^ w) * 1099511628211ull;
+  Entry& slot = cache[(h ^ (h >> 29)) % kSlots];
+  if (slot.valid && slot.key == key) {
+    *map = slot.map;
+    return SPECQ_OK;
+  }
   PFN_encodeTiled enc = get_encode_tiled();
   if (enc == nullptr) return fail(SPECQ_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   cuuint64_t d[5];
@@ -147,6 +182,9 @@ inline int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, c
                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(SPECQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+  slot.key = key;
+  slot.map = *map;
+  slot.valid = true;
   return SPECQ_OK;
 }
 

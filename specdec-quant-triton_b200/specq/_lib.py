@@ -47,6 +47,7 @@ SIGNATURES = {
     "specq_pack_int4": (_i32, [_vp, _i32, _i64, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _i64, _vp]),
     "specq_kernel_info": (_i32, [_i32, _i32, _pi32, _pi32, _pi32, _pi32, _pi32]),
     "specq_last_launch": (_i32, [_pi32, _pi32, _pi32, _pi32, _pi32, _pi32, _pi32]),
+    "specq_last_launch_packed": (_i32, [_vp]),
     "specq_get_status": (_i32, [_pi32, _i32]),
     "specq_selftest_wait_timeout": (_i32, [_u64, _vp]),
     "specq_mma_peak": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
@@ -69,6 +70,8 @@ class SpecqError(RuntimeError):
 def load():
     """Load libspecq.so once and declare every entry point's signature."""
     global _lib
+    if _lib is not None:   # loaded: no lock on the per-call path
+        return _lib
     with _lock:
         if _lib is None:
             if not os.path.exists(LIB_PATH):
@@ -104,13 +107,12 @@ _launch_buf = threading.local()
 
 def last_launch_raw() -> tuple:
     """(variant, grid x, y, z, cluster, threads, dynamic smem) of this thread's last launch, read
-    through buffers allocated once per thread (it runs after every operator call)."""
+    in one call into a buffer allocated once per thread (it runs after every operator call)."""
     b = getattr(_launch_buf, "b", None)
     if b is None:
-        arr = (C.c_int * 7)()
-        b = _launch_buf.b = (arr, [C.pointer(C.c_int.from_buffer(arr, 4 * i)) for i in range(7)])
-    load().specq_last_launch(*b[1])
-    return tuple(b[0])
+        b = _launch_buf.b = (C.c_int * 7)()
+    (_lib or load()).specq_last_launch_packed(b)
+    return tuple(b)
 
 
 def last_launch() -> dict:
