@@ -98,8 +98,13 @@ _w4a16_kernel = CompiledKernelRegistry("_w4a16_kernel")
 _paged_attn_kernel = CompiledKernelRegistry("_paged_attn_kernel")
 
 
-def _stream() -> int:
-    return torch.cuda.current_stream().cuda_stream
+if hasattr(torch._C, "_cuda_getCurrentRawStream") and hasattr(torch._C, "_cuda_getDevice"):
+    def _stream() -> int:
+        """The current stream's cudaStream_t (without building a Stream object: ~0.3 us, not ~3)."""
+        return torch._C._cuda_getCurrentRawStream(torch._C._cuda_getDevice())
+else:
+    def _stream() -> int:
+        return torch.cuda.current_stream().cuda_stream
 
 
 def _ptr(t):
