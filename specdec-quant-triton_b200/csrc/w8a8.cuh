@@ -104,7 +104,8 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
 
   // While the previous kernel on the stream finishes, warm L2 with this CTA's first weight
   // tiles (the first token chunk only: later chunks of the tile find them there).
-  if (VEC == 0 && threadIdx.x == 0 && blockIdx.y == 0) {
+  // (an epilogue warp issues them: thread 0 initialises the barriers meanwhile)
+  if (VEC == 0 && threadIdx.x == 64 && blockIdx.y == 0) {
     tma_prefetch_desc(&tmap_w);
     for (int i = 0; i < min(nkb, kW8A8MaxStages); ++i) tma_prefetch_l2_2d(&tmap_w, kblock(i) * 128, n0);
   }
