@@ -477,11 +477,12 @@ def run_ours(args):
     # calls are independent, so each runs as its own chain (H2D of its inputs -> call -> D2H of
     # its output) on its own stream, as a serving loop would issue them: one call's copies
     # overlap another's kernel.  A call's inputs are staged in one pinned host block and land
-    # with one copy in one device block whose views are the tensors the call takes.
-    x = dict(inputs[0])
+    # with one copy in one device block whose views are the tensors the call takes.  Consecutive
+    # steps alternate between two such sets of streams and buffers (double buffering), so one
+    # step's result copies overlap the next step's input copies and kernels.
     chains = [(("a8", "sa"), "w8a8", "o8"), (("a4",), "w4a16", "o4"), (("q",), "paged_attention", "oa")]
 
-    def _stage(keys):
+    def _stage(x, keys):
         offs, tot = [], 0
         for k in keys:
             offs.append(tot)
@@ -497,15 +498,22 @@ def run_ours(args):
             x[k] = view
         return host_blk, dev_blk
 
-    staged = [_stage(ins) for ins, _, _ in chains]
-    host_out = {o: torch.empty(x[o].shape, dtype=x[o].dtype).pin_memory() for _, _, o in chains}
-    h2d = sum(h.numel() for h, _ in staged)
-    d2h = sum(t.numel() * t.element_size() for t in host_out.values())
-    fns = _kernels(x)
-    streams = [torch.cuda.Stream() for _ in chains]
+    def _buffer_set():
+        x = dict(inputs[0])
+        for _, _, o in chains:
+            x[o] = torch.empty_like(x[o])
+        staged = [_stage(x, ins) for ins, _, _ in chains]
+        host_out = {o: torch.empty(x[o].shape, dtype=x[o].dtype).pin_memory() for _, _, o in chains}
+        return dict(x=x, staged=staged, host_out=host_out, fns=_kernels(x),
+                    streams=[torch.cuda.Stream() for _ in chains])
 
-    def e2e_step():
-        for st, (hb, db), (_, name, o) in zip(streams, staged, chains):
+    sets = [_buffer_set(), _buffer_set()]
+    h2d = sum(h.numel() for h, _ in sets[0]["staged"])
+    d2h = sum(t.numel() * t.element_size() for t in sets[0]["host_out"].values())
+
+    def e2e_step(bs):
+        x, fns, host_out = bs["x"], bs["fns"], bs["host_out"]
+        for st, (hb, db), (_, name, o) in zip(bs["streams"], bs["staged"], chains):
             torch.cuda.set_stream(st)
             db.copy_(hb, non_blocking=True)
             fns[name]()
@@ -513,13 +521,15 @@ def run_ours(args):
 
     def e2e_run(n):
         main = torch.cuda.current_stream()
-        for st in streams:
-            st.wait_stream(main)
-        for _ in range(n):
-            e2e_step()
+        for bs in sets:
+            for st in bs["streams"]:
+                st.wait_stream(main)
+        for i in range(n):
+            e2e_step(sets[i & 1])
         torch.cuda.set_stream(main)
-        for st in streams:
-            main.wait_stream(st)
+        for bs in sets:
+            for st in bs["streams"]:
+                main.wait_stream(st)
 
     e2e_run(max(3, args.warmup))
     torch.cuda.synchronize()
@@ -581,7 +591,8 @@ def run_ours(args):
                              "from a graph of their own; per-kernel: events around replays of captured chains "
                              f"of {chain_len} launches of that kernel over the copies",
                    "e2e": "steps back to back; each call's chain (one H2D copy of its inputs staged in one "
-                          "pinned block, the call, D2H of its output) on its own stream"},
+                          "pinned block, the call, D2H of its output) on its own stream; consecutive steps "
+                          "alternate between two sets of streams and buffers"},
         "kernels": kern,
         "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": traffic,
