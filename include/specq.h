@@ -220,6 +220,29 @@ int specq_peer_gather(const void* src, int64_t ld_src, int row_bytes, const int3
                       float* max_out, int rank, int world, void* stream);
 
 /*
+ * W8A8 GEMM with tensor-parallel output (no reference counterpart: the GEMM fused with the
+ * tensor-parallel stack's all-gather).  The same product as specq_w8a8; its fp16 output rows
+ * (unit column stride, row stride ldo) are stored into EVERY rank's full buffer over NVLink:
+ * `out` is a HOST array of `world` (1..8) device pointers, out[q] = rank q's full buffer at this
+ * rank's column block (out[rank] is this rank's own).  Once a CTA's stores are done it adds 1 to
+ * slot `rank` of every rank's flag array flags[q] (host array of device pointers to uint32
+ * [world], zero before the first call), its own included; the consumer waits with
+ * specq_quant_rows_peer.  Every rank launches the same grid (same shapes and plan).
+ */
+int specq_w8a8_peer(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int64_t ldw, const float* sw,
+                    void* const* out, int64_t ldo, const int32_t* plan, int M, int N, int K, uint32_t* const* flags,
+                    int rank, int world, void* stream);
+
+/*
+ * specq_quant_rows on a full buffer written by every rank's specq_w8a8_peer: each CTA first
+ * waits (bounded: 1 s, then SPECQ_STATUS_TIMEOUT_PEER and it goes on) until every rank's count
+ * in wait_flags (this rank's flag array of that exchange) has reached this rank's own count.
+ */
+int specq_quant_rows_peer(const void* x, int64_t ldx, void* r, int64_t ldr, int8_t* q, int64_t ldq, float* s,
+                          const int32_t* plan, const float* amax_in, float* amax_out, int M, int N, int mode,
+                          const uint32_t* wait_flags, int rank, int world, void* stream);
+
+/*
  * Pipeline tracing (builds compiled with -DSPECQ_TRACE only; other builds return
  * SPECQ_ERR_UNSUPPORTED): the CTA with linear index `cta` records SM-clock timestamps of its
  * pipeline events into `buffer` (device, 64 x 64 uint64: [event slot][iteration]).

@@ -51,15 +51,6 @@ struct PeerGatherParams {
   int* status;
 };
 
-__device__ __forceinline__ void red_release_sys_add_u32(uint32_t* p, uint32_t v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 __global__ void __launch_bounds__(kPeerThreads) peer_gather_kernel(const __grid_constant__ PeerGatherParams p) {
   pdl_launch_dependents();   // the next kernel may begin launching (it waits for this grid)
   pdl_wait();                // the block was written by the previous kernel on the stream

@@ -52,6 +52,10 @@ struct QuantRowsParams {
   int* status;
   int64_t ldx, ldr, ldq;
   int M, N, mode;
+  // optional tensor-parallel input: x is a full buffer that every rank's producer writes over
+  // NVLink; wait until every rank's count in this flag array has reached this rank's own
+  const uint32_t* wait_flags;
+  int wait_rank, wait_world;
 };
 
 // silu(g) = g * sigmoid(g) with the fast exponential and division intrinsics: the fused
@@ -74,6 +78,10 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_kernel(const __grid_co
     M = min(max(pm, 0), p.M);
   }
   if (row >= M) return;
+  if (p.wait_flags != nullptr) {
+    if (threadIdx.x == 0) (void)wait_peer_counts(p.wait_flags, p.wait_rank, p.wait_world, p.status);
+    __syncthreads();
+  }
   const __half* x = p.x + static_cast<int64_t>(row) * p.ldx;
   float y[PER];
   float amax = 0.f;
@@ -135,6 +143,10 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_vec_kernel(const __gri
     M = min(max(pm, 0), p.M);
   }
   if (row >= M) return;
+  if (p.wait_flags != nullptr) {
+    if (threadIdx.x == 0) (void)wait_peer_counts(p.wait_flags, p.wait_rank, p.wait_world, p.status);
+    __syncthreads();
+  }
   const __half* x = p.x + static_cast<int64_t>(row) * p.ldx;
   float y[CH][8];
   float amax = 0.f;
@@ -411,7 +423,9 @@ __global__ void __launch_bounds__(128) kv_append_kernel(const __grid_constant__ 
 
 inline int run_quant_rows(const void* x, int64_t ldx, void* r, int64_t ldr, int8_t* q, int64_t ldq, float* s,
                           const int32_t* plan, const float* amax_in, float* amax_out, int M, int N, int mode,
-                          void* stream) {
+                          void* stream, const uint32_t* wait_flags = nullptr, int wait_rank = 0, int wait_world = 0) {
+  if (wait_flags != nullptr && (wait_world < 1 || wait_world > 8 || wait_rank < 0 || wait_rank >= wait_world))
+    return fail(SPECQ_ERR_INVALID_ARG, "quant_rows: wait rank %d of world %d", wait_rank, wait_world);
   if (M < 0 || N <= 0) return fail(SPECQ_ERR_INVALID_ARG, "quant_rows: bad shape M=%d N=%d", M, N);
   if (mode < 0 || mode > 2) return fail(SPECQ_ERR_INVALID_ARG, "quant_rows: mode %d", mode);
   if (M == 0) return SPECQ_OK;
@@ -436,6 +450,9 @@ inline int run_quant_rows(const void* x, int64_t ldx, void* r, int64_t ldr, int8
   p.status = dev->status;
   p.ldx = ldx; p.ldr = ldr; p.ldq = ldq;
   p.M = M; p.N = N; p.mode = mode;
+  p.wait_flags = wait_flags;
+  p.wait_rank = wait_rank;
+  p.wait_world = wait_world;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool vec = N % 8 == 0 && aligned(x, 16) && ldx % 8 == 0 && aligned(q, 8) && ldq % 8 == 0 &&
                    (mode != 1 || (aligned(r, 16) && ldr % 8 == 0));

@@ -177,6 +177,35 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   }
 }
 
+// System-scope release reduction / acquire load on a word another GPU writes or reads over
+// NVLink (the tensor-parallel exchanges' counters).
+__device__ __forceinline__ void red_release_sys_add_u32(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait (one thread) until every other rank's count in `flags` (this rank's flag array of
+// an exchange, one slot per rank) has reached this rank's own count in slot `rank`: the peers'
+// producers have landed as many blocks here as this rank's producer did.
+__device__ __forceinline__ bool wait_peer_counts(const uint32_t* flags, int rank, int world, int* status) {
+  const uint32_t target = ld_acquire_sys_u32(flags + rank);
+  const uint64_t t0 = globaltimer_ns();
+  for (int q = 0; q < world; ++q) {
+    if (q == rank) continue;
+    while (static_cast<int32_t>(ld_acquire_sys_u32(flags + q) - target) < 0) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        report_status(status, SPECQ_STATUS_TIMEOUT_PEER);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
 // Bounded wait that sleeps between polls, for waiters whose wake-up latency a pipeline hides
 // (a producer waiting for a free stage, a converter or the MMA issuer waiting for its inputs):
 // a polling warp takes an issue slot on every try, a sleeping one leaves them to the warps

@@ -31,10 +31,10 @@ namespace {
 
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in per block on sm_100
 
-template <int VEC>
-int launch_w8a8_variant(const W8A8Params& p, const CUtensorMap& tw, const W8A8ActMaps& ta, dim3 grid, int smem,
-                        cudaStream_t stream) {
-  auto kern = w8a8_kernel<VEC>;
+template <int VEC, typename PeerT>
+int launch_w8a8_variant(const W8A8Params& p, const CUtensorMap& tw, const W8A8ActMaps& ta, const PeerT& peer,
+                        dim3 grid, int smem, cudaStream_t stream) {
+  auto kern = w8a8_kernel<VEC, PeerT>;
   SPECQ_CUDA_TRY(ensure_dyn_smem(reinterpret_cast<const void*>(kern), smem));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
@@ -43,7 +43,7 @@ int launch_w8a8_variant(const W8A8Params& p, const CUtensorMap& tw, const W8A8Ac
   cfg.stream = stream;
   LaunchAttrs attrs(p.splits);
   attrs.apply(cfg);
-  SPECQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p, tw, ta));
+  SPECQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p, tw, ta, peer));
   return SPECQ_OK;
 }
 
@@ -58,9 +58,17 @@ int w8a8_variant_id(int vec) {
   }
 }
 
+// Tensor-parallel output of the W8A8 epilogue (null: the plain output): every rank's output
+// block base (host array of `world` device pointers) and every rank's flag array.
+struct W8A8PeerArgs {
+  void* const* out;
+  uint32_t* const* flags;
+  int rank, world;
+};
+
 int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int64_t ldw, const float* sw,
              void* out, int64_t ldo, int64_t ldo_n, int32_t* acc, int64_t ldacc, const int32_t* plan, int M, int N,
-             int K, void* stream) {
+             int K, void* stream, const W8A8PeerArgs* peer = nullptr) {
   if (M < 0 || N <= 0 || K <= 0) return fail(SPECQ_ERR_INVALID_ARG, "w8a8: bad shape M=%d N=%d K=%d", M, N, K);
   if (M == 0) return SPECQ_OK;   // nothing to compute (empty tensors may carry null pointers)
   if (a == nullptr || w == nullptr) return fail(SPECQ_ERR_INVALID_ARG, "w8a8: null input pointer");
@@ -85,6 +93,24 @@ int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int
   p.status = dev->status;
   p.lda = lda; p.ldw = ldw; p.ldo = ldo; p.ldo_n = ldo_n; p.ldacc = ldacc;
   p.m_rows = M; p.N = N; p.K = K;
+  W8A8PeerOut po = {};
+  if (peer != nullptr) {
+    if (peer->world < 1 || peer->world > kW8A8MaxPeers || peer->rank < 0 || peer->rank >= peer->world ||
+        peer->out == nullptr || peer->flags == nullptr || acc != nullptr || ldo_n != 1)
+      return fail(SPECQ_ERR_INVALID_ARG, "w8a8_peer: rank %d of world %d, fp16 rows of unit column stride",
+                  peer->rank, peer->world);
+    for (int q = 0; q < peer->world; ++q) {
+      if (peer->out[q] == nullptr || peer->flags[q] == nullptr || !aligned(peer->out[q], 2) || !aligned(peer->flags[q], 4))
+        return fail(SPECQ_ERR_INVALID_ARG, "w8a8_peer: null or misaligned buffer of rank %d", q);
+      // the 16-byte epilogue stores need every rank's base aligned like this rank's own
+      if ((reinterpret_cast<uintptr_t>(peer->out[q]) & 15u) != (reinterpret_cast<uintptr_t>(out) & 15u))
+        return fail(SPECQ_ERR_INVALID_ARG, "w8a8_peer: rank %d's output base is aligned unlike this rank's", q);
+      po.out[q] = static_cast<__half*>(peer->out[q]);
+      po.flags[q] = peer->flags[q];
+    }
+    po.world = peer->world;
+    po.rank = peer->rank;
+  }
 
   // One token chunk per CTA up to kW8A8MaxChunk tokens (past 256 rows: a multiple of 32, so a
   // whole chunk arrives in two TMA boxes of chunk / 2 rows) for plan-buffer grids -- the same
@@ -159,13 +185,19 @@ int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int
   const dim3 grid(static_cast<unsigned>(S), static_cast<unsigned>(n_chunks), static_cast<unsigned>(n_tiles));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc;
-  switch (vec) {
-    case 0: rc = launch_w8a8_variant<0>(p, tw, ta, grid, smem, st); break;
-    case 16: rc = launch_w8a8_variant<16>(p, tw, ta, grid, smem, st); break;
-    case 8: rc = launch_w8a8_variant<8>(p, tw, ta, grid, smem, st); break;
-    case 4: rc = launch_w8a8_variant<4>(p, tw, ta, grid, smem, st); break;
-    case 2: rc = launch_w8a8_variant<2>(p, tw, ta, grid, smem, st); break;
-    default: rc = launch_w8a8_variant<1>(p, tw, ta, grid, smem, st); break;
+  if (peer != nullptr) {   // tensor-parallel output: the TMA variant (16-byte aligned operands)
+    if (vec != 0) return fail(SPECQ_ERR_UNSUPPORTED, "w8a8_peer: operands must be 16-byte aligned (TMA)");
+    rc = launch_w8a8_variant<0>(p, tw, ta, po, grid, smem, st);
+  } else {
+    const W8A8NoPeer np = {};
+    switch (vec) {
+      case 0: rc = launch_w8a8_variant<0>(p, tw, ta, np, grid, smem, st); break;
+      case 16: rc = launch_w8a8_variant<16>(p, tw, ta, np, grid, smem, st); break;
+      case 8: rc = launch_w8a8_variant<8>(p, tw, ta, np, grid, smem, st); break;
+      case 4: rc = launch_w8a8_variant<4>(p, tw, ta, np, grid, smem, st); break;
+      case 2: rc = launch_w8a8_variant<2>(p, tw, ta, np, grid, smem, st); break;
+      default: rc = launch_w8a8_variant<1>(p, tw, ta, np, grid, smem, st); break;
+    }
   }
   if (rc == SPECQ_OK) {
     LaunchRecord& r = last_launch_ref();
@@ -180,12 +212,12 @@ int run_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int
 
 const void* w8a8_kernel_by_variant(int variant) {
   switch (variant) {
-    case 0: return reinterpret_cast<const void*>(w8a8_kernel<0>);
-    case 1: return reinterpret_cast<const void*>(w8a8_kernel<16>);
-    case 2: return reinterpret_cast<const void*>(w8a8_kernel<8>);
-    case 3: return reinterpret_cast<const void*>(w8a8_kernel<4>);
-    case 4: return reinterpret_cast<const void*>(w8a8_kernel<2>);
-    case 5: return reinterpret_cast<const void*>(w8a8_kernel<1>);
+    case 0: return reinterpret_cast<const void*>(w8a8_kernel<0, W8A8NoPeer>);
+    case 1: return reinterpret_cast<const void*>(w8a8_kernel<16, W8A8NoPeer>);
+    case 2: return reinterpret_cast<const void*>(w8a8_kernel<8, W8A8NoPeer>);
+    case 3: return reinterpret_cast<const void*>(w8a8_kernel<4, W8A8NoPeer>);
+    case 4: return reinterpret_cast<const void*>(w8a8_kernel<2, W8A8NoPeer>);
+    case 5: return reinterpret_cast<const void*>(w8a8_kernel<1, W8A8NoPeer>);
     default: return nullptr;
   }
 }
@@ -369,6 +401,16 @@ int specq_w8a8(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, i
   return run_w8a8(a, lda, sa, w, ldw, sw, out, ldo, ldo_n, nullptr, 0, plan, M, N, K, stream);
 }
 
+int specq_w8a8_peer(const int8_t* a, int64_t lda, const float* sa, const int8_t* w, int64_t ldw, const float* sw,
+                    void* const* out, int64_t ldo, const int32_t* plan, int M, int N, int K, uint32_t* const* flags,
+                    int rank, int world, void* stream) {
+  last_launch_ref() = LaunchRecord();
+  if (out == nullptr || world < 1 || rank < 0 || rank >= world || world > kW8A8MaxPeers)
+    return fail(SPECQ_ERR_INVALID_ARG, "w8a8_peer: rank %d of world %d", rank, world);
+  const W8A8PeerArgs peer = {out, flags, rank, world};
+  return run_w8a8(a, lda, sa, w, ldw, sw, out[rank], ldo, 1, nullptr, 0, plan, M, N, K, stream, &peer);
+}
+
 int specq_w8a8_acc(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw, int32_t* acc, int64_t ldacc,
                    const int32_t* plan, int M, int N, int K, void* stream) {
   last_launch_ref() = LaunchRecord();
@@ -399,6 +441,15 @@ int specq_quant_rows(const void* x, int64_t ldx, void* r, int64_t ldr, int8_t* q
                      void* stream) {
   last_launch_ref() = LaunchRecord();
   return run_quant_rows(x, ldx, r, ldr, q, ldq, s, plan, amax_in, amax_out, M, N, mode, stream);
+}
+
+int specq_quant_rows_peer(const void* x, int64_t ldx, void* r, int64_t ldr, int8_t* q, int64_t ldq, float* s,
+                          const int32_t* plan, const float* amax_in, float* amax_out, int M, int N, int mode,
+                          const uint32_t* wait_flags, int rank, int world, void* stream) {
+  last_launch_ref() = LaunchRecord();
+  if (wait_flags == nullptr) return fail(SPECQ_ERR_INVALID_ARG, "quant_rows_peer: null flag array");
+  return run_quant_rows(x, ldx, r, ldr, q, ldq, s, plan, amax_in, amax_out, M, N, mode, stream, wait_flags, rank,
+                        world);
 }
 
 int specq_kv_append(const void* x, int64_t ldx, int k_col, int v_col, int8_t* kc, int8_t* vc, int64_t kv_sp,

@@ -31,9 +31,13 @@
 //     of the widest aligned width and write the same swizzled layout.
 #pragma once
 
+#include <type_traits>
+
 #include "gemm_common.cuh"
 
 namespace specq {
+
+constexpr int kW8A8MaxPeers = 8;
 
 struct W8A8Params {
   const int8_t* a;     // [m_rows, K], row stride lda bytes
@@ -58,6 +62,18 @@ struct W8A8Params {
   uint32_t tmem_cols;
 };
 
+// Tensor-parallel output (the W8A8PeerOut instantiation): every fp16 store goes to out[q] for
+// each rank q (this rank's own full buffer included, each base at this rank's column block), and
+// each CTA, once its stores are done, adds 1 to slot `rank` of every rank's flag array (its own
+// included: the consumer on this rank reads its own count as the target).  The plain kernel is
+// instantiated with W8A8NoPeer and carries none of it.
+struct W8A8NoPeer {};
+struct W8A8PeerOut {
+  __half* out[kW8A8MaxPeers];
+  uint32_t* flags[kW8A8MaxPeers];
+  int world, rank;
+};
+
 constexpr int kW8A8Threads = 192;  // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue (+ LDG producer)
 constexpr uint32_t kW8A8WTile = 128 * 128;  // bytes of one weight tile
 constexpr int kW8A8MaxStages = 8;
@@ -72,10 +88,11 @@ struct W8A8ActMaps {
 };
 
 // VEC = 0: TMA producer; VEC in {16, 8, 4, 2, 1}: register-staged loads of that width.
-template <int VEC>
+template <int VEC, typename PeerT>
 __global__ void __launch_bounds__(kW8A8Threads, 1)
     w8a8_kernel(const __grid_constant__ W8A8Params p, const __grid_constant__ CUtensorMap tmap_w,
-                const __grid_constant__ W8A8ActMaps tmap_a) {
+                const __grid_constant__ W8A8ActMaps tmap_a, const __grid_constant__ PeerT peer) {
+  constexpr bool kPeer = std::is_same<PeerT, W8A8PeerOut>::value;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   SPECQ_TRACE_INIT();
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -123,9 +140,21 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
     M = pm;
   }
   const int m_cnt = min(p.chunk, M - m0);
+  // tensor-parallel output: this CTA's stores are done -> one release reduction per rank
+  // (system scope, cumulative over the CTA's stores after the barrier that precedes it)
+  auto signal_peers = [&]() {
+    if constexpr (kPeer) {
+      if (threadIdx.x == 0)
+        for (int q = 0; q < peer.world; ++q) red_release_sys_add_u32(peer.flags[q] + peer.rank, 1u);
+    }
+  };
   // Every CTA of a cluster shares (blockIdx.y, blockIdx.z), so the whole cluster leaves
-  // together and no cluster barrier is left waiting.
-  if (m_cnt <= 0) return;
+  // together and no cluster barrier is left waiting.  (It still counts itself in, so every
+  // launch of a shape adds the same total.)
+  if (m_cnt <= 0) {
+    signal_peers();
+    return;
+  }
   const uint32_t n_pad = static_cast<uint32_t>((m_cnt + 15) & ~15);   // MMA N
   const int a_rows = (m_cnt + 15) & ~15;                               // activation rows staged
   const uint32_t a_bytes = static_cast<uint32_t>(a_rows) * 128u;
@@ -275,6 +304,22 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
   // measured slower, its early CTAs holding SMs this kernel's clusters could use.
   pdl_launch_dependents();
   // ---- epilogue --------------------------------------------------------------------------
+  // fp16 output stores: to p.out, or (tensor-parallel output) to every rank's full buffer at
+  // the same offset -- peer stores over NVLink
+  auto store_h = [&](int64_t off, __half v) {
+    if constexpr (kPeer) {
+      for (int q = 0; q < peer.world; ++q) peer.out[q][off] = v;
+    } else {
+      p.out[off] = v;
+    }
+  };
+  auto store_h8 = [&](int64_t off, uint4 v) {
+    if constexpr (kPeer) {
+      for (int q = 0; q < peer.world; ++q) *reinterpret_cast<uint4*>(peer.out[q] + off) = v;
+    } else {
+      *reinterpret_cast<uint4*>(p.out + off) = v;
+    }
+  };
   const bool epi = warp >= 2;
   const uint32_t quad = warp & 3u;                      // TMEM lane quadrant of this warp
   const int row = static_cast<int>(quad * 32 + lane);   // channel within the tile
@@ -304,7 +349,7 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
                 p.acc_out[static_cast<int64_t>(m) * p.ldacc + n] = acc;
               } else {
                 const float v = __fmul_rn(__fmul_rn(static_cast<float>(acc), sa_s[m - m0]), swn);
-                p.out[static_cast<int64_t>(m) * p.ldo + static_cast<int64_t>(n) * p.ldo_n] = __float2half_rn(v);
+                store_h(static_cast<int64_t>(m) * p.ldo + static_cast<int64_t>(n) * p.ldo_n, __float2half_rn(v));
               }
             }
           }
@@ -380,11 +425,10 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
           }
           const int n = n0 + nl;
           if (n + 8 <= p.N) {
-            *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(m0 + m) * p.ldo + n) =
-                make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            store_h8(static_cast<int64_t>(m0 + m) * p.ldo + n, make_uint4(hw[0], hw[1], hw[2], hw[3]));
           } else {
             const __half* hv = reinterpret_cast<const __half*>(hw);
-            for (int k = 0; k < 8 && n + k < p.N; ++k) p.out[static_cast<int64_t>(m0 + m) * p.ldo + n + k] = hv[k];
+            for (int k = 0; k < 8 && n + k < p.N; ++k) store_h(static_cast<int64_t>(m0 + m) * p.ldo + n + k, hv[k]);
           }
         }
       } else {
@@ -405,7 +449,7 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
                   p.acc_out[static_cast<int64_t>(m) * p.ldacc + n] = sv[j];
                 } else {
                   const float val = __fmul_rn(__fmul_rn(static_cast<float>(sv[j]), sa_s[m - m0]), swn);
-                  p.out[static_cast<int64_t>(m) * p.ldo + static_cast<int64_t>(n) * p.ldo_n] = __float2half_rn(val);
+                  store_h(static_cast<int64_t>(m) * p.ldo + static_cast<int64_t>(n) * p.ldo_n, __float2half_rn(val));
                 }
               }
             }
@@ -420,6 +464,7 @@ __global__ void __launch_bounds__(kW8A8Threads, 1)
   // ---- teardown ----------------------------------------------------------------------------
   tc_fence_before();
   __syncthreads();
+  signal_peers();   // every output store of this CTA precedes the barrier above
   if (threadIdx.x == 0) SPECQ_TRACE_POINT(9, 0);
   SPECQ_TRACE_CTA_END();
   if (warp == 1) {

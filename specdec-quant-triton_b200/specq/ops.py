@@ -307,7 +307,7 @@ QUANT_PLAIN, QUANT_RESIDUAL, QUANT_SILU_MUL = 0, 1, 2
 
 
 def quant_rows(x, mode=QUANT_PLAIN, residual=None, q=None, s=None, plan=None, grid_m_max=None, amax_in=None,
-               amax_out=None):
+               amax_out=None, wait=None):
     """Per-token symmetric INT8 of fp16 rows on the device -> (q int8 [M, N], s fp32 [M]).
 
     mode QUANT_PLAIN: quantise x [M, N] (kernels.py:58-62 bit for bit).
@@ -315,7 +315,9 @@ def quant_rows(x, mode=QUANT_PLAIN, residual=None, q=None, s=None, plan=None, gr
     mode QUANT_SILU_MUL: quantise silu(x[:, :N]) * x[:, N:] for x [M, 2N].
     With `plan`, only the first plan[0] rows are computed (a plan-buffer graph).
     Rows split across GPUs: `amax_out` (fp32 [M]) receives each row's amax and nothing is
-    quantised (returns None); `amax_in` quantises with the given whole-row amax."""
+    quantised (returns None); `amax_in` quantises with the given whole-row amax.
+    `wait` = (flags, rank, world): x is a full buffer that every rank's `specq_w8a8_peer` writes
+    (specq.peer.PeerExchange.wait_args); each CTA first waits until all ranks' blocks landed."""
     if x.dtype != torch.float16 or x.dim() != 2:
         raise TypeError("quant_rows: x must be a 2-D float16 tensor")
     _require_cuda(x, residual, q, s)
@@ -337,6 +339,13 @@ def quant_rows(x, mode=QUANT_PLAIN, residual=None, q=None, s=None, plan=None, gr
     q = torch.empty((M, N), dtype=torch.int8, device=x.device) if q is None else q
     s = torch.empty((M,), dtype=torch.float32, device=x.device) if s is None else s
     m_rows = _row_extent(M, plan, grid_m_max, q.shape[0], s.shape[0])
+    if wait is not None:
+        flags, rank, world = wait
+        _lib.check(lib.specq_quant_rows_peer(x.data_ptr(), x.stride(0), _ptr(residual),
+                                             residual.stride(0) if residual is not None else 0, q.data_ptr(),
+                                             q.stride(0), s.data_ptr(), _plan_ptr(plan), _ptr(amax_in), None, m_rows,
+                                             N, mode, flags.data_ptr(), rank, world, _stream()))
+        return q, s
     _lib.check(lib.specq_quant_rows(x.data_ptr(), x.stride(0), _ptr(residual),
                                     residual.stride(0) if residual is not None else 0, q.data_ptr(), q.stride(0),
                                     s.data_ptr(), _plan_ptr(plan), _ptr(amax_in), None, m_rows, N, mode,

@@ -84,6 +84,34 @@ class PeerExchange:
             torch.cuda.current_stream().cuda_stream))
         return e["full"]
 
+    def w8a8(self, name: str, a_q, sa, w_q, sw, rows: int, plan=None) -> torch.Tensor:
+        """W8A8 GEMM (this rank's [N_local, K] weight shard) whose output block lands straight in
+        column block `rank` of every rank's full buffer of exchange `name` (`specq_w8a8_peer`: the
+        GEMM's epilogue stores over NVLink, then counts its CTAs into every rank's flags); a
+        consumer of the full buffer waits with `wait_args(name)`.  `rows` is the launch's row
+        extent (with a plan, the maximum; plan[0] the active rows).  Returns the full buffer."""
+        e = self._ex[name]
+        M, K = a_q.shape
+        N = w_q.shape[0]
+        if N != e["cols"] or e["full"].dtype != torch.float16:
+            raise ValueError(f"peer exchange {name}: a [{N}]-column fp16 block does not fit")
+        if rows > e["full"].shape[0] or rows > M or a_q.stride(1) != 1 or w_q.stride(1) != 1:
+            raise ValueError(f"peer exchange {name}: {rows} rows / strides")
+        outs = e.get("outs")
+        if outs is None:
+            off = self.rank * e["cols"] * e["esz"]
+            outs = e["outs"] = (C.c_void_p * self.world)(*[p + off for p in e["dst"]])
+        lib = _lib.load()
+        _lib.check(lib.specq_w8a8_peer(
+            a_q.data_ptr(), a_q.stride(0), sa.data_ptr(), w_q.data_ptr(), w_q.stride(0), sw.data_ptr(), outs,
+            e["full"].stride(0), None if plan is None else plan.data_ptr(), rows, N, K, e["fl"], self.rank,
+            self.world, torch.cuda.current_stream().cuda_stream))
+        return e["full"]
+
+    def wait_args(self, name: str) -> tuple:
+        """(flags, rank, world) for `ops.quant_rows(..., wait=...)` on exchange `name`'s full buffer."""
+        return (self._ex[name]["flags"], self.rank, self.world)
+
     def all_max(self, name: str, local: torch.Tensor, out: torch.Tensor, rows: int, plan=None) -> torch.Tensor:
         """out[:rows] <- the maximum over the ranks of local[:rows] (float32 [rows])."""
         if local.dtype != torch.float32 or out.dtype != torch.float32 or not local.is_contiguous():

@@ -77,8 +77,8 @@ def gathered_to_rows(buf: torch.Tensor, world: int, rows: int, out: torch.Tensor
 class StackTP:
     def __init__(self, world, rank, layers=4, hid=4096, ff=14336, heads=32, kv_heads=8, head_dim=128, ctx=1024,
                  b_max=32, ks=(0, 2, 4, 8), page=16, seed=0, device="cuda", group=None, exchange="nccl"):
-        if exchange not in ("nccl", "peer"):
-            raise ValueError(f"exchange {exchange!r}: 'nccl' or 'peer'")
+        if exchange not in ("nccl", "peer", "fused"):
+            raise ValueError(f"exchange {exchange!r}: 'nccl', 'peer' or 'fused'")
         self.g, self.r, self.group, self.exchange = world, rank, group, exchange
         self.L, self.hid, self.ff, self.H, self.H_KV, self.D = layers, hid, ff, heads, kv_heads, head_dim
         self.b_max, self.ks = b_max, tuple(ks)
@@ -110,8 +110,9 @@ class StackTP:
         self.down_l, self.down = mk(M, hid // g), mk(M, hid)
         self.bufs = {n: torch.empty(g * t.numel(), dtype=t.dtype, device=device).view(g * M, t.shape[1])
                      for n, t in (("attn", self.attn_l), ("o", self.o_l), ("f8", self.f8_l), ("down", self.down_l))}
-        if exchange == "peer":
+        if exchange in ("peer", "fused"):
             # the gathered rows land in symmetric full buffers written by every rank's kernel
+            # (with "fused", the O and down projections' own epilogues store them)
             from .peer import PeerExchange
             self.px = PeerExchange(group)
             self.attn = self.px.add("attn", M, self.Hl * D, torch.float16)
@@ -145,7 +146,7 @@ class StackTP:
         self.plan.copy_(h, non_blocking=True)
 
     def _gather(self, name, local, full, rows, plan=None):
-        if self.exchange == "peer":
+        if self.exchange in ("peer", "fused"):
             self.px.gather(name, local, rows, plan=plan)   # lands in `full` (the symmetric buffer)
             return
         buf = self.bufs[name]
@@ -153,7 +154,7 @@ class StackTP:
         gathered_to_rows(buf, self.g, rows, full)
 
     def _amax_all_ranks(self, rows, plan=None):
-        if self.exchange == "peer":
+        if self.exchange in ("peer", "fused"):
             self.px.all_max("amax", self.amax, self.amax, rows, plan=plan)
         else:
             dist.all_reduce(self.amax[:rows], op=dist.ReduceOp.MAX, group=self.group)
@@ -175,7 +176,7 @@ class StackTP:
                 ops.quant_rows(self.h[rows], q=self.x8[rows], s=self.sx[rows], plan=pl)
             else:
                 ops.quant_rows(self.down[rows], mode=ops.QUANT_RESIDUAL, residual=self.h[rows], q=self.x8[rows],
-                               s=self.sx[rows], plan=pl)
+                               s=self.sx[rows], plan=pl, wait=self._wait("down"))
             ops.w8a8_matmul(self.x8[rows], self.sx[rows], *lw["qkv"], out=self.qkv[rows], **gm)
             ops.kv_append(self.qkv, Hl * D, (Hl + Kl) * D, kc, vc, ks, vs, bt[:Bg], cl[:Bg], ql, plan=pa, B=Bg,
                           ql_max=qlg)
@@ -183,20 +184,32 @@ class StackTP:
                                        ql_max=qlg, QPP=self.ql_max, plan=pa)
             self._gather("attn", self.attn_l, self.attn, M, pl)
             ops.quant_rows(self.attn[rows], q=self.x8[rows], s=self.sx[rows], plan=pl)
-            ops.w8a8_matmul(self.x8[rows], self.sx[rows], *lw["o"], out=self.o_l[rows], **gm)
-            self._gather("o", self.o_l, self.o, M, pl)
+            self._gemm_out("o", self.x8, self.sx, lw["o"], self.o_l, self.o, M, pl, gm)
             ops.quant_rows(self.o[rows], mode=ops.QUANT_RESIDUAL, residual=self.h[rows], q=self.x8[rows],
-                           s=self.sx[rows], plan=pl)
+                           s=self.sx[rows], plan=pl, wait=self._wait("o"))
             ops.w8a8_matmul(self.x8[rows], self.sx[rows], *lw["gu"], out=self.gu_l[rows], **gm)
             ops.quant_rows(self.gu_l[rows], mode=ops.QUANT_SILU_MUL, amax_out=self.amax[rows], plan=pl)
             self._amax_all_ranks(M, pl)
             ops.quant_rows(self.gu_l[rows], mode=ops.QUANT_SILU_MUL, q=self.f8_l[rows], s=self.sf[rows], plan=pl,
                            amax_in=self.amax[rows])
             self._gather("f8", self.f8_l, self.f8, M, pl)
-            ops.w8a8_matmul(self.f8[rows], self.sf[rows], *lw["down"], out=self.down_l[rows], **gm)
-            self._gather("down", self.down_l, self.down, M, pl)
+            self._gemm_out("down", self.f8, self.sf, lw["down"], self.down_l, self.down, M, pl, gm)
         ops.quant_rows(self.down[rows], mode=ops.QUANT_RESIDUAL, residual=self.h[rows], q=self.x8[rows],
-                       s=self.sx[rows], plan=pl)
+                       s=self.sx[rows], plan=pl, wait=self._wait("down"))
+
+    def _gemm_out(self, name, a, sa, w, local, full, M, pl, gm):
+        """A row-sharded projection whose output columns every rank needs: with exchange="fused"
+        the GEMM's epilogue stores them into every rank's full buffer; otherwise the GEMM writes
+        its block locally and an all-gather follows."""
+        rows = slice(0, M)
+        if self.exchange == "fused":
+            self.px.w8a8(name, a[rows], sa[rows], *w, M, plan=pl)
+            return
+        ops.w8a8_matmul(a[rows], sa[rows], *w, out=local[rows], **gm)
+        self._gather(name, local, full, M, pl)
+
+    def _wait(self, name):
+        return self.px.wait_args(name) if self.exchange == "fused" else None
 
     def capture(self, fn):
         s = torch.cuda.Stream()
@@ -289,8 +302,9 @@ def main():
     ap.add_argument("--ctx", type=int, default=1024)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--check", action="store_true", help="compare with the single-GPU stack on rank 0")
-    ap.add_argument("--exchange", choices=("nccl", "peer"), default="peer",
-                    help="all-gathers by NCCL or by the library's peer-store kernel")
+    ap.add_argument("--exchange", choices=("nccl", "peer", "fused"), default="peer",
+                    help="all-gathers by NCCL, by the library's peer-store kernel, or (fused) with the O and "
+                         "down projections storing into every rank's buffer from their epilogues")
     args = ap.parse_args()
     rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

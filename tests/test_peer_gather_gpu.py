@@ -84,3 +84,50 @@ def test_missing_peer_signal_times_out_with_status(cuda):
     assert torch.equal(full[0][:, :n], src)
     torch.zeros(1, device="cuda").add_(1)                  # the context is still usable
     torch.cuda.synchronize()
+
+
+def test_w8a8_peer_output_and_counts_two_rank_emulation(cuda):
+    """specq_w8a8_peer as rank 0 of 2: its output block lands in column block 0 of both 'ranks''
+    full buffers (same GPU here), equal to the plain GEMM, and every CTA counts itself into slot 0
+    of both flag arrays; a consumer then waits for rank 1's count to reach rank 0's own."""
+    import specq
+    g = torch.Generator(device="cuda").manual_seed(2)
+    M, N, K, world = 40, 512, 1024, 2
+    a = torch.randint(-127, 128, (M, K), generator=g, device="cuda", dtype=torch.int16).to(torch.int8)
+    w = torch.randint(-127, 128, (N, K), generator=g, device="cuda", dtype=torch.int16).to(torch.int8)
+    sa = torch.rand(M, generator=g, device="cuda") * 0.02 + 0.001
+    sw = torch.rand(N, generator=g, device="cuda") * 0.02 + 0.001
+    ref, _ = specq.w8a8_matmul(a, sa, w, sw)
+    full = [torch.full((M, world * N), 3.0, dtype=torch.float16, device="cuda") for _ in range(world)]
+    flags = [torch.zeros(world, dtype=torch.int32, device="cuda") for _ in range(world)]
+    lib = _lib.load()
+    _lib.check(lib.specq_w8a8_peer(
+        a.data_ptr(), a.stride(0), sa.data_ptr(), w.data_ptr(), w.stride(0), sw.data_ptr(),
+        (C.c_void_p * world)(*[f.data_ptr() for f in full]), full[0].stride(0), None, M, N, K,
+        (C.c_void_p * world)(*[f.data_ptr() for f in flags]), 0, world, torch.cuda.current_stream().cuda_stream))
+    ctas = _lib.last_launch()["grid"]
+    torch.cuda.synchronize()
+    n_ctas = ctas[0] * ctas[1] * ctas[2]
+    for f in full:
+        assert torch.equal(f[:, :N], ref)                    # bit-exact with the plain epilogue
+        assert (f[:, N:] == 3.0).all()                       # the other rank's block untouched
+    assert flags[0].tolist() == [n_ctas, 0] and flags[1].tolist() == [n_ctas, 0]
+    # consumer on rank 0: rank 1's count preset to the same total -> no wait, same result
+    flags[0][1] = n_ctas
+    q, s = specq.quant_rows(full[0], wait=(flags[0], 0, world))
+    torch.cuda.synchronize()
+    q_full, s_full = specq.quant_rows(full[0])
+    assert torch.equal(q, q_full) and torch.equal(s, s_full)
+    assert _lib.get_status() == 0
+
+
+def test_consumer_wait_times_out_without_the_peer_count(cuda):
+    import specq
+    M, N, world = 4, 256, 2
+    x = torch.ones(M, N, dtype=torch.float16, device="cuda")
+    flags = torch.tensor([5, 0], dtype=torch.int32, device="cuda")   # rank 1 never counts in
+    _lib.get_status()
+    q, s = specq.quant_rows(x, wait=(flags, 0, world))
+    torch.cuda.synchronize()                                          # each CTA gives up after 1 s
+    assert _lib.get_status() & _lib.SPECQ_STATUS_TIMEOUT_PEER
+    assert (q == 127).all()                                           # it still quantised its row

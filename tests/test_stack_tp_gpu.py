@@ -1,6 +1,7 @@
 """Tensor-parallel stack on two GPUs, with the all-gathers done by the library's peer-store
-kernel and by NCCL: the plan graph equals eager steps and the residual stream equals the
-single-GPU stack's, bit for bit (skipped with fewer than two GPUs)."""
+kernel, by the O and down projections' own epilogues (fused) and by NCCL: the plan graph
+equals eager steps and the residual stream equals the single-GPU stack's, bit for bit (skipped
+with fewer than two GPUs)."""
 import json
 import os
 import subprocess
@@ -13,7 +14,7 @@ pytestmark = pytest.mark.gpu
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-@pytest.mark.parametrize("exchange,port", [("peer", 29517), ("nccl", 29518)])
+@pytest.mark.parametrize("exchange,port", [("fused", 29519), ("peer", 29517), ("nccl", 29518)])
 def test_two_gpu_stack_matches_single_gpu(cuda, exchange, port):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
