@@ -220,6 +220,33 @@ int specq_peer_gather(const void* src, int64_t ld_src, int row_bytes, const int3
                       float* max_out, int rank, int world, void* stream);
 
 /*
+ * specq_peer_gather for callers that cannot allocate device memory.  No counterpart in the
+ * reference (which has no multi-GPU exchange at all).  Some hosts own every byte of device
+ * memory themselves: a serving engine that reserves all free HBM for its KV cache at start-up
+ * and forbids later cudaMalloc calls, or a plugin that may only use the buffers it is handed.
+ * Such a caller still has its full buffers and flag arrays (they must be peer-visible, so they
+ * come from the host's own symmetric pool), but it has nowhere to put the `state` words.  This
+ * entry point keeps them in a table inside the library instead: a fixed device array of
+ * SPECQ_PEER_NOALLOC_SLOTS exchanges x 2 words (512 bytes), which every GPU that loads the
+ * library holds until the process exits.
+ *   - slot (0 .. SPECQ_PEER_NOALLOC_SLOTS-1) picks the exchange's entry; any other value is
+ *     rejected with SPECQ_ERR_INVALID_ARG.  One slot per flag-array set, like one `state`.
+ *   - restart != 0 zeroes the slot on `stream` before the launch (a stream-ordered memset of the
+ *     library's own table, no allocation).  Pass it on the first call that uses a freshly
+ *     zeroed flag-array set: the table keeps whatever the last call on that slot left there.
+ *   - Every other argument, and the result, is exactly as for specq_peer_gather.
+ *   - The first call on a device looks up the table's device address (once per device, with
+ *     that device current); make that first call before any stream capture.
+ *   - All calls share the one table: calls that may overlap on the GPU (different streams with
+ *     no ordering between them) and name the same slot race on its running total.
+ * Nothing here calls cudaMalloc, cudaFree or any allocating library routine.
+ */
+#define SPECQ_PEER_NOALLOC_SLOTS 64
+int specq_peer_gather_noalloc(const void* src, int64_t ld_src, int row_bytes, const int32_t* plan, int rows,
+                              void* const* dst, int64_t ld_dst, int64_t dst_off, uint32_t* const* flags, int slot,
+                              int restart, float* max_out, int rank, int world, void* stream);
+
+/*
  * W8A8 GEMM with tensor-parallel output (no reference counterpart: the GEMM fused with the
  * tensor-parallel stack's all-gather).  The same product as specq_w8a8; its fp16 output rows
  * (unit column stride, row stride ldo) are stored into EVERY rank's full buffer over NVLink:

@@ -24,6 +24,34 @@ int* device_status_symbol_address() {
   return static_cast<int*>(p);
 }
 
+// The running CTA totals of specq_peer_gather_noalloc: SPECQ_PEER_NOALLOC_SLOTS exchanges x
+// {running total, unused}, in the same layout as specq_peer_gather's caller-owned `state`.
+// Module-scope device storage: every GPU that loads the library holds these 512 bytes until
+// the process exits.  Host code must not pass `g_peer_noalloc_state` itself to a kernel (on the
+// host the name is a stand-in, not a device address); peer_noalloc_table() gives the address.
+static __device__ __align__(256) uint32_t g_peer_noalloc_state[2 * SPECQ_PEER_NOALLOC_SLOTS];
+
+// Device address of the table on the current device, looked up once per device (with that
+// device current, as cudaGetSymbolAddress requires) and cached.
+int peer_noalloc_table(uint32_t** out) {
+  static std::mutex mu;
+  static uint32_t* table[kMaxDevices] = {};
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return fail(SPECQ_ERR_NO_DEVICE, "no current CUDA device");
+  std::lock_guard<std::mutex> lock(mu);
+  if (table[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_peer_noalloc_state);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(SPECQ_ERR_CUDA, "peer_gather_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                  cudaGetErrorString(e));
+    table[dev] = static_cast<uint32_t*>(p);
+  }
+  *out = table[dev];
+  return SPECQ_OK;
+}
+
 // ---------------------------------------------------------------------------------------------
 // W8A8
 // ---------------------------------------------------------------------------------------------
@@ -576,6 +604,21 @@ int specq_peer_gather(const void* src, int64_t ld_src, int row_bytes, const int3
                       void* const* dst, int64_t ld_dst, int64_t dst_off, uint32_t* const* flags, uint32_t* state,
                       float* max_out, int rank, int world, void* stream) {
   last_launch_ref() = LaunchRecord();
+  return run_peer_gather(src, ld_src, row_bytes, plan, rows, dst, ld_dst, dst_off, flags, state, max_out, rank,
+                         world, stream);
+}
+
+int specq_peer_gather_noalloc(const void* src, int64_t ld_src, int row_bytes, const int32_t* plan, int rows,
+                              void* const* dst, int64_t ld_dst, int64_t dst_off, uint32_t* const* flags, int slot,
+                              int restart, float* max_out, int rank, int world, void* stream) {
+  last_launch_ref() = LaunchRecord();
+  if (slot < 0 || slot >= SPECQ_PEER_NOALLOC_SLOTS)
+    return fail(SPECQ_ERR_INVALID_ARG, "peer_gather_noalloc: slot %d outside 0..%d (the library's table holds %d exchanges)",
+                slot, SPECQ_PEER_NOALLOC_SLOTS - 1, SPECQ_PEER_NOALLOC_SLOTS);
+  uint32_t* table = nullptr;
+  if (int rc = peer_noalloc_table(&table)) return rc;
+  uint32_t* state = table + 2 * slot;
+  if (restart) SPECQ_CUDA_TRY(cudaMemsetAsync(state, 0, 2 * sizeof(uint32_t), static_cast<cudaStream_t>(stream)));
   return run_peer_gather(src, ld_src, row_bytes, plan, rows, dst, ld_dst, dst_off, flags, state, max_out, rank,
                          world, stream);
 }

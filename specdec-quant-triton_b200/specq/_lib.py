@@ -52,6 +52,8 @@ SIGNATURES = {
     "specq_selftest_wait_timeout": (_i32, [_u64, _vp]),
     "specq_mma_peak": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
     "specq_peer_gather": (_i32, [_vp, _i64, _i32, _vp, _i32, _vp, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _vp]),
+    "specq_peer_gather_noalloc": (_i32, [_vp, _i64, _i32, _vp, _i32, _vp, _i64, _i64, _vp, _i32, _i32, _vp, _i32,
+                                         _i32, _vp]),
     "specq_w8a8_peer": (_i32, [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _vp, _i32, _i32, _i32, _vp, _i32, _i32,
                                _vp]),
     "specq_quant_rows_peer": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp,
